@@ -1,0 +1,278 @@
+"""B200 (sm_100a) GPT-2 decode hot path: host-side mirror of the reference's launch API.
+
+The kernels live in ``libb2decode.so`` (built in-tree from ``csrc/`` by ``build_lib.py``)
+and are reached only through its C ABI (``include/b2decode.h``) and the reference-named
+C++ entry points (``include/b2_reference_api.h``). Torch tensors are used here purely as
+device memory and for the current CUDA stream; every computation runs in the library.
+
+Reference-named functions (same argument order and meaning as the reference):
+    run_decode_attn              kernels/decode/13_decode_attn.cuh:192-199
+    run_quantize_fp32_to_int8    kernels/quantization/14_int8_gemm.cuh:20-23
+    run_int8_gemm[_bias|_bias_gelu|_bias_residual]  kernels/quantization/14_int8_gemm.cuh:28-64
+They call the library's reference-compatible C++ symbols on the legacy default stream,
+exactly as the reference's wrappers launch. Where the reference fails silently (an
+unsupported GQA group is a no-op, 13_decode_attn.cu:306) these raise ``B2Error``.
+
+Extended entry points (C ABI): ``decode_attn`` (bf16 KV, head_dim 128, explicit stream,
+bounds-checked block table), ``int8_gemm`` and ``int8_gemm_s32`` (raw int32 accumulators).
+
+There is no CPU path: importing works anywhere, but every call needs the built library
+and a CUDA device, and fails loudly otherwise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG_DIR, "libb2decode.so")
+
+B2_OK, B2_ERR_INVALID, B2_ERR_UNSUPPORTED, B2_ERR_WORKSPACE, B2_ERR_CUDA = 0, 1, 2, 3, 4
+B2_DEVERR_TIMEOUT, B2_DEVERR_CTX_RANGE, B2_DEVERR_BLOCK_RANGE = 1, 2, 4
+B2_KV_F32, B2_KV_BF16 = 0, 1
+EPI_PLAIN, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL = 0, 1, 2, 3
+DA_MAX_SPLITS = 16  # reference kernels/decode/13_decode_attn.cuh:12; sizes run_decode_attn's workspace
+
+# Mangled names of the reference-compatible C++ entry points (include/b2_reference_api.h).
+_CXX = {
+    "run_decode_attn": "_Z15run_decode_attniiiiPKfS0_S0_PKiS2_iiiPfS3_",
+    "run_quantize_fp32_to_int8": "_Z25run_quantize_fp32_to_int8iiPKfPiPf",
+    "run_int8_gemm": "_Z13run_int8_gemmiiiPKiS0_PKfS2_Pf",
+    "run_int8_gemm_bias": "_Z18run_int8_gemm_biasiiiPKiS0_PKfS2_S2_Pf",
+    "run_int8_gemm_bias_gelu": "_Z23run_int8_gemm_bias_geluiiiPKiS0_PKfS2_S2_Pf",
+    "run_int8_gemm_bias_residual": "_Z27run_int8_gemm_bias_residualiiiPKiS0_PKfS2_S2_S2_Pf",
+}
+
+# Every symbol include/*.h declares (checked by the CPU tests).
+C_ABI_SYMBOLS = [
+    "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
+    "b2_int8_gemm_s32", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
+]
+
+
+class B2Error(RuntimeError):
+    """A library call returned a non-OK status, or the device error word was set."""
+
+
+class DecodeAttnArgs(ctypes.Structure):
+    """Mirror of ``b2_decode_attn_args`` (include/b2decode.h)."""
+
+    _fields_ = [
+        ("B", ctypes.c_int), ("H_q", ctypes.c_int), ("H_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("Q", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+        ("kv_dtype", ctypes.c_int), ("block_table", ctypes.c_void_p), ("context_lens", ctypes.c_void_p),
+        ("max_context_len", ctypes.c_int), ("block_size", ctypes.c_int), ("num_blocks_per_seq", ctypes.c_int),
+        ("num_phys_blocks", ctypes.c_int), ("scale", ctypes.c_float), ("O", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lib = None
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Loads libb2decode.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise B2Error(f"{p} is missing: build it with `python {_PKG_DIR}/build_lib.py` "
+                      "(there is no CPU fallback)")
+    lib = ctypes.CDLL(p, mode=ctypes.RTLD_LOCAL)
+    vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    lib.b2_decode_attn_workspace_size.argtypes = [i, i, i, i, i, i]
+    lib.b2_decode_attn_workspace_size.restype = sz
+    lib.b2_decode_attn.argtypes = [ctypes.POINTER(DecodeAttnArgs), vp]
+    lib.b2_decode_attn.restype = i
+    lib.b2_quantize_fp32_to_int8.argtypes = [i, i, vp, vp, vp, vp]
+    lib.b2_quantize_fp32_to_int8.restype = i
+    lib.b2_int8_gemm.argtypes = [i, i, i, vp, vp, vp, vp, vp, vp, vp, i, vp]
+    lib.b2_int8_gemm.restype = i
+    lib.b2_int8_gemm_s32.argtypes = [i, i, i, vp, vp, vp, vp]
+    lib.b2_int8_gemm_s32.restype = i
+    lib.b2_get_device_error.argtypes = [i]
+    lib.b2_get_device_error.restype = ctypes.c_uint
+    lib.b2_last_status.argtypes = []
+    lib.b2_last_status.restype = i
+    lib.b2_status_string.argtypes = [i]
+    lib.b2_status_string.restype = ctypes.c_char_p
+    lib.b2_version.argtypes = []
+    lib.b2_version.restype = i
+    cx = {}
+    for name, mangled in _CXX.items():
+        f = getattr(lib, mangled)
+        f.restype = None
+        cx[name] = f
+    f = cx["run_decode_attn"]
+    f.argtypes = [i, i, i, i, vp, vp, vp, vp, vp, i, i, i, vp, vp]
+    cx["run_quantize_fp32_to_int8"].argtypes = [i, i, vp, vp, vp]
+    cx["run_int8_gemm"].argtypes = [i, i, i, vp, vp, vp, vp, vp]
+    cx["run_int8_gemm_bias"].argtypes = [i, i, i, vp, vp, vp, vp, vp, vp]
+    cx["run_int8_gemm_bias_gelu"].argtypes = [i, i, i, vp, vp, vp, vp, vp, vp]
+    cx["run_int8_gemm_bias_residual"].argtypes = [i, i, i, vp, vp, vp, vp, vp, vp, vp]
+    lib._cxx = cx
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise B2Error("expected a CUDA tensor (all pointers are device pointers)")
+    if not t.is_contiguous():
+        raise B2Error("expected a contiguous tensor")
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is not None:
+        return ctypes.c_void_p(getattr(stream, "cuda_stream", stream))
+    import torch
+
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check(status: int, what: str):
+    if status != B2_OK:
+        msg = load_library().b2_status_string(status).decode()
+        raise B2Error(f"{what}: {msg} (status {status})")
+
+
+def _check_last(what: str):
+    _check(load_library().b2_last_status(), what)
+
+
+def device_error(clear: bool = True) -> int:
+    """Synchronises the device and returns (and by default clears) the device error bits."""
+    return int(load_library().b2_get_device_error(1 if clear else 0))
+
+
+# ---------------------------------------------------------------- reference-named API
+def run_decode_attn(B, H_q, H_kv, d, Q, k_cache, v_cache, block_table, context_lens, max_context_len,
+                    block_size, num_blocks_per_seq, O, workspace):
+    """K13 decode attention with the reference's signature (13_decode_attn.cuh:192-199).
+
+    fp32 KV cache; workspace is the reference's ``[B, H_q, DA_MAX_SPLITS, d+2]`` floats."""
+    lib = load_library()
+    lib._cxx["run_decode_attn"](B, H_q, H_kv, d, _ptr(Q), _ptr(k_cache), _ptr(v_cache), _ptr(block_table),
+                                _ptr(context_lens), max_context_len, block_size, num_blocks_per_seq, _ptr(O),
+                                _ptr(workspace))
+    _check_last("run_decode_attn")
+
+
+def run_quantize_fp32_to_int8(rows, cols, input, output_packed, scales):
+    """Per-row int8 quantiser with the reference's signature (14_int8_gemm.cuh:20-23)."""
+    load_library()._cxx["run_quantize_fp32_to_int8"](rows, cols, _ptr(input), _ptr(output_packed), _ptr(scales))
+    _check_last("run_quantize_fp32_to_int8")
+
+
+def run_int8_gemm(M, N, K, A_packed, BT_packed, scale_A, scale_B, C):
+    load_library()._cxx["run_int8_gemm"](M, N, K, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A), _ptr(scale_B),
+                                         _ptr(C))
+    _check_last("run_int8_gemm")
+
+
+def run_int8_gemm_bias(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, C):
+    load_library()._cxx["run_int8_gemm_bias"](M, N, K, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A),
+                                              _ptr(scale_B), _ptr(bias), _ptr(C))
+    _check_last("run_int8_gemm_bias")
+
+
+def run_int8_gemm_bias_gelu(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, C):
+    load_library()._cxx["run_int8_gemm_bias_gelu"](M, N, K, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A),
+                                                   _ptr(scale_B), _ptr(bias), _ptr(C))
+    _check_last("run_int8_gemm_bias_gelu")
+
+
+def run_int8_gemm_bias_residual(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C):
+    load_library()._cxx["run_int8_gemm_bias_residual"](M, N, K, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A),
+                                                       _ptr(scale_B), _ptr(bias), _ptr(residual), _ptr(C))
+    _check_last("run_int8_gemm_bias_residual")
+
+
+# ---------------------------------------------------------------- C-ABI API
+def decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size=16) -> int:
+    return int(load_library().b2_decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size))
+
+
+def make_decode_workspace(B, H_q, H_kv, head_dim, max_context_len, block_size=16, device=None):
+    """Allocates (torch) and zeroes a workspace for ``decode_attn``."""
+    import torch
+
+    n = max(256, decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size))
+    return torch.zeros(n, dtype=torch.uint8, device=device or "cuda")
+
+
+def decode_attn(Q, k_cache, v_cache, block_table, context_lens, max_context_len, O=None, workspace=None,
+                block_size=None, num_phys_blocks=None, scale=0.0, stream=None):
+    """Paged decode attention through ``b2_decode_attn``.
+
+    Q [B, H_q, d] (or [B, H_q, 1, d]) fp32; k/v_cache [P, block_size, H_kv, d] fp32 or bf16;
+    block_table [B, nbps] int32; context_lens [B] int32. Returns O (same shape as Q)."""
+    import torch
+
+    B, H_q, d = Q.shape[0], Q.shape[1], Q.shape[-1]
+    P, bs, H_kv, d2 = k_cache.shape
+    if d2 != d or v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
+        raise B2Error("k_cache / v_cache / Q shapes disagree")
+    if block_size is not None and block_size != bs:
+        raise B2Error("block_size disagrees with k_cache.shape[1]")
+    if k_cache.dtype == torch.float32:
+        kvd = B2_KV_F32
+    elif k_cache.dtype == torch.bfloat16:
+        kvd = B2_KV_BF16
+    else:
+        raise B2Error(f"unsupported KV dtype {k_cache.dtype}")
+    if O is None:
+        O = torch.empty_like(Q)
+    if workspace is None:
+        workspace = make_decode_workspace(B, H_q, H_kv, d, max_context_len, bs, device=Q.device)
+    a = DecodeAttnArgs(B, H_q, H_kv, d, _ptr(Q), _ptr(k_cache), _ptr(v_cache), kvd, _ptr(block_table),
+                       _ptr(context_lens), int(max_context_len), bs, block_table.shape[1],
+                       int(P if num_phys_blocks is None else num_phys_blocks), float(scale), _ptr(O),
+                       _ptr(workspace), workspace.numel() * workspace.element_size())
+    _check(load_library().b2_decode_attn(ctypes.byref(a), _stream(stream)), "b2_decode_attn")
+    return O
+
+
+def quantize_fp32_to_int8(x, out=None, scales=None, stream=None):
+    """Returns (packed int32 [rows, cols/4], scales fp32 [rows])."""
+    import torch
+
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(rows, cols // 4, dtype=torch.int32, device=x.device)
+    if scales is None:
+        scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _check(load_library().b2_quantize_fp32_to_int8(rows, cols, _ptr(x), _ptr(out), _ptr(scales), _stream(stream)),
+           "b2_quantize_fp32_to_int8")
+    return out, scales
+
+
+def int8_gemm(A_packed, BT_packed, scale_A, scale_B, bias=None, residual=None, epilogue=EPI_PLAIN, C=None,
+              stream=None):
+    import torch
+
+    M, K4 = A_packed.shape
+    N = BT_packed.shape[0]
+    if C is None:
+        C = torch.empty(M, N, dtype=torch.float32, device=A_packed.device)
+    _check(load_library().b2_int8_gemm(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A), _ptr(scale_B),
+                                       _ptr(bias), _ptr(residual), _ptr(C), epilogue, _stream(stream)),
+           "b2_int8_gemm")
+    return C
+
+
+def int8_gemm_s32(A_packed, BT_packed, C=None, stream=None):
+    import torch
+
+    M, K4 = A_packed.shape
+    N = BT_packed.shape[0]
+    if C is None:
+        C = torch.empty(M, N, dtype=torch.int32, device=A_packed.device)
+    _check(load_library().b2_int8_gemm_s32(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(C), _stream(stream)),
+           "b2_int8_gemm_s32")
+    return C

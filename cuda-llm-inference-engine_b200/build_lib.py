@@ -1,0 +1,87 @@
+"""Builds libb2decode.so (the C-ABI library) in-tree with nvcc for sm_100a.
+
+    python cuda-llm-inference-engine_b200/build_lib.py [--force]
+
+Each csrc/*.cu is compiled to an object under _build/ (in parallel, skipped when newer
+than its sources), then linked into cuda-llm-inference-engine_b200/libb2decode.so.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+BUILD = os.path.join(ROOT, "_build", "lib")
+LIB = os.path.join(PKG, "libb2decode.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=default",
+    "--expt-relaxed-constexpr",
+    "-I", CSRC, "-I", os.path.join(ROOT, "include"),
+]
+
+
+def _sources():
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
+def _headers():
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    inc = os.path.join(ROOT, "include")
+    hs += [os.path.join(inc, f) for f in os.listdir(inc) if f.endswith(".h")]
+    return hs
+
+
+def _stale(target, deps):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    headers = _headers()
+    flags = NVCC_FLAGS + list(extra_flags or [])
+    jobs = []
+    objs = []
+    for src in _sources():
+        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        objs.append(obj)
+        if force or _stale(obj, [src] + headers + [__file__]):
+            jobs.append([NVCC, *flags, "-c", src, "-o", obj])
+
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+        return r.stderr
+
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        for err in ex.map(run, jobs):
+            if verbose and err:
+                print(err)
+    if force or jobs or _stale(LIB, objs):
+        run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
+             *objs, "-o", LIB, "-lcudart"])
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--ptxas-v", action="store_true", help="print register/smem usage")
+    a = ap.parse_args()
+    extra = ["-Xptxas", "-v"] if a.ptxas_v else []
+    print(build(force=a.force or a.ptxas_v, verbose=True, extra_flags=extra))
+    sys.exit(0)

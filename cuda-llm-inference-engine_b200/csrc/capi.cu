@@ -1,0 +1,174 @@
+// C ABI (include/b2decode.h) and the reference-compatible C++ entry points
+// (include/b2_reference_api.h) over the sm_100a kernels.
+#include "common.cuh"
+#include "b2_reference_api.h"
+#include <mutex>
+
+namespace b2 {
+
+// The library's device error word (B2_DEVERR_* bits), one per device.
+__device__ unsigned int g_device_error = 0;
+
+int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counters_zeroed, cudaStream_t st);
+size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size, int max_splits,
+                                  int kv_bytes);
+int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st);
+int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
+                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st);
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSlots = 64;
+
+int num_sms_current_device() {
+    static int cache[kMaxDevices] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel slot, device).
+bool set_smem_attr_once(const void* func, int bytes, int slot) {
+    static unsigned long long done[kMaxDevices] = {0};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= kMaxSlots)
+        return false;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done[dev] & (1ull << slot)) return true;
+    if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+    done[dev] |= 1ull << slot;
+    return true;
+}
+
+unsigned int* device_error_ptr() {
+    static unsigned int* cache[kMaxDevices] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    if (!cache[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        cache[dev] = static_cast<unsigned int*>(p);
+    }
+    return cache[dev];
+}
+
+constexpr int kAbiMaxSplits = 64;
+// The reference workspace holds DA_MAX_SPLITS rows per head; the drop-in wrapper keeps one
+// row's worth for the arrival counters.
+constexpr int kDropInMaxSplits = DA_MAX_SPLITS - 1;
+
+static thread_local int t_last_status = B2_OK;
+
+}  // namespace b2
+
+using namespace b2;
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim, int max_context_len, int block_size) {
+    if (B <= 0 || H_q <= 0 || H_kv <= 0 || head_dim <= 0 || block_size <= 0 || max_context_len < 0) return 0;
+    // sized for the fp32 plan, which never has fewer splits than the bf16 one
+    return decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size, kAbiMaxSplits, 2);
+}
+
+int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream) {
+    return decode_attn_launch(args, kAbiMaxSplits, true, static_cast<cudaStream_t>(stream));
+}
+
+int b2_quantize_fp32_to_int8(int rows, int cols, const float* input, int32_t* output_packed, float* scales,
+                             b2_stream_t stream) {
+    return quantize_launch(rows, cols, input, output_packed, scales, static_cast<cudaStream_t>(stream));
+}
+
+int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, const float* scale_A,
+                 const float* scale_B, const float* bias, const float* residual, float* C, int epilogue,
+                 b2_stream_t stream) {
+    return gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C, epilogue, false,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, int32_t* C_acc,
+                     b2_stream_t stream) {
+    return gemm_launch(M, N, K, A_packed, BT_packed, nullptr, nullptr, nullptr, nullptr, C_acc, B2_EPI_PLAIN, true,
+                       static_cast<cudaStream_t>(stream));
+}
+
+unsigned int b2_get_device_error(int clear) {
+    unsigned int v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (clear) {
+        const unsigned int z = 0;
+        cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+    }
+    return v;
+}
+
+int b2_last_status(void) { return t_last_status; }
+
+const char* b2_status_string(int status) {
+    switch (status) {
+        case B2_OK: return "ok";
+        case B2_ERR_INVALID: return "invalid argument";
+        case B2_ERR_UNSUPPORTED: return "unsupported shape";
+        case B2_ERR_WORKSPACE: return "workspace missing or too small";
+        case B2_ERR_CUDA: return "CUDA runtime error";
+        default: return "unknown status";
+    }
+}
+
+int b2_version(void) { return 100; }
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ reference-compatible C++ API
+// Same names and parameter lists as the reference; launches go to the legacy default
+// stream as the reference's do. Errors, which the reference drops, land in b2_last_status().
+
+void run_decode_attn(int B, int H_q, int H_kv, int d, const float* Q, const float* k_cache, const float* v_cache,
+                     const int* block_table, const int* context_lens, int max_context_len, int block_size,
+                     int num_blocks_per_seq, float* O, float* workspace) {
+    b2_decode_attn_args a{};
+    a.B = B; a.H_q = H_q; a.H_kv = H_kv; a.head_dim = d;
+    a.Q = Q; a.k_cache = k_cache; a.v_cache = v_cache; a.kv_dtype = B2_KV_F32;
+    a.block_table = block_table; a.context_lens = context_lens;
+    a.max_context_len = max_context_len; a.block_size = block_size; a.num_blocks_per_seq = num_blocks_per_seq;
+    a.num_phys_blocks = 0; a.scale = 0.f; a.O = O;
+    a.workspace = workspace;
+    a.workspace_bytes = (size_t)(B > 0 ? B : 0) * (H_q > 0 ? H_q : 0) * DA_MAX_SPLITS * (d + 2) * sizeof(float);
+    t_last_status = decode_attn_launch(&a, kDropInMaxSplits, false, 0);
+}
+
+void run_quantize_fp32_to_int8(int rows, int cols, const float* input, int32_t* output_packed, float* scales) {
+    t_last_status = quantize_launch(rows, cols, input, output_packed, scales, 0);
+}
+
+void run_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, const float* scale_A,
+                   const float* scale_B, float* C) {
+    t_last_status = gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, nullptr, nullptr, C, B2_EPI_PLAIN,
+                                false, 0);
+}
+
+void run_int8_gemm_bias(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                        const float* scale_A, const float* scale_B, const float* bias, float* C) {
+    t_last_status = gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, nullptr, C, B2_EPI_BIAS, false, 0);
+}
+
+void run_int8_gemm_bias_gelu(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                             const float* scale_A, const float* scale_B, const float* bias, float* C) {
+    t_last_status =
+        gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, nullptr, C, B2_EPI_BIAS_GELU, false, 0);
+}
+
+void run_int8_gemm_bias_residual(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                                 const float* scale_A, const float* scale_B, const float* bias,
+                                 const float* residual, float* C) {
+    t_last_status = gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C,
+                                B2_EPI_BIAS_RESIDUAL, false, 0);
+}

@@ -1,0 +1,498 @@
+// K13 on sm_100a: split-K paged decode attention, one query token per sequence.
+//
+// Semantics follow the reference's decode_attn_partial_kernel + decode_attn_reduce_kernel
+// (kernels/decode/13_decode_attn.cuh:30-189, kernels/decode/13_decode_attn.cu:10-53):
+//   O[b,h,:] = softmax(q[b,h] . K[b, 0..ctx_b)^T * scale) . V[b, 0..ctx_b)
+// with K/V rows found through the block table, kv_head = h / (H_q / H_kv), and the KV
+// sequence split into ranges of whole blocks whose partial (o, m, l) are merged by
+// log-sum-exp. It implements the intended math where the reference does not: empty
+// splits contribute nothing (the reference leaves their workspace rows unwritten and then
+// reads them, 13_decode_attn.cuh:56), a zero-length context yields O = 0, head_dim 128
+// and bf16 caches are supported, and cache offsets are 64-bit.
+//
+// B200 design (one CTA per (split, kv_head, sequence)):
+//   - the CTA serves all G = H_q/H_kv query heads of its KV head, so every K/V byte is
+//     read from HBM once (the reference re-reads it once per query head);
+//   - warp 8 is a producer: each lane issues a 1-D bulk copy (cp.async.bulk, TMA engine)
+//     of one token's K row and V row into a STAGES-deep shared-memory ring, completion
+//     counted on an mbarrier; the block table is read by the producer only;
+//   - warps 0..7 consume 32-token tiles: split-d partial dot products (no shuffles), an
+//     exp2-domain online softmax per tile, then P.V with each lane owning head_dim/32
+//     output columns; K rows sit 16 B apart from a 128 B multiple so all shared loads
+//     are bank-conflict free;
+//   - the split merge is fused: every CTA of a (sequence, KV head) writes its partial to
+//     the workspace, and the last to arrive (atomic ticket) merges and writes O.
+#include "common.cuh"
+#include <cuda_bf16.h>
+#include <algorithm>
+#include <cmath>
+
+namespace b2 {
+
+constexpr int DA_NW = 8;                 // consumer warps
+constexpr int DA_NT = (DA_NW + 1) * 32;  // + producer warp
+constexpr int DA_T = 32;                 // tokens per tile
+
+struct DecodeAttnParams {
+    const float* Q;
+    const unsigned char* k_cache;
+    const unsigned char* v_cache;
+    const int* block_table;
+    const int* context_lens;
+    float* O;
+    float* ws_partial;          // [B, H_q, num_splits, D + 2]
+    unsigned int* ws_counter;   // [B, H_kv]
+    int H_q, H_kv, block_size, num_blocks_per_seq, num_phys_blocks;
+    int num_splits, blocks_per_split;
+    float scale_log2;           // softmax scale * log2(e)
+    unsigned int* err;          // device error word
+};
+
+template <int G, int D, typename KV>
+struct DACfg {
+    static constexpr int ES = (int)sizeof(KV);
+    static constexpr int ROW = D * ES;                 // bytes of one K or V row
+    static constexpr int KROW = ROW + 16;              // skewed K row pitch in shared memory
+    static constexpr int STAGE = DA_T * KROW + DA_T * ROW;
+    static constexpr int STAGES_RAW = (100 * 1024) / STAGE;
+    static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+    static constexpr int DS = D / DA_NW;               // dims per warp in the score phase
+    static constexpr int VPL = D / 32;                 // dims per lane in the P.V phase
+    // shared-memory carve-up (bytes)
+    static constexpr int OFF_Q = STAGES * STAGE;                         // f32 [G][D]
+    static constexpr int OFF_SC = OFF_Q + G * D * 4;                     // f32 [NW][G][T]
+    static constexpr int OFF_P = OFF_SC + DA_NW * G * DA_T * 4;          // f32 [T][G]
+    static constexpr int OFF_ALPHA = OFF_P + DA_T * G * 4;               // f32 [G]
+    static constexpr int OFF_ML = OFF_ALPHA + 8 * 4;                     // f32 [G][2]
+    static constexpr int OFF_MISC = OFF_ML + 16 * 4;                     // u32 flags
+    static constexpr int OFF_BAR = (OFF_MISC + 16 + 7) & ~7;             // u64 full[S], empty[S]
+    static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8;
+    static_assert(D % 32 == 0 && DS % 8 == 0, "head_dim must be 64 or 128");
+    static_assert(DA_NW * G * D * 4 <= STAGES * STAGE, "final reduction must fit the ring");
+    static_assert(G <= DA_NW, "group size must not exceed the consumer warp count");
+};
+
+// Load N elements of a K/V row from shared memory into fp32 registers.
+template <typename KV, int N>
+__device__ __forceinline__ void load_row(const unsigned char* p, float (&f)[N]) {
+    if constexpr (sizeof(KV) == 4) {
+        static_assert(N % 2 == 0, "");
+        if constexpr (N % 4 == 0) {
+#pragma unroll
+            for (int i = 0; i < N / 4; ++i) {
+                float4 v = reinterpret_cast<const float4*>(p)[i];
+                f[4 * i] = v.x; f[4 * i + 1] = v.y; f[4 * i + 2] = v.z; f[4 * i + 3] = v.w;
+            }
+        } else {
+            float2 v = *reinterpret_cast<const float2*>(p);
+            f[0] = v.x; f[1] = v.y;
+        }
+    } else {
+        // bf16 -> fp32 is exact: the bf16 bits are the top half of the fp32 word.
+        if constexpr (N % 8 == 0) {
+#pragma unroll
+            for (int i = 0; i < N / 8; ++i) {
+                uint4 v = reinterpret_cast<const uint4*>(p)[i];
+                uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    f[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+                    f[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+                }
+            }
+        } else if constexpr (N == 4) {
+            uint2 v = *reinterpret_cast<const uint2*>(p);
+            f[0] = __uint_as_float(v.x << 16); f[1] = __uint_as_float(v.x & 0xffff0000u);
+            f[2] = __uint_as_float(v.y << 16); f[3] = __uint_as_float(v.y & 0xffff0000u);
+        } else {
+            static_assert(N == 2, "");
+            uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+            f[0] = __uint_as_float(v << 16); f[1] = __uint_as_float(v & 0xffff0000u);
+        }
+    }
+}
+
+template <int G, int D, typename KV>
+__global__ void __launch_bounds__(DA_NT, 2)
+decode_attn_kernel(const DecodeAttnParams p) {
+    using C = DACfg<G, D, KV>;
+    extern __shared__ __align__(1024) unsigned char smem[];
+
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y;
+    const int b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    // ---- this CTA's token range (whole blocks, as the reference splits, 13_decode_attn.cu:63-65)
+    int ctx = p.context_lens[b];
+    const int cap = p.num_blocks_per_seq * p.block_size;
+    if (ctx > cap) {
+        if (tid == 0 && split == 0 && kvh == 0) raise_error(p.err, B2_DEVERR_CTX_RANGE);
+        ctx = cap;
+    }
+    if (ctx < 0) ctx = 0;
+    const int nblk = (ctx + p.block_size - 1) / p.block_size;
+    const int nsplit = (nblk + p.blocks_per_split - 1) / p.blocks_per_split;  // non-empty splits
+    const int hq0 = kvh * G;
+    float* O = p.O + ((size_t)b * p.H_q + hq0) * D;
+
+    if (nblk == 0) {  // empty context: O = 0 (reference reduce writes o * 0, 13_decode_attn.cu:48-52)
+        if (split == 0)
+            for (int i = tid; i < G * D; i += DA_NT) O[i] = 0.f;
+        return;
+    }
+    if (split >= nsplit) return;  // empty split: contributes nothing
+
+    const int tok_begin = split * p.blocks_per_split * p.block_size;
+    const int tok_end = min(ctx, (split + 1) * p.blocks_per_split * p.block_size);
+    const int ntiles = (tok_end - tok_begin + DA_T - 1) / DA_T;
+
+    float* q_s = reinterpret_cast<float*>(smem + C::OFF_Q);
+    float* sc_s = reinterpret_cast<float*>(smem + C::OFF_SC);
+    float* p_s = reinterpret_cast<float*>(smem + C::OFF_P);
+    float* alpha_s = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
+    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);
+    volatile unsigned int* misc = reinterpret_cast<volatile unsigned int*>(smem + C::OFF_MISC);
+    const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+    const uint32_t ring = smem_u32(smem);
+
+    if (tid == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), DA_NW);
+        }
+        misc[0] = 0;  // abort flag
+        misc[1] = 0;  // merge ticket
+        fence_mbar_init();
+    }
+    // q pre-scaled into the exp2 domain
+    const float* Qb = p.Q + ((size_t)b * p.H_q + hq0) * D;
+    for (int i = tid; i < G * D; i += DA_NT) q_s[i] = Qb[i] * p.scale_log2;
+    __syncthreads();
+
+    if (warp == DA_NW) {
+        // ------------------------------------------------------------ producer warp
+        const int* bt = p.block_table + (size_t)b * p.num_blocks_per_seq;
+        const uint64_t pol = policy_evict_first();
+        int issued = 0;
+        for (int i = 0; i < ntiles; ++i) {
+            const int st = i % C::STAGES;
+            if (i >= C::STAGES) {
+                const uint32_t par = ((i / C::STAGES) - 1) & 1;
+                bool ok = misc[0] == 0 && mbar_wait(empty_bar(st), par, p.err);
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) { if (lane == 0) misc[0] = 1; break; }
+            }
+            const int t0 = tok_begin + i * DA_T;
+            const int n = min(DA_T, tok_end - t0);
+            if (lane == 0) mbar_arrive_expect_tx(full_bar(st), (uint32_t)(n * 2 * C::ROW));
+            __syncwarp();
+            if (lane < n) {
+                const int pos = t0 + lane;
+                const int blk = pos / p.block_size;
+                const int slot = pos - blk * p.block_size;
+                int phys = bt[blk];
+                if (p.num_phys_blocks > 0 && (unsigned)phys >= (unsigned)p.num_phys_blocks) {
+                    raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
+                    phys = 0;
+                }
+                const size_t off = (((size_t)phys * p.block_size + slot) * p.H_kv + kvh) * (size_t)C::ROW;
+                const uint32_t sbase = ring + st * C::STAGE;
+                bulk_g2s(sbase + lane * C::KROW, p.k_cache + off, C::ROW, full_bar(st), pol);
+                bulk_g2s(sbase + DA_T * C::KROW + lane * C::ROW, p.v_cache + off, C::ROW, full_bar(st), pol);
+            }
+            issued = i + 1;
+        }
+        // Drain: if consumers aborted, make sure no copy is still landing in the ring.
+        if (misc[0] != 0 && lane == 0) {
+            for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+                (void)mbar_wait(full_bar(i % C::STAGES), (i / C::STAGES) & 1, p.err);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumer warps
+    constexpr int NC = DA_NW * 32;
+    float acc[G][C::VPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < C::VPL; ++j) acc[g][j] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;  // meaningful in warp g < G (head g)
+
+    for (int i = 0; i < ntiles; ++i) {
+        const int st = i % C::STAGES;
+        const int n = min(DA_T, tok_end - (tok_begin + i * DA_T));
+        if (misc[0] == 0) {
+            if (!mbar_wait(full_bar(st), (i / C::STAGES) & 1, p.err)) misc[0] = 1;
+        }
+        const unsigned char* Kt = smem + st * C::STAGE;
+        const unsigned char* Vt = Kt + DA_T * C::KROW;
+
+        // Phase A: partial scores over this warp's slice of head_dim. Thread = token.
+        {
+            const int t = lane;
+            float part[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) part[g] = 0.f;
+            if (t < n) {
+                float kf[C::DS];
+                load_row<KV, C::DS>(Kt + t * C::KROW + warp * C::DS * C::ES, kf);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4* q4 = reinterpret_cast<const float4*>(q_s + g * D + warp * C::DS);
+#pragma unroll
+                    for (int j = 0; j < C::DS / 4; ++j) {
+                        const float4 q = q4[j];
+                        part[g] = fmaf(q.x, kf[4 * j], part[g]);
+                        part[g] = fmaf(q.y, kf[4 * j + 1], part[g]);
+                        part[g] = fmaf(q.z, kf[4 * j + 2], part[g]);
+                        part[g] = fmaf(q.w, kf[4 * j + 3], part[g]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc_s[(warp * G + g) * DA_T + t] = part[g];
+        }
+        named_barrier(1, NC);
+
+        // Phase B: online softmax for head g = warp (exp2 domain). Lane = token.
+        if (warp < G) {
+            const int g = warp;
+            float s = -INFINITY;
+            if (lane < n) {
+                s = 0.f;
+#pragma unroll
+                for (int w = 0; w < DA_NW; ++w) s += sc_s[(w * G + g) * DA_T + lane];
+            }
+            const float m_new = fmaxf(m_run, warp_max(s));
+            const float alpha = exp2f(m_run - m_new);  // m_run = -inf on the first tile -> 0
+            const float pr = (lane < n) ? exp2f(s - m_new) : 0.f;
+            l_run = l_run * alpha + warp_sum(pr);
+            m_run = m_new;
+            p_s[lane * G + g] = pr;
+            if (lane == 0) alpha_s[g] = alpha;
+        }
+        named_barrier(1, NC);
+
+        // Phase C: acc = acc * alpha + P.V. Warp = token subset, lane = head_dim columns.
+        {
+            float al[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) al[g] = alpha_s[g];
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int j = 0; j < C::VPL; ++j) acc[g][j] *= al[g];
+#pragma unroll
+            for (int k = 0; k < DA_T / DA_NW; ++k) {
+                const int t = warp + k * DA_NW;
+                if (t < n) {
+                    float vf[C::VPL];
+                    load_row<KV, C::VPL>(Vt + t * C::ROW + lane * C::VPL * C::ES, vf);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float pg = p_s[t * G + g];
+#pragma unroll
+                        for (int j = 0; j < C::VPL; ++j) acc[g][j] = fmaf(pg, vf[j], acc[g][j]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(st));
+    }
+
+    // ---- combine the 8 warps' accumulators (same running max, so a plain sum)
+    named_barrier(1, NC);  // every warp is done reading the ring
+    float* red = reinterpret_cast<float*>(smem);  // [NW][G][D], reuses the ring
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < C::VPL; ++j) red[(warp * G + g) * D + lane * C::VPL + j] = acc[g][j];
+    if (warp < G && lane == 0) {
+        ml_s[2 * warp] = m_run;
+        ml_s[2 * warp + 1] = l_run;
+    }
+    named_barrier(1, NC);
+    if (misc[0] != 0) return;  // a wait gave up: the error bit is set, O is left untouched
+
+    if (nsplit == 1) {
+        for (int i = tid; i < G * D; i += NC) {
+            const int g = i / D;
+            float o = 0.f;
+#pragma unroll
+            for (int w = 0; w < DA_NW; ++w) o += red[w * G * D + i];
+            const float l = ml_s[2 * g + 1];
+            O[i] = l > 0.f ? o / l : 0.f;
+        }
+        return;
+    }
+
+    // ---- write this split's partial, then the last CTA of the (b, kv_head) merges
+    const size_t rowlen = D + 2;
+    for (int i = tid; i < G * D; i += NC) {
+        const int g = i / D, d = i - g * D;
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < DA_NW; ++w) o += red[w * G * D + i];
+        float* ws = p.ws_partial + (((size_t)b * p.H_q + hq0 + g) * p.num_splits + split) * rowlen;
+        ws[d] = o;
+        if (d == 0) { ws[D] = ml_s[2 * g]; ws[D + 1] = ml_s[2 * g + 1]; }
+    }
+    __threadfence();
+    named_barrier(1, NC);
+    unsigned int* counter = p.ws_counter + (size_t)b * p.H_kv + kvh;
+    if (tid == 0) misc[1] = atomicAdd(counter, 1u);
+    named_barrier(1, NC);
+    if (misc[1] != (unsigned)(nsplit - 1)) return;
+    __threadfence();
+    for (int i = tid; i < G * D; i += NC) {
+        const int g = i / D, d = i - g * D;
+        const float* ws = p.ws_partial + ((size_t)b * p.H_q + hq0 + g) * p.num_splits * rowlen;
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(ws + s * rowlen + D));
+        float L = 0.f, o = 0.f;
+        for (int s = 0; s < nsplit; ++s) {
+            const float w = exp2f(__ldcg(ws + s * rowlen + D) - M);
+            L = fmaf(__ldcg(ws + s * rowlen + D + 1), w, L);
+            o = fmaf(__ldcg(ws + s * rowlen + d), w, o);
+        }
+        O[i] = L > 0.f ? o / L : 0.f;
+    }
+    if (tid == 0) *counter = 0u;  // every sibling has arrived: leave the counter reusable
+}
+
+// ------------------------------------------------------------------ host side
+
+struct SplitPlan {
+    int num_splits;
+    int blocks_per_split;
+};
+
+// Split policy: enough CTAs to fill the GPU a few times over, and no CTA streaming more
+// than ~512 KB of K+V, so ragged batches balance; capped by max_splits.
+static SplitPlan plan_splits(int B, int H_kv, int head_dim, int kv_bytes, int max_ctx, int block_size,
+                             int max_splits, int num_sms) {
+    const int max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
+    const long long pairs = (long long)B * H_kv;
+    const long long row_bytes = 2LL * head_dim * kv_bytes;           // K + V bytes per token
+    const long long tok_per_cta = std::max<long long>(64, (512LL * 1024) / row_bytes);
+    long long want = std::max<long long>((4LL * num_sms + pairs - 1) / pairs,
+                                         ((long long)max_ctx + tok_per_cta - 1) / tok_per_cta);
+    // at least 2 blocks (32 tokens) of work per split
+    want = std::min<long long>(want, std::max(1, max_blocks / 2));
+    want = std::max<long long>(1, std::min<long long>(want, max_splits));
+    SplitPlan sp;
+    sp.blocks_per_split = (int)((max_blocks + want - 1) / want);
+    sp.num_splits = (max_blocks + sp.blocks_per_split - 1) / sp.blocks_per_split;
+    return sp;
+}
+
+bool set_smem_attr_once(const void* func, int bytes, int slot);
+
+template <int G, int D, typename KV>
+static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int B, cudaStream_t st) {
+    using C = DACfg<G, D, KV>;
+    constexpr int slot = 32 + (G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3) + (D == 64 ? 0 : 4) + (sizeof(KV) == 4 ? 0 : 8);
+    if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV>, C::SMEM, slot)) return cudaErrorInvalidValue;
+    dim3 grid(prm.num_splits, prm.H_kv, B);
+    decode_attn_kernel<G, D, KV><<<grid, DA_NT, C::SMEM, st>>>(prm);
+    return cudaGetLastError();
+}
+
+template <int D, typename KV>
+static cudaError_t dispatch_group(int G, const DecodeAttnParams& prm, int B, cudaStream_t st) {
+    switch (G) {
+        case 1: return launch_decode_attn_t<1, D, KV>(prm, B, st);
+        case 2: return launch_decode_attn_t<2, D, KV>(prm, B, st);
+        case 4: return launch_decode_attn_t<4, D, KV>(prm, B, st);
+        case 8: return launch_decode_attn_t<8, D, KV>(prm, B, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+int num_sms_current_device();
+
+// Workspace layout: [B, H_q, num_splits, D+2] f32 partials, then [B, H_kv] u32 counters
+// (256-byte aligned).
+static size_t partial_bytes(int B, int H_q, int D, int S) {
+    size_t b = (size_t)B * H_q * S * (D + 2) * sizeof(float);
+    return (b + 255) & ~(size_t)255;
+}
+
+constexpr int DA_MAX_SPLITS_ABI = 64;
+
+size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size,
+                                  int max_splits, int kv_bytes) {
+    SplitPlan sp = plan_splits(B, H_kv, D, kv_bytes, max_ctx, block_size, max_splits, num_sms_current_device());
+    return partial_bytes(B, H_q, D, sp.num_splits) + (size_t)B * H_kv * sizeof(unsigned int);
+}
+
+// Validates, plans and launches. `max_splits` bounds the split count (the drop-in
+// wrapper passes the reference workspace's capacity). `counters_zeroed` false makes the
+// launcher clear the counter region first (stream-ordered memset).
+int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counters_zeroed, cudaStream_t st) {
+    if (!a) return B2_ERR_INVALID;
+    if (a->B < 0 || a->H_q <= 0 || a->H_kv <= 0 || a->block_size <= 0 || a->num_blocks_per_seq < 0 ||
+        a->max_context_len < 0)
+        return B2_ERR_INVALID;
+    if (a->B == 0) return B2_OK;
+    if (!a->Q || !a->k_cache || !a->v_cache || !a->block_table || !a->context_lens || !a->O)
+        return B2_ERR_INVALID;
+    if (a->H_q % a->H_kv != 0) return B2_ERR_UNSUPPORTED;
+    const int G = a->H_q / a->H_kv;
+    if (G != 1 && G != 2 && G != 4 && G != 8) return B2_ERR_UNSUPPORTED;
+    if (a->head_dim != 64 && a->head_dim != 128) return B2_ERR_UNSUPPORTED;
+    if (a->kv_dtype != B2_KV_F32 && a->kv_dtype != B2_KV_BF16) return B2_ERR_UNSUPPORTED;
+    if (((uintptr_t)a->k_cache | (uintptr_t)a->v_cache) & 15) return B2_ERR_INVALID;  // bulk-copy alignment
+    if (((uintptr_t)a->Q | (uintptr_t)a->O) & 15) return B2_ERR_INVALID;
+    const int kvb = a->kv_dtype == B2_KV_F32 ? 4 : 2;
+
+    SplitPlan sp = plan_splits(a->B, a->H_kv, a->head_dim, kvb, a->max_context_len, a->block_size, max_splits,
+                               num_sms_current_device());
+    DecodeAttnParams prm;
+    prm.Q = a->Q;
+    prm.k_cache = static_cast<const unsigned char*>(a->k_cache);
+    prm.v_cache = static_cast<const unsigned char*>(a->v_cache);
+    prm.block_table = a->block_table;
+    prm.context_lens = a->context_lens;
+    prm.O = a->O;
+    prm.H_q = a->H_q;
+    prm.H_kv = a->H_kv;
+    prm.block_size = a->block_size;
+    prm.num_blocks_per_seq = a->num_blocks_per_seq;
+    prm.num_phys_blocks = a->num_phys_blocks;
+    prm.num_splits = sp.num_splits;
+    prm.blocks_per_split = sp.blocks_per_split;
+    const float scale = a->scale != 0.f ? a->scale : 1.0f / sqrtf((float)a->head_dim);
+    prm.scale_log2 = scale * 1.4426950408889634f;
+    prm.err = device_error_ptr();
+    prm.ws_partial = nullptr;
+    prm.ws_counter = nullptr;
+    if (sp.num_splits > 1) {
+        const size_t pb = partial_bytes(a->B, a->H_q, a->head_dim, sp.num_splits);
+        const size_t need = pb + (size_t)a->B * a->H_kv * sizeof(unsigned int);
+        if (!a->workspace || a->workspace_bytes < need) return B2_ERR_WORKSPACE;
+        if ((uintptr_t)a->workspace & 255) return B2_ERR_INVALID;
+        prm.ws_partial = static_cast<float*>(a->workspace);
+        prm.ws_counter = reinterpret_cast<unsigned int*>(static_cast<char*>(a->workspace) + pb);
+        if (!counters_zeroed) {
+            if (cudaMemsetAsync(prm.ws_counter, 0, (size_t)a->B * a->H_kv * sizeof(unsigned int), st) !=
+                cudaSuccess)
+                return B2_ERR_CUDA;
+        }
+    }
+    cudaError_t e;
+    if (a->head_dim == 64)
+        e = kvb == 4 ? dispatch_group<64, float>(G, prm, a->B, st) : dispatch_group<64, __nv_bfloat16>(G, prm, a->B, st);
+    else
+        e = kvb == 4 ? dispatch_group<128, float>(G, prm, a->B, st) : dispatch_group<128, __nv_bfloat16>(G, prm, a->B, st);
+    return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+}  // namespace b2

@@ -1,0 +1,385 @@
+// K14 on sm_100a: per-row symmetric INT8 quantiser and the INT8 GEMM on tcgen05.
+//
+// Quantiser semantics (reference kernels/quantization/14_int8_gemm.cu:10-60):
+//   amax = max_k |x[r,k]|;  scale = amax > 0 ? amax / 127 : 1;  inv = 1 / scale (IEEE);
+//   q = clamp(rint(x * inv), -128, 127) (round half to even);  packed little-endian 4 per int32.
+// GEMM semantics (reference kernels/quantization/14_int8_gemm.cu:65-170):
+//   acc = sum_k A[m,k] * B[n,k] (exact int32);  v = float(acc) * sA[m] * sB[n]
+//   then  +bias[n]  /  +bias, GELU-tanh  /  +bias +residual[m,n].
+// The reference's nvcc build contracts `v * sB + bias` into one fused multiply-add; the
+// epilogue below spells the same operations out (fmaf) so results are bit-identical.
+//
+// B200 design of the GEMM (one 128 x BN output tile per CTA, 192 threads):
+//   warp 0  : TMA producer — 2-D tensor-map loads of 128 x 128-byte A and BN x 128-byte B
+//             tiles in the 128-byte swizzle into a STAGES-deep ring (mbarrier full/empty);
+//   warp 1  : allocates BN TMEM columns and issues tcgen05.mma.cta_group::1.kind::i8
+//             (M=128, N=BN, K=32 per instruction, int32 accumulators in TMEM), releasing
+//             ring slots with tcgen05.commit;
+//   warps 2-5: epilogue — tcgen05.ld of the accumulator (one TMEM lane quadrant per warp,
+//             thread = output row), dequantise + bias / GELU / residual in registers, store.
+#include "common.cuh"
+#include <algorithm>
+#include <cmath>
+
+namespace b2 {
+
+// ------------------------------------------------------------------ quantiser
+constexpr int QZ_THREADS = 256;
+
+__global__ void __launch_bounds__(QZ_THREADS)
+quantize_rows_kernel(int cols, const float* __restrict__ in, int32_t* __restrict__ out,
+                     float* __restrict__ scales) {
+    const int row = blockIdx.x;
+    const float* x = in + (size_t)row * cols;
+    const int c4 = cols >> 2;
+    const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    float amax = 0.f;
+    if (vec) {
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (int i = threadIdx.x; i < c4; i += QZ_THREADS) {
+            float4 v = x4[i];
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        for (int i = threadIdx.x; i < cols; i += QZ_THREADS) amax = fmaxf(amax, fabsf(x[i]));
+    }
+    __shared__ float red[QZ_THREADS / 32];
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < QZ_THREADS / 32; ++w) amax = fmaxf(amax, red[w]);
+    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (threadIdx.x == 0) scales[row] = scale;
+    int32_t* o = out + (size_t)row * c4;
+    for (int i = threadIdx.x; i < c4; i += QZ_THREADS) {
+        float v[4];
+        if (vec) {
+            float4 t = reinterpret_cast<const float4*>(x)[i];
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+            v[0] = x[4 * i]; v[1] = x[4 * i + 1]; v[2] = x[4 * i + 2]; v[3] = x[4 * i + 3];
+        }
+        uint32_t packed = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float q = fminf(fmaxf(rintf(__fmul_rn(v[j], inv)), -128.f), 127.f);
+            packed |= (uint32_t)(uint8_t)(int8_t)(int)q << (8 * j);
+        }
+        o[i] = (int32_t)packed;
+    }
+}
+
+int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st) {
+    if (rows < 0 || cols < 0 || (cols & 3)) return B2_ERR_INVALID;
+    if (rows == 0) return B2_OK;
+    if (!in || !out || !scales) return B2_ERR_INVALID;
+    quantize_rows_kernel<<<rows, QZ_THREADS, 0, st>>>(cols, in, out, scales);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ epilogue math
+__device__ __forceinline__ float gelu_tanh(float v) {
+    // 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))), operation order of the reference
+    // epilogue (kernels/quantization/14_int8_gemm.cu:158-160) with its contraction.
+    const float x3 = __fmul_rn(__fmul_rn(v, v), v);
+    const float inner = __fmul_rn(0.7978845608f, __fmaf_rn(0.044715f, x3, v));
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <int EPI>
+__device__ __forceinline__ float epilogue(int32_t acc, float sa, float sb, float bias, float res) {
+    const float t = __fmul_rn(__int2float_rn(acc), sa);
+    if constexpr (EPI == B2_EPI_PLAIN) {
+        return __fmul_rn(t, sb);
+    } else {
+        const float v = __fmaf_rn(t, sb, bias);
+        if constexpr (EPI == B2_EPI_BIAS) return v;
+        if constexpr (EPI == B2_EPI_BIAS_GELU) return gelu_tanh(v);
+        return __fadd_rn(v, res);
+    }
+}
+
+// ------------------------------------------------------------------ tcgen05 GEMM
+constexpr int GM_BM = 128;
+constexpr int GM_BK = 128;  // bytes of K per stage (one 128-byte swizzle atom row)
+constexpr int GM_THREADS = 192;
+
+struct GemmParams {
+    int M, N, K;
+    const float* scale_A;
+    const float* scale_B;
+    const float* bias;
+    const float* residual;
+    void* C;  // float* or int32_t*
+    unsigned int* err;
+};
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int A_BYTES = GM_BM * GM_BK;
+    static constexpr int B_BYTES = BN * GM_BK;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int STAGES = std::min(8, (196 * 1024) / STAGE);
+    static constexpr int OFF_BAR = STAGES * STAGE;
+    static constexpr int SMEM = OFF_BAR + (2 * STAGES + 2) * 8 + 16 + 1024;  // + 1 KB for alignment
+    static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+};
+
+template <int BN, int EPI, bool S32>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                    const GemmParams p) {
+    using C = GemmCfg<BN>;
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-byte alignment for the 128-byte swizzle atoms
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + C::OFF_BAR;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+    const uint32_t accum_bar = bar0 + 8u * (2 * C::STAGES);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_BAR + (2 * C::STAGES + 2) * 8);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * GM_BM;
+    const int n0 = blockIdx.x * BN;
+    const int nk = (p.K + GM_BK - 1) / GM_BK;
+
+    if (threadIdx.x == 0) {
+        prefetch_tensormap(&mapA);
+        prefetch_tensormap(&mapB);
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(accum_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------------------- TMA producer
+            const uint64_t pol = policy_evict_last();
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % C::STAGES;
+                if (kb >= C::STAGES) {
+                    if (*abort_flag || !mbar_wait(empty_bar(s), ((kb / C::STAGES) - 1) & 1, p.err)) { *abort_flag = 1; break; }
+                }
+                const uint32_t a_s = sbase + s * C::STAGE;
+                const uint32_t b_s = a_s + C::A_BYTES;
+                mbar_arrive_expect_tx(full_bar(s), C::STAGE);
+                tma_load_2d(a_s, &mapA, kb * GM_BK, m0, full_bar(s), pol);
+                tma_load_2d(b_s, &mapB, kb * GM_BK, n0, full_bar(s), pol);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------------------------------------------------------- MMA issuer
+            constexpr uint32_t idesc = idesc_i8(GM_BM, BN);
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % C::STAGES;
+                if (*abort_flag || !mbar_wait(full_bar(s), (kb / C::STAGES) & 1, p.err)) { ok = false; *abort_flag = 1; break; }
+                tc_fence_after();
+                const uint32_t a_s = sbase + s * C::STAGE;
+                const uint32_t b_s = a_s + C::A_BYTES;
+                const uint64_t da = smem_desc_sw128(a_s);
+                const uint64_t db = smem_desc_sw128(b_s);
+#pragma unroll
+                for (int k = 0; k < GM_BK / 32; ++k) {
+                    // advance 32 bytes of K inside the swizzle atom: +2 in the 16-byte address field
+                    mma_i8(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                }
+                mma_commit(empty_bar(s));
+            }
+            (void)ok;
+            mma_commit(accum_bar);  // fires once every MMA issued above has completed
+        }
+        __syncwarp();
+    } else {
+        // -------------------------------------------------------------------- epilogue
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const bool ok = mbar_wait(accum_bar, 0, p.err) && *abort_flag == 0;
+        tc_fence_after();
+        const int row = m0 + quad * 32 + lane;
+        const bool row_ok = ok && row < p.M;
+        const float sa = row_ok ? p.scale_A[row] : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), r);
+            tmem_ld_wait();
+            const int n = n0 + c * 16;
+            if (!row_ok || n >= p.N) continue;
+            if constexpr (S32) {
+                int32_t* Crow = static_cast<int32_t*>(p.C) + (size_t)row * p.N;
+                if (n + 16 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4)
+                        *reinterpret_cast<int4*>(Crow + n + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+                } else {
+                    for (int j = 0; j < 16 && n + j < p.N; ++j) Crow[n + j] = (int32_t)r[j];
+                }
+            } else {
+                float* Crow = static_cast<float*>(p.C) + (size_t)row * p.N;
+                const float* Rrow = (EPI == B2_EPI_BIAS_RESIDUAL) ? p.residual + (size_t)row * p.N : nullptr;
+                float v[16];
+                if (n + 16 <= p.N) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float sb = __ldg(p.scale_B + n + j);
+                        const float bi = (EPI != B2_EPI_PLAIN) ? __ldg(p.bias + n + j) : 0.f;
+                        const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? Rrow[n + j] : 0.f;
+                        v[j] = epilogue<EPI>((int32_t)r[j], sa, sb, bi, rs);
+                    }
+                    if ((p.N & 3) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4*>(Crow + n + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) Crow[n + j] = v[j];
+                    }
+                } else {
+                    for (int j = 0; j < 16 && n + j < p.N; ++j) {
+                        const float sb = p.scale_B[n + j];
+                        const float bi = (EPI != B2_EPI_PLAIN) ? p.bias[n + j] : 0.f;
+                        const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? Rrow[n + j] : 0.f;
+                        Crow[n + j] = epilogue<EPI>((int32_t)r[j], sa, sb, bi, rs);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ SIMT path for K % 16 != 0
+// (the tensor-map row stride must be a multiple of 16 bytes). Plain exact int32 dot products.
+template <int EPI, bool S32>
+__global__ void __launch_bounds__(256)
+int8_gemm_simt_kernel(const int32_t* __restrict__ A, const int32_t* __restrict__ BT, const GemmParams p) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int m = blockIdx.y;
+    if (n >= p.N) return;
+    const int K4 = p.K >> 2;
+    const int32_t* a = A + (size_t)m * K4;
+    const int32_t* bb = BT + (size_t)n * K4;
+    int acc = 0;
+    for (int k = 0; k < K4; ++k) acc = __dp4a(a[k], bb[k], acc);
+    if constexpr (S32) {
+        static_cast<int32_t*>(p.C)[(size_t)m * p.N + n] = acc;
+    } else {
+        const float bi = (EPI != B2_EPI_PLAIN) ? p.bias[n] : 0.f;
+        const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? p.residual[(size_t)m * p.N + n] : 0.f;
+        static_cast<float*>(p.C)[(size_t)m * p.N + n] = epilogue<EPI>(acc, p.scale_A[m], p.scale_B[n], bi, rs);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// int8 row-major [rows, K] operand, box = box_rows x 128 bytes, 128-byte swizzle.
+static bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K};
+    cuuint32_t box[2] = {(cuuint32_t)GM_BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+int num_sms_current_device();
+bool set_smem_attr_once(const void* func, int bytes, int slot);
+
+template <int BN, int EPI, bool S32>
+static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, cudaStream_t st, int slot) {
+    using C = GemmCfg<BN>;
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, A, p.M, p.K, GM_BM) || !make_map(&mb, BT, p.N, p.K, BN)) return B2_ERR_CUDA;
+    auto kfn = int8_gemm_tc_kernel<BN, EPI, S32>;
+    if (!set_smem_attr_once((const void*)kfn, C::SMEM, slot)) return B2_ERR_CUDA;
+    dim3 grid((p.N + BN - 1) / BN, (p.M + GM_BM - 1) / GM_BM);
+    kfn<<<grid, GM_THREADS, C::SMEM, st>>>(ma, mb, p);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+template <int EPI, bool S32>
+static int gemm_dispatch(const GemmParams& p, const int32_t* A, const int32_t* BT, cudaStream_t st) {
+    // K == 0 (empty contraction, acc = 0) and K % 16 != 0 take the SIMT kernel
+    if (p.K == 0 || (p.K & 15) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)BT & 15)) {
+        dim3 grid((p.N + 255) / 256, p.M);
+        int8_gemm_simt_kernel<EPI, S32><<<grid, 256, 0, st>>>(A, BT, p);
+        return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    }
+    const int sms = num_sms_current_device();
+    const long long mt = (p.M + GM_BM - 1) / GM_BM;
+    // widest tile that still gives every SM a tile; otherwise the narrowest
+    const int slot_base = (EPI + (S32 ? 4 : 0)) * 3;
+    if (mt * ((p.N + 255) / 256) >= sms) return launch_tc<256, EPI, S32>(p, A, BT, st, slot_base + 0);
+    if (mt * ((p.N + 127) / 128) >= sms) return launch_tc<128, EPI, S32>(p, A, BT, st, slot_base + 1);
+    return launch_tc<64, EPI, S32>(p, A, BT, st, slot_base + 2);
+}
+
+int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
+                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st) {
+    if (M < 0 || N < 0 || K < 0 || (K & 3)) return B2_ERR_INVALID;
+    if (M == 0 || N == 0) return B2_OK;
+    if (!A || !BT || !C) return B2_ERR_INVALID;
+    if (!s32) {
+        if (!sA || !sB) return B2_ERR_INVALID;
+        if (epi < B2_EPI_PLAIN || epi > B2_EPI_BIAS_RESIDUAL) return B2_ERR_INVALID;
+        if (epi != B2_EPI_PLAIN && !bias) return B2_ERR_INVALID;
+        if (epi == B2_EPI_BIAS_RESIDUAL && !residual) return B2_ERR_INVALID;
+    }
+    GemmParams p{M, N, K, sA, sB, bias, residual, C, device_error_ptr()};
+    if (s32) return gemm_dispatch<B2_EPI_PLAIN, true>(p, A, BT, st);
+    switch (epi) {
+        case B2_EPI_PLAIN: return gemm_dispatch<B2_EPI_PLAIN, false>(p, A, BT, st);
+        case B2_EPI_BIAS: return gemm_dispatch<B2_EPI_BIAS, false>(p, A, BT, st);
+        case B2_EPI_BIAS_GELU: return gemm_dispatch<B2_EPI_BIAS_GELU, false>(p, A, BT, st);
+        default: return gemm_dispatch<B2_EPI_BIAS_RESIDUAL, false>(p, A, BT, st);
+    }
+}
+
+}  // namespace b2

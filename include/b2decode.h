@@ -1,0 +1,135 @@
+/*
+ * b2decode.h — C ABI of the B200 (sm_100a) GPT-2 decode hot path.
+ *
+ * Two kernels families sit behind this boundary:
+ *   - K13: split-K paged decode attention (one query token per sequence) over a
+ *     paged KV cache addressed through a per-sequence block table;
+ *   - K14: per-row symmetric INT8 quantizer and INT8 x INT8 -> INT32 GEMM with a fused
+ *     dequantisation epilogue (plain / +bias / +bias+GELU / +bias+residual).
+ *
+ * Conventions (all entry points):
+ *   - every pointer is a DEVICE pointer owned by the caller; nothing here allocates;
+ *   - work is enqueued asynchronously on `stream` (NULL = legacy default stream);
+ *   - every entry returns a b2_status; shapes the kernels do not support are errors,
+ *     never silent no-ops;
+ *   - faults detected on the device (a wait that timed out, a context length beyond its
+ *     block-table row, a block-table entry outside the pool) are recorded as bits in a
+ *     device error word, read with b2_get_device_error().
+ *
+ * Layouts are the reference's (mohith-suresh/CUDA-LLM-Inference-Engine):
+ *   Q, O            [B, H_q, 1, head_dim] fp32                      (kernels/decode/13_decode_attn.cuh:34)
+ *   k/v cache       [num_phys_blocks, block_size, H_kv, head_dim]  (kernels/decode/13_decode_attn.cuh:35-36)
+ *   block_table     [B, num_blocks_per_seq] int32                  (kernels/decode/13_decode_attn.cuh:37)
+ *   context_lens    [B] int32, read on the device                   (kernels/decode/13_decode_attn.cuh:38)
+ *   int8 operands   [rows, K/4] int32, byte j of word i = element 4i+j (little endian)
+ *                                                                   (kernels/quantization/14_int8_gemm.cu:43-58)
+ *   scales          [rows] fp32, scale = absmax/127 (1 if the row is all zero)
+ *                                                                   (kernels/quantization/14_int8_gemm.cu:36-38)
+ */
+#ifndef B2DECODE_H
+#define B2DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* b2_stream_t; /* a cudaStream_t */
+
+/* Host-side status codes. */
+enum {
+    B2_OK = 0,
+    B2_ERR_INVALID = 1,      /* bad argument: null pointer, negative size, misaligned buffer */
+    B2_ERR_UNSUPPORTED = 2,  /* shape the kernels do not implement (e.g. GQA group 3) */
+    B2_ERR_WORKSPACE = 3,    /* workspace missing or smaller than the size query returned */
+    B2_ERR_CUDA = 4          /* a CUDA runtime call failed (launch error, bad device) */
+};
+
+/* Device error bits (b2_get_device_error). */
+#define B2_DEVERR_TIMEOUT 1u      /* a bounded wait (mbarrier / flag) gave up */
+#define B2_DEVERR_CTX_RANGE 2u    /* context_lens[b] > num_blocks_per_seq * block_size */
+#define B2_DEVERR_BLOCK_RANGE 4u  /* block_table entry outside [0, num_phys_blocks) */
+
+/* KV-cache element types. */
+enum { B2_KV_F32 = 0, B2_KV_BF16 = 1 };
+
+/* INT8 GEMM epilogues; same order as the reference's `enum class I8Epilogue`
+ * (kernels/quantization/14_int8_gemm.cuh:36). */
+enum { B2_EPI_PLAIN = 0, B2_EPI_BIAS = 1, B2_EPI_BIAS_GELU = 2, B2_EPI_BIAS_RESIDUAL = 3 };
+
+/* ------------------------------------------------------------------ K13 decode attention */
+
+typedef struct {
+    int B, H_q, H_kv, head_dim;      /* head_dim in {64, 128}; H_q / H_kv in {1, 2, 4, 8} */
+    const float* Q;                  /* [B, H_q, head_dim] */
+    const void* k_cache;             /* [P, block_size, H_kv, head_dim], kv_dtype elements */
+    const void* v_cache;
+    int kv_dtype;                    /* B2_KV_F32 or B2_KV_BF16 */
+    const int* block_table;          /* [B, num_blocks_per_seq] */
+    const int* context_lens;         /* [B] (device) */
+    int max_context_len;             /* host upper bound of context_lens; sizes the split count */
+    int block_size;                  /* tokens per KV block (engine: 16) */
+    int num_blocks_per_seq;          /* block-table row stride */
+    int num_phys_blocks;             /* P, for device bounds checks; 0 = unchecked */
+    float scale;                     /* softmax scale; 0 = 1/sqrt(head_dim) */
+    float* O;                        /* [B, H_q, head_dim] */
+    void* workspace;                 /* see b2_decode_attn_workspace_size */
+    size_t workspace_bytes;
+} b2_decode_attn_args;
+
+/* Bytes of workspace b2_decode_attn needs for these shapes. The workspace holds per-split
+ * partial results and one arrival counter per (sequence, KV head). The counters must be
+ * zero before the first call (cudaMemset once); every call leaves them zero again.
+ * Replaces the caller-side sizing `B*H_q*DA_MAX_SPLITS*(d+2)` floats
+ * (reference src/gpt2_engine.cu:156, tests/test_decode_attention.cu:91). */
+size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim,
+                                     int max_context_len, int block_size);
+
+/* Split-K paged decode attention, one launch (split merge fused into the kernel).
+ * Replaces run_decode_attn (reference kernels/decode/13_decode_attn.cu:84-109). */
+int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ K14 INT8 */
+
+/* Per-row symmetric fp32 -> int8 quantisation, packed 4 per int32, plus fp32 scales.
+ * Replaces run_quantize_fp32_to_int8 (reference kernels/quantization/14_int8_gemm.cu:172-180).
+ * cols must be a multiple of 4. */
+int b2_quantize_fp32_to_int8(int rows, int cols, const float* input, int32_t* output_packed,
+                             float* scales, b2_stream_t stream);
+
+/* C[M,N] = epilogue( float(sum_k A[m,k] * BT[n,k]) * scale_A[m] * scale_B[n] ).
+ * bias [N] is read for every epilogue but PLAIN; residual [M,N] only for BIAS_RESIDUAL.
+ * Replaces run_int8_gemm / _bias / _bias_gelu / _bias_residual
+ * (reference kernels/quantization/14_int8_gemm.cu:182-232). K must be a multiple of 4. */
+int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                 const float* scale_A, const float* scale_B, const float* bias,
+                 const float* residual, float* C, int epilogue, b2_stream_t stream);
+
+/* Raw int32 accumulators C_acc[M,N] = sum_k A[m,k] * BT[n,k] (no dequantisation): the
+ * bit-exact view of the contraction inside the reference's int8_gemm_dp4a_kernel
+ * (kernels/quantization/14_int8_gemm.cu:96-140), which the reference never exposes. */
+int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                     int32_t* C_acc, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ diagnostics */
+
+/* Returns the device error word of the current device (B2_DEVERR_* bits), synchronising
+ * the device first; clears it when clear != 0. */
+unsigned int b2_get_device_error(int clear);
+
+/* Status of the last call made through the reference-compatible C++ wrappers, which
+ * return void (include/b2_reference_api.h). */
+int b2_last_status(void);
+
+const char* b2_status_string(int status);
+
+/* Library ABI version (major * 100 + minor). */
+int b2_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2DECODE_H */

@@ -1,0 +1,25 @@
+#!/usr/bin/env bash
+# Builds the oracle libraries (test infrastructure only):
+#   oracle/liboracle.so    the C restatement (oracle.c), gcc, OpenMP;
+#   oracle/_ref/libref.so  the reference's own sources, compiled unchanged from where they
+#                          lie (REF, default /root/reference): its CPU attention harness and
+#                          its K10-K14 CUDA kernels for sm_100a. Skipped when REF is absent
+#                          (the GPU box uses the prebuilt file).
+set -euo pipefail
+HERE="$(cd "$(dirname "$0")" && pwd)"
+REF="${REF:-/root/reference}"
+NVCC="${NVCC:-/usr/local/cuda/bin/nvcc}"
+gcc -O2 -fPIC -shared -fopenmp -ffp-contract=off -o "$HERE/liboracle.so" "$HERE/oracle.c" -lm
+if [ -d "$REF/kernels" ]; then
+  mkdir -p "$HERE/_ref"
+  "$NVCC" -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -shared -Xcompiler -fPIC \
+    -Xcompiler -fvisibility=hidden -Xcompiler -ffp-contract=off \
+    -I "$HERE/ref_shim" -I "$REF/include" -I "$REF/kernels" -I "$REF" \
+    -o "$HERE/_ref/libref.so" \
+    "$HERE/ref_wrappers.cu" \
+    "$REF/kernels/flash_attention/10_flash_attn_v2.cu" \
+    "$REF/kernels/paged_attention/11_paged_attn.cu" \
+    "$REF/kernels/paged_attention/12_gqa.cu" \
+    "$REF/kernels/decode/13_decode_attn.cu" \
+    "$REF/kernels/quantization/14_int8_gemm.cu"
+fi

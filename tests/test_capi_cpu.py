@@ -1,0 +1,76 @@
+"""CPU checks of the boundary: the library loads without a GPU and exports every symbol
+declared in include/*.h; host-side argument validation needs no device."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_c_symbols():
+    txt = open(os.path.join(ROOT, "include", "b2decode.h")).read()
+    return sorted(set(re.findall(r"\b(b2_[a-z0-9_]+)\s*\(", txt)))
+
+
+def declared_cxx_symbols():
+    txt = open(os.path.join(ROOT, "include", "b2_reference_api.h")).read()
+    return sorted(set(re.findall(r"^void\s+(run_[a-z0-9_]+)\s*\(", txt, re.M)))
+
+
+def test_header_symbol_lists_match_package(b2):
+    assert declared_c_symbols() == sorted(b2.C_ABI_SYMBOLS)
+    assert declared_cxx_symbols() == sorted(b2._CXX)
+
+
+def test_library_exports_every_declared_symbol(b2):
+    lib = b2.load_library()
+    for s in declared_c_symbols():
+        assert hasattr(lib, s), s
+    out = subprocess.run(["nm", "-D", "--defined-only", b2.LIB_PATH], capture_output=True, text=True).stdout
+    for name, mangled in b2._CXX.items():
+        assert f" T {mangled}" in out, name
+        demangled = subprocess.run(["c++filt", mangled], capture_output=True, text=True).stdout
+        assert demangled.startswith(name + "("), demangled
+
+
+def test_version_and_status_strings(b2):
+    lib = b2.load_library()
+    assert lib.b2_version() >= 100
+    assert lib.b2_status_string(b2.B2_ERR_UNSUPPORTED) == b"unsupported shape"
+    assert lib.b2_status_string(99) == b"unknown status"
+
+
+def test_host_validation_without_device(b2):
+    """Argument errors are reported before any CUDA call is made."""
+    lib = b2.load_library()
+    a = b2.DecodeAttnArgs()
+    a.B, a.H_q, a.H_kv, a.head_dim, a.block_size = 1, 3, 1, 64, 16
+    a.Q = a.k_cache = a.v_cache = a.block_table = a.context_lens = a.O = 16
+    assert lib.b2_decode_attn(ctypes.byref(a), None) == b2.B2_ERR_UNSUPPORTED  # group 3
+    a.H_q, a.head_dim = 2, 96
+    assert lib.b2_decode_attn(ctypes.byref(a), None) == b2.B2_ERR_UNSUPPORTED  # head_dim 96
+    a.head_dim = 64
+    a.k_cache = 8
+    assert lib.b2_decode_attn(ctypes.byref(a), None) == b2.B2_ERR_INVALID     # misaligned cache
+    assert lib.b2_decode_attn(None, None) == b2.B2_ERR_INVALID
+    assert lib.b2_quantize_fp32_to_int8(2, 6, 16, 16, 16, None) == b2.B2_ERR_INVALID  # cols % 4
+    assert lib.b2_int8_gemm(2, 2, 6, 16, 16, 16, 16, None, None, 16, 0, None) == b2.B2_ERR_INVALID
+    assert lib.b2_int8_gemm(2, 2, 8, 16, 16, 16, 16, None, None, 16, 1, None) == b2.B2_ERR_INVALID  # no bias
+    assert lib.b2_int8_gemm(0, 2, 8, 16, 16, 16, 16, None, None, 16, 0, None) == b2.B2_OK  # empty
+
+
+def test_workspace_size_query(b2):
+    lib = b2.load_library()
+    # 1 split (short context): counters only; long context: partial rows + counters
+    short = lib.b2_decode_attn_workspace_size(1, 12, 12, 64, 32, 16)
+    long_ = lib.b2_decode_attn_workspace_size(32, 32, 8, 128, 8192, 16)
+    assert short > 0 and long_ > short
+    assert lib.b2_decode_attn_workspace_size(0, 1, 1, 64, 1, 16) == 0
+
+
+def test_missing_library_fails_loudly(b2, tmp_path):
+    with pytest.raises(b2.B2Error, match="no CPU fallback"):
+        b2.load_library(str(tmp_path / "nope.so"))
