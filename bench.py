@@ -1,0 +1,484 @@
+"""Benchmark of the B200 decode hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1; heads sharded across ranks)
+
+Headline workload: GQA paged decode attention, batch 32, 32 query /
+8 KV heads (group 4), head_dim 128, ragged context lengths U[512, 8192] (seeded), 16-token
+blocks behind a seeded random block table, fp32 KV cache, Q/K/V ~ N(0,1). One step = one
+decode-attention launch over the whole batch. Metric: algorithmic HBM GB/s = bytes of the
+live K/V + Q + O + block table + context lengths per step / step time (workspace traffic
+excluded). KV heads are sharded across ranks (no collective on the data path); the
+whole-job value is total bytes / max-over-ranks time ("strong": total work is fixed).
+
+Secondary lines (N=1 only): the same batch with a bf16 KV cache, BASELINE config 1 (MHA,
+B1 H12 d64 ctx1024), and the INT8 GEMMs of config 2 (2048^3, 64x3072x768) plus the
+north-star 8192^3, in TOPS.
+
+--impl reference times the reference's CPU implementation of the path (the oracle's
+restatement of its CPU attention harness, all host threads) on a bounded sample of the
+same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+SEED = 42
+B, H_Q, H_KV, D, BS = 32, 32, 8, 128, 16
+CTX_LO, CTX_HI = 512, 8192
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def workload_meta():
+    """Context lengths, block table and physical block count of the headline workload
+    (identical on every rank; numpy, seeded)."""
+    import numpy as np
+
+    rng = np.random.default_rng(SEED)
+    lens = rng.integers(CTX_LO, CTX_HI + 1, B).astype(np.int32)
+    nb = (lens + BS - 1) // BS
+    P = int(nb.sum())
+    nbps = int(nb.max())
+    perm = rng.permutation(P).astype(np.int32)
+    bt = np.zeros((B, nbps), np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, : nb[b]] = perm[off: off + nb[b]]
+        off += int(nb[b])
+    return lens, bt, P
+
+
+def attn_alg_bytes(lens, h_kv, h_q, d, kv_bytes, nbps):
+    """Algorithmic HBM bytes of one decode-attention call: live K and V rows, Q, O, the
+    block table and context lengths, each once."""
+    kv = int(lens.sum()) * 2 * h_kv * d * kv_bytes
+    qo = 2 * len(lens) * h_q * d * 4
+    return kv + qo + len(lens) * nbps * 4 + len(lens) * 4
+
+
+class ClockMonitor:
+    """Samples nvidia-smi clocks and throttle reasons every 100 ms in the background."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.25)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def time_steps(torch, fn, steps, warmup, dist=None):
+    """W untimed steps, then K steps bracketed by barrier + synchronize, timed with CUDA
+    events on the current stream; returns the max over ranks of the elapsed ms."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    return ms
+
+
+def make_kv_shard(torch, P, h0, h1, dtype, device):
+    """K/V cache [P, BS, h1-h0, D] for KV heads [h0, h1); each head's values come from its
+    own seeded generator, so a shard equals the same heads of the unsharded cache."""
+    nh = h1 - h0
+    kc = torch.empty(P, BS, nh, D, dtype=dtype, device=device)
+    vc = torch.empty_like(kc)
+    for i, h in enumerate(range(h0, h1)):
+        g = torch.Generator(device=device).manual_seed(SEED * 1000 + h)
+        kc[:, :, i].copy_(torch.randn(P, BS, D, generator=g, device=device).to(dtype))
+        vc[:, :, i].copy_(torch.randn(P, BS, D, generator=g, device=device).to(dtype))
+    return kc, vc
+
+
+def cpu_sample(torch, kc, vc, bt, lens, seqs):
+    """Numpy copy of sequences `seqs` of a device KV cache, with the blocks compacted and
+    the block table remapped (for the CPU legs)."""
+    import numpy as np
+
+    rows, sub_bt = [], np.zeros((len(seqs), bt.shape[1]), np.int32)
+    for i, b in enumerate(seqs):
+        nb = (int(lens[b]) + BS - 1) // BS
+        sub_bt[i, :nb] = np.arange(len(rows), len(rows) + nb)
+        rows.extend(int(x) for x in bt[b, :nb])
+    idx = torch.tensor(rows, device=kc.device, dtype=torch.long)
+
+    def host(t):
+        h = t[idx]
+        if h.dtype == torch.bfloat16:
+            return h.view(torch.int16).cpu().numpy().view(np.uint16)
+        return h.cpu().numpy()
+
+    return host(kc), host(vc), sub_bt, lens[list(seqs)].copy()
+
+
+def time_cpu_attention(oracle, q, kc, vc, bt, lens, nthreads, budget_s, min_reps=1):
+    """Runs the oracle over the sample until `budget_s` seconds have passed (at least
+    min_reps times); returns seconds per repetition."""
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.decode_attn(q, kc, vc, bt, lens, nthreads=nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if reps >= min_reps and el >= budget_s:
+            return el / reps
+        if el > 4 * budget_s:
+            return el / reps
+
+
+def gemm_secondary(torch, b2, M, N, K, steps, peak_int8):
+    """TOPS of the INT8 GEMM (fp32 dequantised output, plain epilogue) at M x N x K."""
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(SEED + M + N + K)
+    # rotate enough operand copies that the working set of consecutive calls exceeds L2
+    per = M * K + N * K + 4 * M * N
+    copies = max(1, min(16, (512 << 20) // per + 1))
+    bufs = []
+    for _ in range(copies):
+        A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g).view(torch.int32)
+        Bt = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g).view(torch.int32)
+        sA = torch.rand(M, device=dev, generator=g) / 127
+        sB = torch.rand(N, device=dev, generator=g) / 127
+        C = torch.empty(M, N, device=dev)
+        bufs.append((A, Bt, sA, sB, C))
+    it = [0]
+
+    def step():
+        A, Bt, sA, sB, C = bufs[it[0] % copies]
+        it[0] += 1
+        b2.int8_gemm(A, Bt, sA, sB, C=C)
+
+    n = max(3, min(steps, 200))
+    ms = time_steps(torch, step, n, 3)
+    tops = 2.0 * M * N * K / (ms / n * 1e-3) / 1e12
+    return {"tops": round(tops, 2), "us_per_call": round(ms / n * 1e3, 2), "frac_of_int8_peak": round(tops / peak_int8, 4),
+            "operand_copies": copies}
+
+
+def run_gpu(args):
+    import numpy as np
+    import torch
+
+    b2 = importlib.import_module("cuda-llm-inference-engine_b200")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        dist = tdist
+    if H_KV % world:
+        raise SystemExit(f"{H_KV} KV heads do not shard over {world} ranks")
+    b2.load_library()
+    dev = torch.device("cuda", local)
+    hbm_peak, bf16_peak, peak_kind = measured_peaks()
+
+    lens, bt, P = workload_meta()
+    nbps = bt.shape[1]
+    hkv = H_KV // world
+    hq = H_Q // world
+    h0 = rank * hkv
+    kc, vc = make_kv_shard(torch, P, h0, h0 + hkv, torch.float32, dev)
+    gq = torch.Generator(device=dev).manual_seed(SEED + 1)
+    q_full = torch.randn(B, H_Q, D, generator=gq, device=dev)
+    q = q_full[:, rank * hq:(rank + 1) * hq].contiguous()
+    O = torch.empty_like(q)
+    btd = torch.from_numpy(bt).to(dev)
+    lensd = torch.from_numpy(lens).to(dev)
+    max_ctx = int(lens.max())
+    ws = b2.make_decode_workspace(B, hq, hkv, D, max_ctx, BS, device=dev)
+
+    def step():
+        b2.decode_attn(q, kc, vc, btd, lensd, max_ctx, O=O, workspace=ws)
+
+    with ClockMonitor(local) as mon:
+        ms = time_steps(torch, step, args.steps, args.warmup, dist)
+    clocks = mon.summary()
+    assert b2.device_error() == 0, "device error during the timed region"
+    bytes_rank = attn_alg_bytes(lens, hkv, hq, D, 4, nbps)
+    bytes_total = attn_alg_bytes(lens, H_KV, H_Q, D, 4, nbps)
+    ms_step = ms / args.steps
+    value = bytes_total / (ms_step * 1e-3) / 1e9
+    # dominant (only) kernel: one decode_attn_kernel launch per step on this stream
+    achieved = bytes_rank / (ms_step * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers: pinned Q, block table and
+    # context lengths copied in, O copied out, every step (the KV cache stays resident)
+    q_h = q.cpu().pin_memory()
+    bt_h = torch.from_numpy(bt).pin_memory()
+    lens_h = torch.from_numpy(lens).pin_memory()
+    o_h = torch.empty_like(q_h).pin_memory()
+    q_d, bt_d, lens_d = torch.empty_like(q), torch.empty_like(btd), torch.empty_like(lensd)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        lens_d.copy_(lens_h, non_blocking=True)
+        b2.decode_attn(q_d, kc, vc, bt_d, lens_d, max_ctx, O=O, workspace=ws)
+        o_h.copy_(O, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 500))
+    ms_e2e = time_steps(torch, e2e_step, e2e_steps, args.warmup, dist)
+    torch.cuda.synchronize()
+    e2e_value = bytes_total / (ms_e2e / e2e_steps * 1e-3) / 1e9
+    h2d = q_h.numel() * 4 + bt_h.numel() * 4 + lens_h.numel() * 4
+    d2h = o_h.numel() * 4
+
+    line = {
+        "metric": "decode-attn HBM GB/s (GQA paged decode, BASELINE config 3, fp32 KV)",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, ragged lengths U[512,8192], random block table)",
+        "config": {"workload": "gqa_decode_attn_config3", "batch": B, "h_q": H_Q, "h_kv": H_KV, "head_dim": D,
+                   "block_size": BS, "ctx_lens": "U[512,8192] seed 42", "sum_ctx": int(lens.sum()),
+                   "kv_dtype": "fp32", "parallelism": f"kv-heads x{world}", "l2": "inputs larger than L2 "
+                   f"({bytes_rank / 1e9:.3f} GB per rank per step vs 126 MB L2)", "algorithmic_bytes": bytes_total},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                     "traffic": ncu_traffic("decode_attn_kernel", bytes_rank)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and rank == 0:
+        line["secondary"] = secondary(torch, b2, np, args, kc, vc, q, btd, lensd, lens, bt, P, hbm_peak, bf16_peak)
+        line["cpu_baseline"] = cpu_baseline(torch, q, kc, vc, bt, lens)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def ncu_traffic(kernel, alg_bytes_per_launch):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/ncu_traffic.json: read+write bytes and the algorithmic bytes of the captured
+    launch), scaled to this launch by algorithmic bytes; None when not captured."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)[kernel]
+        return int(j["dram_bytes"] / j["alg_bytes"] * alg_bytes_per_launch)
+    except Exception:
+        return None
+
+
+def secondary(torch, b2, np, args, kc, vc, q, btd, lensd, lens, bt, P, hbm_peak, bf16_peak):
+    out = {}
+    max_ctx = int(lens.max())
+    n = max(3, min(args.steps, 200))
+    # bf16 KV cache, same batch and values rounded to bf16
+    kb, vb = kc.to(torch.bfloat16), vc.to(torch.bfloat16)
+    O = torch.empty_like(q)
+    ws = b2.make_decode_workspace(B, H_Q, H_KV, D, max_ctx, BS)
+    ms = time_steps(torch, lambda: b2.decode_attn(q, kb, vb, btd, lensd, max_ctx, O=O, workspace=ws), n, 3)
+    by = attn_alg_bytes(lens, H_KV, H_Q, D, 2, bt.shape[1])
+    gbs = by / (ms / n * 1e-3) / 1e9
+    out["gqa_config3_bf16_kv"] = {"gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / hbm_peak, 4),
+                                  "us_per_call": round(ms / n * 1e3, 2), "algorithmic_bytes": by}
+    del kb, vb
+    # config 1: MHA B1 H12 d64 ctx1024, 64-block random permutation; 6.3 MB fits in L2, so
+    # 40 independent copies (250 MB) are rotated
+    rng = np.random.default_rng(SEED)
+    copies = 40
+    bt1 = torch.from_numpy(rng.permutation(64).astype(np.int32).reshape(1, 64)).cuda()
+    l1 = torch.tensor([1024], dtype=torch.int32, device="cuda")
+    sets = [(torch.randn(64, 16, 12, 64, device="cuda"), torch.randn(64, 16, 12, 64, device="cuda"),
+             torch.randn(1, 12, 64, device="cuda")) for _ in range(copies)]
+    O1 = torch.empty(1, 12, 64, device="cuda")
+    ws1 = b2.make_decode_workspace(1, 12, 12, 64, 1024, 16)
+    it = [0]
+
+    def step1():
+        k, v, qq = sets[it[0] % copies]
+        it[0] += 1
+        b2.decode_attn(qq, k, v, bt1, l1, 1024, O=O1, workspace=ws1)
+
+    n1 = max(3, min(args.steps * 4, 2000))
+    ms = time_steps(torch, step1, n1, 10)
+    by1 = attn_alg_bytes(np.array([1024]), 12, 12, 64, 4, 64)
+    out["mha_config1"] = {"gbs": round(by1 / (ms / n1 * 1e-3) / 1e9, 1), "us_per_call": round(ms / n1 * 1e3, 2),
+                          "algorithmic_bytes": by1, "l2": "40 rotated copies (250 MB)"}
+    del sets
+    peak_int8 = 2.0 * bf16_peak  # dense int8 rate is twice the bf16 rate on the same tensor cores
+    for (M, N, K) in [(2048, 2048, 2048), (64, 3072, 768), (8192, 8192, 8192)]:
+        out[f"int8_gemm_{M}x{N}x{K}"] = gemm_secondary(torch, b2, M, N, K, args.steps, peak_int8)
+    out["int8_peak_tops"] = peak_int8
+    return out
+
+
+def cpu_baseline(torch, q, kc, vc, bt, lens):
+    """The oracle (C restatement of the reference's CPU attention), 1 thread, on the first
+    4 sequences of the workload, repeated for ~10 s."""
+    from oracle import oracle
+
+    seqs = [0, 1, 2, 3]
+    k, v, sbt, sl = cpu_sample(torch, kc, vc, bt, lens, seqs)
+    qs = q[seqs].cpu().numpy()
+    sec = time_cpu_attention(oracle, qs, k, v, sbt, sl, 1, 10.0)
+    by = attn_alg_bytes(sl, H_KV, H_Q, D, 4, bt.shape[1])
+    return {"value": round(by / sec / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"sequences 0-3 of the workload (ctx {list(map(int, sl))}), all 32 heads, fp32 KV, "
+                      f"{sec * 1e3:.0f} ms per pass"}
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (the oracle's restatement of its
+    CPU attention harness, tests/test_paged_attention.cu:138-179, on all host threads),
+    timed on a bounded sample of the headline workload per step. Rank 0 only."""
+    import numpy as np
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from oracle import oracle
+
+    lens, bt, P = workload_meta()
+    threads = oracle.max_threads()
+    rng = np.random.default_rng(SEED)
+    # size the per-step sample so the whole run stays within ~2 minutes
+    probe = [0]
+    nb0 = (int(lens[0]) + BS - 1) // BS
+    kc = rng.standard_normal((nb0, BS, H_KV, D)).astype(np.float32)
+    vc = rng.standard_normal((nb0, BS, H_KV, D)).astype(np.float32)
+    q = rng.standard_normal((1, H_Q, D)).astype(np.float32)
+    sbt = np.arange(nb0, dtype=np.int32).reshape(1, nb0)
+    t1 = time_cpu_attention(oracle, q, kc, vc, sbt, lens[probe], threads, 0.2)
+    per_seq = t1 * float(lens.mean()) / float(lens[0])
+    nseq = int(max(1, min(B, 120.0 / max(1, args.steps + args.warmup) / per_seq)))
+    seqs = list(range(nseq))
+    sl = lens[seqs]
+    nbs = [(int(l) + BS - 1) // BS for l in sl]
+    Ptot = sum(nbs)
+    kc = rng.standard_normal((Ptot, BS, H_KV, D)).astype(np.float32)
+    vc = rng.standard_normal((Ptot, BS, H_KV, D)).astype(np.float32)
+    q = rng.standard_normal((nseq, H_Q, D)).astype(np.float32)
+    sbt = np.zeros((nseq, max(nbs)), np.int32)
+    off = 0
+    for i, nb in enumerate(nbs):
+        sbt[i, :nb] = rng.permutation(np.arange(off, off + nb))
+        off += nb
+    for _ in range(args.warmup):
+        oracle.decode_attn(q, kc, vc, sbt, sl, nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.decode_attn(q, kc, vc, sbt, sl, nthreads=threads)
+    sec = time.perf_counter() - t0
+    by = attn_alg_bytes(sl, H_KV, H_Q, D, 4, sbt.shape[1])
+    v = by * args.steps / sec / 1e9
+    sample = f"sequences 0-{nseq - 1} of the workload per step (sum ctx {int(sl.sum())}), all heads, fp32 KV"
+    print(json.dumps({
+        "impl": "reference", "metric": "decode-attn HBM GB/s (GQA paged decode, BASELINE config 3, fp32 KV)",
+        "value": round(v, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), ragged lengths U[512,8192])",
+        "config": {"workload": "gqa_decode_attn_config3", "batch": B, "h_q": H_Q, "h_kv": H_KV, "head_dim": D,
+                   "block_size": BS, "kv_dtype": "fp32", "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -74,7 +74,7 @@ extern "C" {
 size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim, int max_context_len, int block_size) {
     if (B <= 0 || H_q <= 0 || H_kv <= 0 || head_dim <= 0 || block_size <= 0 || max_context_len < 0) return 0;
     // sized for the fp32 plan, which never has fewer splits than the bf16 one
-    return decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size, kAbiMaxSplits, 2);
+    return decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size, kAbiMaxSplits, 4);
 }
 
 int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream) {
