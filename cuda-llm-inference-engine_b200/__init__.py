@@ -45,7 +45,7 @@ _CXX = {
 
 # Every symbol include/*.h declares (checked by the CPU tests).
 C_ABI_SYMBOLS = [
-    "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
+    "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_decode_attn_noalloc", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
     "b2_int8_gemm_s32", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
 ]
 
@@ -85,6 +85,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     lib.b2_decode_attn_workspace_size.restype = sz
     lib.b2_decode_attn.argtypes = [ctypes.POINTER(DecodeAttnArgs), vp]
     lib.b2_decode_attn.restype = i
+    lib.b2_decode_attn_noalloc.argtypes = [ctypes.POINTER(DecodeAttnArgs), vp]
+    lib.b2_decode_attn_noalloc.restype = i
     lib.b2_quantize_fp32_to_int8.argtypes = [i, i, vp, vp, vp, vp]
     lib.b2_quantize_fp32_to_int8.restype = i
     lib.b2_int8_gemm.argtypes = [i, i, i, vp, vp, vp, vp, vp, vp, vp, i, vp]
@@ -235,6 +237,27 @@ def decode_attn(Q, k_cache, v_cache, block_table, context_lens, max_context_len,
                        int(P if num_phys_blocks is None else num_phys_blocks), float(scale), _ptr(O),
                        _ptr(workspace), workspace.numel() * workspace.element_size())
     _check(load_library().b2_decode_attn(ctypes.byref(a), _stream(stream)), "b2_decode_attn")
+    return O
+
+
+DECODE_NOALLOC_SCRATCH_BYTES = 16 << 20  # B2_DECODE_NOALLOC_SCRATCH_BYTES
+
+
+def decode_attn_noalloc(Q, k_cache, v_cache, block_table, context_lens, max_context_len, O, scale=0.0,
+                        num_phys_blocks=None, stream=None):
+    """Decode attention through ``b2_decode_attn_noalloc``: the library allocates nothing and
+    uses its fixed per-GPU scratch array instead of a workspace. For callers that cannot
+    allocate device memory; O must be provided. Overlapping calls on one GPU race on the
+    shared scratch, so issue them on one stream (or otherwise serialise them)."""
+    import torch
+
+    B, H_q, d = Q.shape[0], Q.shape[1], Q.shape[-1]
+    P, bs, H_kv, _ = k_cache.shape
+    kvd = B2_KV_BF16 if k_cache.dtype == torch.bfloat16 else B2_KV_F32
+    a = DecodeAttnArgs(B, H_q, H_kv, d, _ptr(Q), _ptr(k_cache), _ptr(v_cache), kvd, _ptr(block_table),
+                       _ptr(context_lens), int(max_context_len), bs, block_table.shape[1],
+                       int(P if num_phys_blocks is None else num_phys_blocks), float(scale), _ptr(O), None, 0)
+    _check(load_library().b2_decode_attn_noalloc(ctypes.byref(a), _stream(stream)), "b2_decode_attn_noalloc")
     return O
 
 

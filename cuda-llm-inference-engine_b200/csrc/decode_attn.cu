@@ -26,6 +26,7 @@
 #include <cuda_bf16.h>
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 namespace b2 {
 
@@ -496,3 +497,45 @@ int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counte
 }
 
 }  // namespace b2
+
+// ------------------------------------------------------------------ allocation-free variant
+// For callers that cannot call cudaMalloc (see b2_decode_attn_noalloc in b2decode.h): the
+// split workspace lives in this fixed device array instead of caller memory. Every GPU that
+// loads the library holds it until the process exits. Host code must not pass the array's
+// name to a kernel — on the host it is only a stand-in symbol — so its device address is
+// looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[B2_DECODE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device (first call per device does
+// the lookup; returns nullptr on failure).
+void* noalloc_scratch_address() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_noalloc_scratch) != cudaSuccess) return nullptr;
+        g_noalloc_addr[dev] = p;
+    }
+    return g_noalloc_addr[dev];
+}
+}  // namespace
+
+extern "C" int b2_decode_attn_noalloc(const b2_decode_attn_args* args, b2_stream_t stream) {
+    if (!args) return B2_ERR_INVALID;
+    void* scratch = noalloc_scratch_address();
+    if (!scratch) return B2_ERR_CUDA;
+    b2_decode_attn_args a = *args;
+    a.workspace = scratch;
+    a.workspace_bytes = B2_DECODE_NOALLOC_SCRATCH_BYTES;
+    // Same split plan as b2_decode_attn. A plan whose workspace exceeds the fixed array is
+    // rejected with B2_ERR_WORKSPACE by the launcher's size check. The arrival counters are
+    // cleared with a stream-ordered memset on every call, since the array keeps whatever
+    // the previous call left in it.
+    return b2::decode_attn_launch(&a, 64, false, static_cast<cudaStream_t>(stream));
+}

@@ -91,6 +91,27 @@ size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim,
  * Replaces run_decode_attn (reference kernels/decode/13_decode_attn.cu:84-109). */
 int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream);
 
+/* Capacity of the fixed device scratch array used by b2_decode_attn_noalloc: 16 MiB per GPU. */
+#define B2_DECODE_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* Decode attention that allocates nothing and needs no caller workspace. No counterpart
+ * in the reference: it exists for callers that cannot call cudaMalloc — code running while
+ * a CUDA graph is being captured by someone else, allocator-restricted plugin hosts, or
+ * real-time loops that forbid allocation after start-up — and that also cannot hand over
+ * a workspace buffer of their own.
+ *   - The caller still passes Q, the caches, the block table, context_lens and O;
+ *     args->workspace and args->workspace_bytes are ignored.
+ *   - The split workspace is a file-scope device array of B2_DECODE_NOALLOC_SCRATCH_BYTES
+ *     held by every GPU that loads the library until the process exits. Shapes whose
+ *     workspace (b2_decode_attn_workspace_size) exceeds it return B2_ERR_WORKSPACE.
+ *   - The first call on each device looks up the array's device address; make that first
+ *     call before any stream capture that should contain this entry point.
+ *   - Every call uses the same array: calls that may overlap on the GPU (different streams,
+ *     or different host threads on one device) race on it and must be serialised by the
+ *     caller. Each call clears the array's arrival counters itself (a stream-ordered memset).
+ *   - Calls no cudaMalloc, cudaFree or allocating library routine. */
+int b2_decode_attn_noalloc(const b2_decode_attn_args* args, b2_stream_t stream);
+
 /* ------------------------------------------------------------------ K14 INT8 */
 
 /* Per-row symmetric fp32 -> int8 quantisation, packed 4 per int32, plus fp32 scales.
