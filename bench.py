@@ -465,16 +465,51 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_only(args):
+    """One workload, W + K launches, no secondary legs (a small, fixed command for ncu)."""
+    import torch
+
+    b2 = importlib.import_module("cuda-llm-inference-engine_b200")
+    b2.load_library()
+    dev = torch.device("cuda", 0)
+    if args.only.startswith("attn"):
+        dt = torch.bfloat16 if args.only == "attn_bf16" else torch.float32
+        lens, bt, P = workload_meta()
+        kc, vc = make_kv_shard(torch, P, 0, H_KV, dt, dev)
+        q = torch.randn(B, H_Q, D, device=dev)
+        O = torch.empty_like(q)
+        btd, lensd = torch.from_numpy(bt).to(dev), torch.from_numpy(lens).to(dev)
+        ws = b2.make_decode_workspace(B, H_Q, H_KV, D, int(lens.max()), BS, device=dev)
+        fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, int(lens.max()), O=O, workspace=ws)  # noqa: E731
+        by = attn_alg_bytes(lens, H_KV, H_Q, D, 2 if dt == torch.bfloat16 else 4, bt.shape[1])
+    else:
+        M, N, K = {"gemm2048": (2048,) * 3, "gemm8192": (8192,) * 3, "gemm_rect": (64, 3072, 768)}[args.only]
+        A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev).view(torch.int32)
+        Bt = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev).view(torch.int32)
+        sA, sB = torch.rand(M, device=dev), torch.rand(N, device=dev)
+        C = torch.empty(M, N, device=dev)
+        fn = lambda: b2.int8_gemm(A, Bt, sA, sB, C=C)  # noqa: E731
+        by = 2 * M * N * K
+    ms = time_steps(torch, fn, args.steps, args.warmup)
+    assert b2.device_error() == 0
+    print(f"{args.only}: {ms / args.steps * 1e3:.2f} us/launch, {by / (ms / args.steps * 1e-3) / 1e9:.1f} "
+          f"{'GB/s' if args.only.startswith('attn') else 'GOP/s'} (not a bench value)", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
+    ap.add_argument("--only", default=None, choices=["attn", "attn_bf16", "gemm2048", "gemm8192", "gemm_rect"],
+                    help="run one workload for a few steps with no JSON line (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

@@ -87,6 +87,22 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                  :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
 }
 
+// 16-byte cp.async global -> shared (L1 bypassed), with an L2 eviction-policy hint.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
+                 :: "r"(dst), "l"(src), "l"(policy) : "memory");
+}
+
+// Arrive on an mbarrier once every cp.async this thread issued so far has landed. The
+// barrier's expected count must include this arrival (no pending-count increment).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -180,6 +196,13 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 }
 
 // ---------------------------------------------------------------- misc
+// 2^x with the hardware approximation (MUFU.EX2, about 2 ulp; ex2(-inf) = +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -13,13 +13,15 @@
 // B200 design (one CTA per (split, kv_head, sequence)):
 //   - the CTA serves all G = H_q/H_kv query heads of its KV head, so every K/V byte is
 //     read from HBM once (the reference re-reads it once per query head);
-//   - warp 8 is a producer: each lane issues a 1-D bulk copy (cp.async.bulk, TMA engine)
-//     of one token's K row and V row into a STAGES-deep shared-memory ring, completion
-//     counted on an mbarrier; the block table is read by the producer only;
-//   - warps 0..7 consume 32-token tiles: split-d partial dot products (no shuffles), an
-//     exp2-domain online softmax per tile, then P.V with each lane owning head_dim/32
-//     output columns; K rows sit 16 B apart from a 128 B multiple so all shared loads
-//     are bank-conflict free;
+//   - warp 8 is a producer: it gathers each tile's K and V rows (tiles of ~32 KB: 32-128
+//     tokens) through the block table with coalesced 16-byte cp.async (one warp
+//     instruction per 512-byte row) into a 64 KB shared-memory ring, completion counted
+//     on a per-stage mbarrier (cp.async.mbarrier.arrive). 1-D bulk copies of single rows
+//     were measured to be request-rate bound here (fp32 and bf16 took equal time);
+//   - warps 0..7 consume: each owns a slice of every tile's tokens and runs its own
+//     exp2-domain online softmax with no CTA barrier inside the loop; the warps' partial
+//     (o, m, l) are merged by log-sum-exp at the end of the split;
+//   - 3 CTAs per SM (ring 64 KB) hide the per-CTA start-up and merge latency;
 //   - the split merge is fused: every CTA of a (sequence, KV head) writes its partial to
 //     the workspace, and the last to arrive (atomic ticket) merges and writes O.
 #include "common.cuh"
@@ -32,7 +34,7 @@ namespace b2 {
 
 constexpr int DA_NW = 8;                 // consumer warps
 constexpr int DA_NT = (DA_NW + 1) * 32;  // + producer warp
-constexpr int DA_T = 32;                 // tokens per tile
+constexpr int DA_MINB = 3;               // CTAs per SM the register budget is sized for (G <= 4)
 
 struct DecodeAttnParams {
     const float* Q;
@@ -49,29 +51,56 @@ struct DecodeAttnParams {
     unsigned int* err;          // device error word
 };
 
+constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
+
 template <int G, int D, typename KV>
 struct DACfg {
     static constexpr int ES = (int)sizeof(KV);
     static constexpr int ROW = D * ES;                 // bytes of one K or V row
-    static constexpr int KROW = ROW + 16;              // skewed K row pitch in shared memory
-    static constexpr int STAGE = DA_T * KROW + DA_T * ROW;
-    static constexpr int STAGES_RAW = (100 * 1024) / STAGE;
+    // tokens per tile: about 32 KB of K+V per tile whatever the element size
+    static constexpr int T = (16384 / ROW) < 32 ? 32 : ((16384 / ROW) > 128 ? 128 : (16384 / ROW));
+    static constexpr int STAGE = 2 * T * ROW;          // K tile then V tile, rows dense
+    static constexpr int STAGES_RAW = (64 * 1024) / STAGE;  // 64 KB ring: 3 CTAs per SM
     static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
-    static constexpr int DS = D / DA_NW;               // dims per warp in the score phase
-    static constexpr int VPL = D / 32;                 // dims per lane in the P.V phase
+    static constexpr int VPL = D / 32;                 // head_dim columns per lane
+    static constexpr int TPW = G >= 8 ? 2 : 4;         // tokens per consumer group (TPW * G <= 16)
+    static constexpr int TW = T / DA_NW;               // tokens of a tile per consumer warp
     // shared-memory carve-up (bytes)
-    static constexpr int OFF_Q = STAGES * STAGE;                         // f32 [G][D]
-    static constexpr int OFF_SC = OFF_Q + G * D * 4;                     // f32 [NW][G][T]
-    static constexpr int OFF_P = OFF_SC + DA_NW * G * DA_T * 4;          // f32 [T][G]
-    static constexpr int OFF_ALPHA = OFF_P + DA_T * G * 4;               // f32 [G]
-    static constexpr int OFF_ML = OFF_ALPHA + 8 * 4;                     // f32 [G][2]
-    static constexpr int OFF_MISC = OFF_ML + 16 * 4;                     // u32 flags
+    static constexpr int OFF_X = STAGES * STAGE;                         // f32 [NW][32] p / alpha exchange
+    static constexpr int OFF_ML = OFF_X + DA_NW * 32 * 4;                // f32 [NW][G][2]
+    static constexpr int OFF_BT = OFF_ML + DA_NW * G * 2 * 4;            // i32 [BT_CAP] block-table slice
+    static constexpr int BT_CAP = 256;
+    static constexpr int OFF_MISC = OFF_BT + BT_CAP * 4;                 // u32 flags
     static constexpr int OFF_BAR = (OFF_MISC + 16 + 7) & ~7;             // u64 full[S], empty[S]
     static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8;
-    static_assert(D % 32 == 0 && DS % 8 == 0, "head_dim must be 64 or 128");
+    static_assert(D % 32 == 0, "head_dim must be 64 or 128");
     static_assert(DA_NW * G * D * 4 <= STAGES * STAGE, "final reduction must fit the ring");
-    static_assert(G <= DA_NW, "group size must not exceed the consumer warp count");
+    static_assert(TW % TPW == 0 && T % 32 == 0, "tile must split evenly over the consumer warps");
 };
+
+// Sum of NV per-lane values across the warp for every index at once: lane l ends with
+// the full sum of value (l >> (5 - log2 NV)). Each halving step trades half the values
+// with the partner lane, so NV sums cost NV - 1 + (5 - log2 NV) shuffles, not 5 * NV.
+template <int NV>
+__device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
+    constexpr int L = ilog2(NV);
+#pragma unroll
+    for (int k = 0; k < L; ++k) {
+        const int h = NV >> (k + 1);
+        const int o = 16 >> k;
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < h; ++i) {
+            const float send = up ? v[i] : v[i + h];
+            const float keep = up ? v[i + h] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int o = 16 >> L; o >= 1; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
 
 // Load N elements of a K/V row from shared memory into fp32 registers.
 template <typename KV, int N>
@@ -114,7 +143,7 @@ __device__ __forceinline__ void load_row(const unsigned char* p, float (&f)[N]) 
 }
 
 template <int G, int D, typename KV>
-__global__ void __launch_bounds__(DA_NT, 2)
+__global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
 decode_attn_kernel(const DecodeAttnParams p) {
     using C = DACfg<G, D, KV>;
     extern __shared__ __align__(1024) unsigned char smem[];
@@ -148,13 +177,8 @@ decode_attn_kernel(const DecodeAttnParams p) {
 
     const int tok_begin = split * p.blocks_per_split * p.block_size;
     const int tok_end = min(ctx, (split + 1) * p.blocks_per_split * p.block_size);
-    const int ntiles = (tok_end - tok_begin + DA_T - 1) / DA_T;
+    const int ntiles = (tok_end - tok_begin + C::T - 1) / C::T;
 
-    float* q_s = reinterpret_cast<float*>(smem + C::OFF_Q);
-    float* sc_s = reinterpret_cast<float*>(smem + C::OFF_SC);
-    float* p_s = reinterpret_cast<float*>(smem + C::OFF_P);
-    float* alpha_s = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
-    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);
     volatile unsigned int* misc = reinterpret_cast<volatile unsigned int*>(smem + C::OFF_MISC);
     const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -163,23 +187,50 @@ decode_attn_kernel(const DecodeAttnParams p) {
 
     if (tid == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(full_bar(s), 1);
+            mbar_init(full_bar(s), 32);  // one cp.async arrival per producer lane
             mbar_init(empty_bar(s), DA_NW);
         }
         misc[0] = 0;  // abort flag
         misc[1] = 0;  // merge ticket
         fence_mbar_init();
     }
-    // q pre-scaled into the exp2 domain
-    const float* Qb = p.Q + ((size_t)b * p.H_q + hq0) * D;
-    for (int i = tid; i < G * D; i += DA_NT) q_s[i] = Qb[i] * p.scale_log2;
     __syncthreads();
 
     if (warp == DA_NW) {
         // ------------------------------------------------------------ producer warp
+        // The split's slice of the block table is staged in shared memory once, so no tile
+        // waits on a dependent global load (long splits fall back to global reads). Lane r
+        // resolves the cache offset of row r of each 32-row chunk; the warp then moves rows
+        // with coalesced 16-byte cp.async, CPR lanes per row, and every lane arrives on the
+        // stage's full barrier once its copies have landed.
+        constexpr int CPR = C::ROW / 16;  // 16-byte chunks per row
+        constexpr int RPI = 32 / CPR;     // rows per warp instruction
+        constexpr int RC = C::T / 32;     // 32-row chunks per tile
         const int* bt = p.block_table + (size_t)b * p.num_blocks_per_seq;
+        const int blk0 = tok_begin / p.block_size;
+        const int nbt = (tok_end - 1) / p.block_size - blk0 + 1;
+        int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT);
+        const bool staged = nbt <= C::BT_CAP;
+        if (staged) {
+            for (int j = lane; j < nbt; j += 32) bt_s[j] = bt[blk0 + j];
+            __syncwarp();
+        }
         const uint64_t pol = policy_evict_first();
-        int issued = 0;
+        auto row_off = [&](int i, int c) -> long long {
+            const int t0 = tok_begin + i * C::T + c * 32;
+            if (lane >= tok_end - t0) return 0;
+            const int pos = t0 + lane;
+            const int blk = pos / p.block_size;
+            const int slot = pos - blk * p.block_size;
+            int phys = staged ? bt_s[blk - blk0] : bt[blk];
+            if (p.num_phys_blocks > 0 && (unsigned)phys >= (unsigned)p.num_phys_blocks) {
+                raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
+                phys = 0;
+            }
+            return ((((long long)phys * p.block_size + slot) * p.H_kv + kvh) * (long long)C::ROW);
+        };
+        const int sub = lane / CPR;
+        const int chunk = (lane % CPR) * 16;
         for (int i = 0; i < ntiles; ++i) {
             const int st = i % C::STAGES;
             if (i >= C::STAGES) {
@@ -188,119 +239,126 @@ decode_attn_kernel(const DecodeAttnParams p) {
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                 if (!ok) { if (lane == 0) misc[0] = 1; break; }
             }
-            const int t0 = tok_begin + i * DA_T;
-            const int n = min(DA_T, tok_end - t0);
-            if (lane == 0) mbar_arrive_expect_tx(full_bar(st), (uint32_t)(n * 2 * C::ROW));
-            __syncwarp();
-            if (lane < n) {
-                const int pos = t0 + lane;
-                const int blk = pos / p.block_size;
-                const int slot = pos - blk * p.block_size;
-                int phys = bt[blk];
-                if (p.num_phys_blocks > 0 && (unsigned)phys >= (unsigned)p.num_phys_blocks) {
-                    raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
-                    phys = 0;
+            const int n = min(C::T, tok_end - (tok_begin + i * C::T));
+            const uint32_t sK = ring + st * C::STAGE;
+            const uint32_t sV = sK + C::T * C::ROW;
+#pragma unroll
+            for (int c = 0; c < RC; ++c) {
+                if (c * 32 >= n) break;
+                const long long cur = row_off(i, c);
+#pragma unroll 4
+                for (int r0 = c * 32; r0 < min(n, c * 32 + 32); r0 += RPI) {
+                    const int r = r0 + sub;
+                    const long long off = __shfl_sync(0xffffffffu, cur, r & 31);
+                    if (r < n) {
+                        cp_async16(sK + r * C::ROW + chunk, p.k_cache + off + chunk, pol);
+                        cp_async16(sV + r * C::ROW + chunk, p.v_cache + off + chunk, pol);
+                    }
                 }
-                const size_t off = (((size_t)phys * p.block_size + slot) * p.H_kv + kvh) * (size_t)C::ROW;
-                const uint32_t sbase = ring + st * C::STAGE;
-                bulk_g2s(sbase + lane * C::KROW, p.k_cache + off, C::ROW, full_bar(st), pol);
-                bulk_g2s(sbase + DA_T * C::KROW + lane * C::ROW, p.v_cache + off, C::ROW, full_bar(st), pol);
             }
-            issued = i + 1;
+            cp_async_mbar_arrive_noinc(full_bar(st));
         }
-        // Drain: if consumers aborted, make sure no copy is still landing in the ring.
-        if (misc[0] != 0 && lane == 0) {
-            for (int i = max(0, issued - C::STAGES); i < issued; ++i)
-                (void)mbar_wait(full_bar(i % C::STAGES), (i / C::STAGES) & 1, p.err);
-        }
+        cp_async_wait_all();  // nothing may still be landing in the ring when the warp exits
         return;
     }
 
     // ---------------------------------------------------------------- consumer warps
+    // Warp w owns tokens [TW w, TW (w+1)) of every tile and keeps its own online softmax
+    // state; lanes span head_dim (VPL columns each), so K/V rows are read as contiguous,
+    // conflict-free shared loads. The TPW x G dot products of a token group are reduced
+    // across the warp with a transposed butterfly (about one shuffle per dot product), p
+    // and alpha are exchanged through warp-private shared memory, and no CTA-wide barrier
+    // is taken inside the tile loop.
     constexpr int NC = DA_NW * 32;
+    constexpr int TPW = C::TPW;            // tokens per group
+    constexpr int NV = TPW * G;            // dot products per group (<= 16)
+    constexpr int SHIFT = 5 - ilog2(NV);   // lane -> (token, head) index: idx = lane >> SHIFT
+    constexpr int LG = ilog2(G);
+    const int idx = lane >> SHIFT;
+    const int my_t = idx / G, my_g = idx % G;
+    const bool owner = (lane & ((1 << SHIFT) - 1)) == 0;
+    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
+
+    float q[G][C::VPL];
+    {
+        const float* Qb = p.Q + ((size_t)b * p.H_q + hq0) * D;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < C::VPL; ++j) q[g][j] = Qb[g * D + lane * C::VPL + j] * p.scale_log2;
+    }
     float acc[G][C::VPL];
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int j = 0; j < C::VPL; ++j) acc[g][j] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;  // meaningful in warp g < G (head g)
+    float m_run = -INFINITY, l_run = 0.f;  // head my_g; l over this lane's token subset
 
     for (int i = 0; i < ntiles; ++i) {
         const int st = i % C::STAGES;
-        const int n = min(DA_T, tok_end - (tok_begin + i * DA_T));
+        const int n = min(C::T, tok_end - (tok_begin + i * C::T));
         if (misc[0] == 0) {
             if (!mbar_wait(full_bar(st), (i / C::STAGES) & 1, p.err)) misc[0] = 1;
         }
         const unsigned char* Kt = smem + st * C::STAGE;
-        const unsigned char* Vt = Kt + DA_T * C::KROW;
-
-        // Phase A: partial scores over this warp's slice of head_dim. Thread = token.
-        {
-            const int t = lane;
-            float part[G];
+        const unsigned char* Vt = Kt + C::T * C::ROW;
 #pragma unroll
-            for (int g = 0; g < G; ++g) part[g] = 0.f;
-            if (t < n) {
-                float kf[C::DS];
-                load_row<KV, C::DS>(Kt + t * C::KROW + warp * C::DS * C::ES, kf);
+        for (int grp = 0; grp < C::TW / TPW; ++grp) {
+            const int tok0 = warp * C::TW + grp * TPW;
+            if (tok0 >= n) break;  // warp-uniform
+            float s[NV];
+#pragma unroll
+            for (int t = 0; t < TPW; ++t) {
+                float kf[C::VPL];
+                if (tok0 + t < n) {
+                    load_row<KV, C::VPL>(Kt + (tok0 + t) * C::ROW + lane * C::VPL * C::ES, kf);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < C::VPL; ++j) kf[j] = 0.f;
+                }
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float4* q4 = reinterpret_cast<const float4*>(q_s + g * D + warp * C::DS);
+                    float a = 0.f;
 #pragma unroll
-                    for (int j = 0; j < C::DS / 4; ++j) {
-                        const float4 q = q4[j];
-                        part[g] = fmaf(q.x, kf[4 * j], part[g]);
-                        part[g] = fmaf(q.y, kf[4 * j + 1], part[g]);
-                        part[g] = fmaf(q.z, kf[4 * j + 2], part[g]);
-                        part[g] = fmaf(q.w, kf[4 * j + 3], part[g]);
-                    }
+                    for (int j = 0; j < C::VPL; ++j) a = fmaf(q[g][j], kf[j], a);
+                    s[t * G + g] = a;
                 }
             }
+            float sc = warp_transpose_sum<NV>(s, lane);
+            if (tok0 + my_t >= n) sc = -INFINITY;
+            float tmax = sc;
 #pragma unroll
-            for (int g = 0; g < G; ++g) sc_s[(warp * G + g) * DA_T + t] = part[g];
-        }
-        named_barrier(1, NC);
-
-        // Phase B: online softmax for head g = warp (exp2 domain). Lane = token.
-        if (warp < G) {
-            const int g = warp;
-            float s = -INFINITY;
-            if (lane < n) {
-                s = 0.f;
-#pragma unroll
-                for (int w = 0; w < DA_NW; ++w) s += sc_s[(w * G + g) * DA_T + lane];
-            }
-            const float m_new = fmaxf(m_run, warp_max(s));
-            const float alpha = exp2f(m_run - m_new);  // m_run = -inf on the first tile -> 0
-            const float pr = (lane < n) ? exp2f(s - m_new) : 0.f;
-            l_run = l_run * alpha + warp_sum(pr);
+            for (int k = 0; k < ilog2(TPW); ++k)
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1 << (SHIFT + LG + k)));
+            const float m_new = fmaxf(m_run, tmax);
+            const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
+            const float pr = sc == -INFINITY ? 0.f : fast_exp2(sc - m_new);
+            l_run = fmaf(l_run, alpha, pr);
             m_run = m_new;
-            p_s[lane * G + g] = pr;
-            if (lane == 0) alpha_s[g] = alpha;
-        }
-        named_barrier(1, NC);
-
-        // Phase C: acc = acc * alpha + P.V. Warp = token subset, lane = head_dim columns.
-        {
-            float al[G];
+            if (owner) {
+                xw[idx] = pr;
+                if (my_t == 0) xw[16 + my_g] = alpha;
+            }
+            __syncwarp();
+            float al[G], pv[NV];
 #pragma unroll
-            for (int g = 0; g < G; ++g) al[g] = alpha_s[g];
+            for (int g = 0; g < G; ++g) al[g] = xw[16 + g];
+#pragma unroll
+            for (int k = 0; k < NV; ++k) pv[k] = xw[k];
+            __syncwarp();
 #pragma unroll
             for (int g = 0; g < G; ++g)
 #pragma unroll
                 for (int j = 0; j < C::VPL; ++j) acc[g][j] *= al[g];
 #pragma unroll
-            for (int k = 0; k < DA_T / DA_NW; ++k) {
-                const int t = warp + k * DA_NW;
-                if (t < n) {
+            for (int t = 0; t < TPW; ++t) {
+                if (tok0 + t < n) {
                     float vf[C::VPL];
-                    load_row<KV, C::VPL>(Vt + t * C::ROW + lane * C::VPL * C::ES, vf);
+                    load_row<KV, C::VPL>(Vt + (tok0 + t) * C::ROW + lane * C::VPL * C::ES, vf);
 #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const float pg = p_s[t * G + g];
+                    for (int g = 0; g < G; ++g)
 #pragma unroll
-                        for (int j = 0; j < C::VPL; ++j) acc[g][j] = fmaf(pg, vf[j], acc[g][j]);
-                    }
+                        for (int j = 0; j < C::VPL; ++j) acc[g][j] = fmaf(pv[t * G + g], vf[j], acc[g][j]);
                 }
             }
         }
@@ -308,28 +366,48 @@ decode_attn_kernel(const DecodeAttnParams p) {
         if (lane == 0) mbar_arrive(empty_bar(st));
     }
 
-    // ---- combine the 8 warps' accumulators (same running max, so a plain sum)
+    // ---- per-warp totals: l summed over the lanes holding this head's tokens
+    float l_tot = owner ? l_run : 0.f;
+#pragma unroll
+    for (int k = 0; k < ilog2(TPW); ++k) l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 1 << (SHIFT + LG + k));
     named_barrier(1, NC);  // every warp is done reading the ring
     float* red = reinterpret_cast<float*>(smem);  // [NW][G][D], reuses the ring
+    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);  // [NW][G][2]
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int j = 0; j < C::VPL; ++j) red[(warp * G + g) * D + lane * C::VPL + j] = acc[g][j];
-    if (warp < G && lane == 0) {
-        ml_s[2 * warp] = m_run;
-        ml_s[2 * warp + 1] = l_run;
+    if (owner && my_t == 0) {
+        ml_s[(warp * G + my_g) * 2] = m_run;
+        ml_s[(warp * G + my_g) * 2 + 1] = l_tot;
     }
     named_barrier(1, NC);
     if (misc[0] != 0) return;  // a wait gave up: the error bit is set, O is left untouched
 
+    // Log-sum-exp merge of the 8 warps for element i = g*D + d -> (o, M, L).
+    auto merge_warps = [&](int i, float& o, float& M, float& L) {
+        const int g = i / D;
+        M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < DA_NW; ++w) M = fmaxf(M, ml_s[(w * G + g) * 2]);
+        o = 0.f;
+        L = 0.f;
+        if (M == -INFINITY) return;
+#pragma unroll
+        for (int w = 0; w < DA_NW; ++w) {
+            const float mw = ml_s[(w * G + g) * 2];
+            if (mw == -INFINITY) continue;
+            const float sc = fast_exp2(mw - M);
+            o = fmaf(red[w * G * D + i], sc, o);
+            L = fmaf(ml_s[(w * G + g) * 2 + 1], sc, L);
+        }
+    };
+
     if (nsplit == 1) {
         for (int i = tid; i < G * D; i += NC) {
-            const int g = i / D;
-            float o = 0.f;
-#pragma unroll
-            for (int w = 0; w < DA_NW; ++w) o += red[w * G * D + i];
-            const float l = ml_s[2 * g + 1];
-            O[i] = l > 0.f ? o / l : 0.f;
+            float o, M, L;
+            merge_warps(i, o, M, L);
+            O[i] = L > 0.f ? o / L : 0.f;
         }
         return;
     }
@@ -338,12 +416,11 @@ decode_attn_kernel(const DecodeAttnParams p) {
     const size_t rowlen = D + 2;
     for (int i = tid; i < G * D; i += NC) {
         const int g = i / D, d = i - g * D;
-        float o = 0.f;
-#pragma unroll
-        for (int w = 0; w < DA_NW; ++w) o += red[w * G * D + i];
+        float o, M, L;
+        merge_warps(i, o, M, L);
         float* ws = p.ws_partial + (((size_t)b * p.H_q + hq0 + g) * p.num_splits + split) * rowlen;
         ws[d] = o;
-        if (d == 0) { ws[D] = ml_s[2 * g]; ws[D + 1] = ml_s[2 * g + 1]; }
+        if (d == 0) { ws[D] = M; ws[D + 1] = L; }
     }
     __threadfence();
     named_barrier(1, NC);
@@ -359,7 +436,7 @@ decode_attn_kernel(const DecodeAttnParams p) {
         for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(ws + s * rowlen + D));
         float L = 0.f, o = 0.f;
         for (int s = 0; s < nsplit; ++s) {
-            const float w = exp2f(__ldcg(ws + s * rowlen + D) - M);
+            const float w = fast_exp2(__ldcg(ws + s * rowlen + D) - M);
             L = fmaf(__ldcg(ws + s * rowlen + D + 1), w, L);
             o = fmaf(__ldcg(ws + s * rowlen + d), w, o);
         }
@@ -426,7 +503,6 @@ static size_t partial_bytes(int B, int H_q, int D, int S) {
     return (b + 255) & ~(size_t)255;
 }
 
-constexpr int DA_MAX_SPLITS_ABI = 64;
 
 size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size,
                                   int max_splits, int kv_bytes) {
