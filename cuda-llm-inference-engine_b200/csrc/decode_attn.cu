@@ -63,8 +63,9 @@ struct DACfg {
     static constexpr int STAGES_RAW = (64 * 1024) / STAGE;  // 64 KB ring: 3 CTAs per SM
     static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
     static constexpr int VPL = D / 32;                 // head_dim columns per lane
-    static constexpr int TPW = G >= 8 ? 2 : 4;         // tokens per consumer group (TPW * G <= 16)
     static constexpr int TW = T / DA_NW;               // tokens of a tile per consumer warp
+    // tokens per consumer group: as many as keep TPW * G <= 16 dot products per reduction
+    static constexpr int TPW = (16 / G) < TW ? (16 / G) : TW;
     // shared-memory carve-up (bytes)
     static constexpr int OFF_X = STAGES * STAGE;                         // f32 [NW][32] p / alpha exchange
     static constexpr int OFF_ML = OFF_X + DA_NW * 32 * 4;                // f32 [NW][G][2]
@@ -279,19 +280,23 @@ decode_attn_kernel(const DecodeAttnParams p) {
     const bool owner = (lane & ((1 << SHIFT) - 1)) == 0;
     float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
 
-    float q[G][C::VPL];
+    // q and the output accumulator are held as fp32 pairs for the packed f32x2 FMA
+    constexpr int VP = C::VPL / 2;
+    float2 q[G][VP];
     {
         const float* Qb = p.Q + ((size_t)b * p.H_q + hq0) * D;
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int j = 0; j < C::VPL; ++j) q[g][j] = Qb[g * D + lane * C::VPL + j] * p.scale_log2;
+            for (int j = 0; j < VP; ++j)
+                q[g][j] = make_float2(Qb[g * D + lane * C::VPL + 2 * j] * p.scale_log2,
+                                      Qb[g * D + lane * C::VPL + 2 * j + 1] * p.scale_log2);
     }
-    float acc[G][C::VPL];
+    float2 acc[G][VP];
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int j = 0; j < C::VPL; ++j) acc[g][j] = 0.f;
+        for (int j = 0; j < VP; ++j) acc[g][j] = make_float2(0.f, 0.f);
     float m_run = -INFINITY, l_run = 0.f;  // head my_g; l over this lane's token subset
 
     for (int i = 0; i < ntiles; ++i) {
@@ -318,10 +323,10 @@ decode_attn_kernel(const DecodeAttnParams p) {
                 }
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    float a = 0.f;
+                    float2 a = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int j = 0; j < C::VPL; ++j) a = fmaf(q[g][j], kf[j], a);
-                    s[t * G + g] = a;
+                    for (int j = 0; j < VP; ++j) a = ffma2(q[g][j], make_float2(kf[2 * j], kf[2 * j + 1]), a);
+                    s[t * G + g] = a.x + a.y;
                 }
             }
             float sc = warp_transpose_sum<NV>(s, lane);
@@ -349,16 +354,19 @@ decode_attn_kernel(const DecodeAttnParams p) {
 #pragma unroll
             for (int g = 0; g < G; ++g)
 #pragma unroll
-                for (int j = 0; j < C::VPL; ++j) acc[g][j] *= al[g];
+                for (int j = 0; j < VP; ++j) acc[g][j] = fmul2(acc[g][j], make_float2(al[g], al[g]));
 #pragma unroll
             for (int t = 0; t < TPW; ++t) {
                 if (tok0 + t < n) {
                     float vf[C::VPL];
                     load_row<KV, C::VPL>(Vt + (tok0 + t) * C::ROW + lane * C::VPL * C::ES, vf);
 #pragma unroll
-                    for (int g = 0; g < G; ++g)
+                    for (int g = 0; g < G; ++g) {
+                        const float2 pp = make_float2(pv[t * G + g], pv[t * G + g]);
 #pragma unroll
-                        for (int j = 0; j < C::VPL; ++j) acc[g][j] = fmaf(pv[t * G + g], vf[j], acc[g][j]);
+                        for (int j = 0; j < VP; ++j)
+                            acc[g][j] = ffma2(pp, make_float2(vf[2 * j], vf[2 * j + 1]), acc[g][j]);
+                    }
                 }
             }
         }
@@ -376,7 +384,10 @@ decode_attn_kernel(const DecodeAttnParams p) {
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int j = 0; j < C::VPL; ++j) red[(warp * G + g) * D + lane * C::VPL + j] = acc[g][j];
+        for (int j = 0; j < VP; ++j) {
+            red[(warp * G + g) * D + lane * C::VPL + 2 * j] = acc[g][j].x;
+            red[(warp * G + g) * D + lane * C::VPL + 2 * j + 1] = acc[g][j].y;
+        }
     if (owner && my_t == 0) {
         ml_s[(warp * G + my_g) * 2] = m_run;
         ml_s[(warp * G + my_g) * 2 + 1] = l_tot;
