@@ -9,7 +9,7 @@
 // The reference's nvcc build contracts `v * sB + bias` into one fused multiply-add; the
 // epilogue below spells the same operations out (fmaf) so results are bit-identical.
 //
-// B200 design of the GEMM (one 128 x BN output tile per CTA, 192 threads):
+// B200 design of the GEMM (persistent, one CTA per SM, 128 x BN output tiles, 192 threads):
 //   warp 0  : TMA producer — 2-D tensor-map loads of 128 x 128-byte A and BN x 128-byte B
 //             tiles in the 128-byte swizzle into a STAGES-deep ring (mbarrier full/empty);
 //   warp 1  : allocates BN TMEM columns and issues tcgen05.mma.cta_group::1.kind::i8
@@ -17,9 +17,13 @@
 //             ring slots with tcgen05.commit;
 //   warps 2-5: epilogue — tcgen05.ld of the accumulator (one TMEM lane quadrant per warp,
 //             thread = output row), dequantise + bias / GELU / residual in registers, store.
+//   Two TMEM accumulators (2 x BN columns) let the epilogue of tile j overlap the MMAs of
+//   tile j+1; tiles are visited in groups of 8 row-tiles so concurrently running CTAs
+//   share A and B tiles in L2.
 #include "common.cuh"
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 namespace b2 {
 
@@ -124,10 +128,78 @@ struct GemmCfg {
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int STAGES = std::min(8, (196 * 1024) / STAGE);
     static constexpr int OFF_BAR = STAGES * STAGE;
-    static constexpr int SMEM = OFF_BAR + (2 * STAGES + 2) * 8 + 16 + 1024;  // + 1 KB for alignment
-    static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+    // full[S], empty[S], acc_full[2], acc_empty[2]
+    static constexpr int NBAR = 2 * STAGES + 4;
+    static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + 1 KB for alignment
+    static constexpr uint32_t ACC_COLS = BN < 32 ? 32 : BN;      // one accumulator
+    static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;          // double-buffered
 };
 
+constexpr int GM_GROUP_M = 8;  // tile rasterisation: 8 row-tiles share each sweep over N
+
+// Tile index -> (m-tile, n-tile), grouped so CTAs running together reuse A and B in L2.
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+    const int per_group = GM_GROUP_M * n_tiles;
+    const int group = t / per_group;
+    const int first_m = group * GM_GROUP_M;
+    const int gsize = min(m_tiles - first_m, GM_GROUP_M);
+    const int r = t - group * per_group;
+    mt = first_m + r % gsize;
+    nt = r / gsize;
+}
+
+// Dequantise + epilogue for 16 consecutive columns [n, n+16) of one row, then store.
+template <int EPI, bool S32>
+__device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n, float sa, const GemmParams& p) {
+    if constexpr (S32) {
+        int32_t* Crow = static_cast<int32_t*>(p.C) + (size_t)row * p.N;
+        if (n + 16 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<int4*>(Crow + n + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (n + j < p.N) Crow[n + j] = (int32_t)r[j];
+        }
+    } else {
+        float* Crow = static_cast<float*>(p.C) + (size_t)row * p.N;
+        const float* Rrow = (EPI == B2_EPI_BIAS_RESIDUAL) ? p.residual + (size_t)row * p.N : nullptr;
+        if (n + 16 <= p.N && (p.N & 3) == 0) {
+            float rs[16];
+            if constexpr (EPI == B2_EPI_BIAS_RESIDUAL) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4) {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(Rrow + n + j));
+                    rs[j] = t.x; rs[j + 1] = t.y; rs[j + 2] = t.z; rs[j + 3] = t.w;
+                }
+            }
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float sb = __ldg(p.scale_B + n + j);
+                const float bi = (EPI != B2_EPI_PLAIN) ? __ldg(p.bias + n + j) : 0.f;
+                v[j] = epilogue<EPI>((int32_t)r[j], sa, sb, bi, EPI == B2_EPI_BIAS_RESIDUAL ? rs[j] : 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(Crow + n + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                if (n + j < p.N) {
+                    const float bi = (EPI != B2_EPI_PLAIN) ? p.bias[n + j] : 0.f;
+                    const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? Rrow[n + j] : 0.f;
+                    Crow[n + j] = epilogue<EPI>((int32_t)r[j], sa, p.scale_B[n + j], bi, rs);
+                }
+            }
+        }
+    }
+}
+
+// Persistent: CTA c processes tiles c, c + gridDim.x, ... The TMA ring runs continuously
+// across tiles, and two TMEM accumulators let the epilogue of one tile overlap the MMAs
+// of the next.
 template <int BN, int EPI, bool S32>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -141,15 +213,17 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     const uint32_t bar0 = sbase + C::OFF_BAR;
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
-    const uint32_t accum_bar = bar0 + 8u * (2 * C::STAGES);
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_BAR + (2 * C::STAGES + 2) * 8);
+    auto accf_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
+    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_BAR + C::NBAR * 8);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * GM_BM;
-    const int n0 = blockIdx.x * BN;
     const int nk = (p.K + GM_BK - 1) / GM_BK;
+    const int m_tiles = (p.M + GM_BM - 1) / GM_BM;
+    const int n_tiles = (p.N + BN - 1) / BN;
+    const int num_tiles = m_tiles * n_tiles;
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&mapA);
@@ -158,7 +232,10 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
-        mbar_init(accum_bar, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(accf_bar(a), 1);   // tcgen05.commit of the tile's last MMA
+            mbar_init(acce_bar(a), 4);   // one arrival per epilogue warp
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -175,16 +252,24 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         if (lane == 0) {
             // ---------------------------------------------------------------- TMA producer
             const uint64_t pol = policy_evict_last();
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % C::STAGES;
-                if (kb >= C::STAGES) {
-                    if (*abort_flag || !mbar_wait(empty_bar(s), ((kb / C::STAGES) - 1) & 1, p.err)) { *abort_flag = 1; break; }
+            int it = 0;  // k-block counter across all tiles of this CTA
+            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+                int mt, nt;
+                tile_coords(t, m_tiles, n_tiles, mt, nt);
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    if (it >= C::STAGES) {
+                        if (*abort_flag || !mbar_wait(empty_bar(s), ((it / C::STAGES) - 1) & 1, p.err)) {
+                            *abort_flag = 1;
+                            break;
+                        }
+                    }
+                    const uint32_t a_s = sbase + s * C::STAGE;
+                    const uint32_t b_s = a_s + C::A_BYTES;
+                    mbar_arrive_expect_tx(full_bar(s), C::STAGE);
+                    tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
+                    tma_load_2d(b_s, &mapB, kb * GM_BK, nt * BN, full_bar(s), pol);
                 }
-                const uint32_t a_s = sbase + s * C::STAGE;
-                const uint32_t b_s = a_s + C::A_BYTES;
-                mbar_arrive_expect_tx(full_bar(s), C::STAGE);
-                tma_load_2d(a_s, &mapA, kb * GM_BK, m0, full_bar(s), pol);
-                tma_load_2d(b_s, &mapB, kb * GM_BK, n0, full_bar(s), pol);
             }
         }
         __syncwarp();
@@ -192,79 +277,59 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         if (lane == 0) {
             // ---------------------------------------------------------------- MMA issuer
             constexpr uint32_t idesc = idesc_i8(GM_BM, BN);
-            bool ok = true;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % C::STAGES;
-                if (*abort_flag || !mbar_wait(full_bar(s), (kb / C::STAGES) & 1, p.err)) { ok = false; *abort_flag = 1; break; }
+            int it = 0, j = 0;  // k-block counter, local tile counter
+            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++j) {
+                const int a = j & 1, u = j >> 1;
+                if (u >= 1 && !mbar_wait(acce_bar(a), (u - 1) & 1, p.err)) { *abort_flag = 1; break; }
                 tc_fence_after();
-                const uint32_t a_s = sbase + s * C::STAGE;
-                const uint32_t b_s = a_s + C::A_BYTES;
-                const uint64_t da = smem_desc_sw128(a_s);
-                const uint64_t db = smem_desc_sw128(b_s);
+                const uint32_t d_tmem = tmem + a * C::ACC_COLS;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    if (*abort_flag || !mbar_wait(full_bar(s), (it / C::STAGES) & 1, p.err)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_s = sbase + s * C::STAGE;
+                    const uint32_t b_s = a_s + C::A_BYTES;
+                    const uint64_t da = smem_desc_sw128(a_s);
+                    const uint64_t db = smem_desc_sw128(b_s);
 #pragma unroll
-                for (int k = 0; k < GM_BK / 32; ++k) {
-                    // advance 32 bytes of K inside the swizzle atom: +2 in the 16-byte address field
-                    mma_i8(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < GM_BK / 32; ++k) {
+                        // advance 32 bytes of K inside the swizzle atom: +2 in the 16-byte address field
+                        mma_i8(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(empty_bar(s));  // ring slot free once these MMAs have read it
                 }
-                mma_commit(empty_bar(s));
+                mma_commit(accf_bar(a));  // accumulator a complete
             }
-            (void)ok;
-            mma_commit(accum_bar);  // fires once every MMA issued above has completed
         }
         __syncwarp();
     } else {
         // -------------------------------------------------------------------- epilogue
         const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-        const bool ok = mbar_wait(accum_bar, 0, p.err) && *abort_flag == 0;
-        tc_fence_after();
-        const int row = m0 + quad * 32 + lane;
-        const bool row_ok = ok && row < p.M;
-        const float sa = row_ok ? p.scale_A[row] : 0.f;
+        int j = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
+            const int a = j & 1, u = j >> 1;
+            if (*abort_flag || !mbar_wait(accf_bar(a), u & 1, p.err)) { *abort_flag = 1; break; }
+            tc_fence_after();
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, mt, nt);
+            const int row = mt * GM_BM + quad * 32 + lane;
+            const bool row_ok = row < p.M;
+            const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
+            const uint32_t tbase = tmem + a * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
-        for (int c = 0; c < BN / 16; ++c) {
-            uint32_t r[16];
-            tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), r);
-            tmem_ld_wait();
-            const int n = n0 + c * 16;
-            if (!row_ok || n >= p.N) continue;
-            if constexpr (S32) {
-                int32_t* Crow = static_cast<int32_t*>(p.C) + (size_t)row * p.N;
-                if (n + 16 <= p.N && (p.N & 3) == 0) {
-#pragma unroll
-                    for (int j = 0; j < 16; j += 4)
-                        *reinterpret_cast<int4*>(Crow + n + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-                } else {
-                    for (int j = 0; j < 16 && n + j < p.N; ++j) Crow[n + j] = (int32_t)r[j];
-                }
-            } else {
-                float* Crow = static_cast<float*>(p.C) + (size_t)row * p.N;
-                const float* Rrow = (EPI == B2_EPI_BIAS_RESIDUAL) ? p.residual + (size_t)row * p.N : nullptr;
-                float v[16];
-                if (n + 16 <= p.N) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float sb = __ldg(p.scale_B + n + j);
-                        const float bi = (EPI != B2_EPI_PLAIN) ? __ldg(p.bias + n + j) : 0.f;
-                        const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? Rrow[n + j] : 0.f;
-                        v[j] = epilogue<EPI>((int32_t)r[j], sa, sb, bi, rs);
-                    }
-                    if ((p.N & 3) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 16; j += 4)
-                            *reinterpret_cast<float4*>(Crow + n + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) Crow[n + j] = v[j];
-                    }
-                } else {
-                    for (int j = 0; j < 16 && n + j < p.N; ++j) {
-                        const float sb = p.scale_B[n + j];
-                        const float bi = (EPI != B2_EPI_PLAIN) ? p.bias[n + j] : 0.f;
-                        const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? Rrow[n + j] : 0.f;
-                        Crow[n + j] = epilogue<EPI>((int32_t)r[j], sa, sb, bi, rs);
-                    }
-                }
+            for (int c = 0; c < BN / 16; ++c) {
+                uint32_t r[16];
+                tmem_ld16(tbase + (uint32_t)(c * 16), r);
+                tmem_ld_wait();
+                const int n = nt * BN + c * 16;
+                if (row_ok && n < p.N) store16<EPI, S32>(r, row, n, sa, p);
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
         }
     }
 
@@ -316,7 +381,7 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // int8 row-major [rows, K] operand, box = box_rows x 128 bytes, 128-byte swizzle.
-static bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+static bool encode_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
@@ -329,6 +394,31 @@ static bool make_map(CUtensorMap* map, const void* base, int rows, int K, int bo
     return r == CUDA_SUCCESS;
 }
 
+// Small cache of encoded tensor maps (decode loops call the same weights every step).
+static bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    struct Entry { int dev; const void* base; int rows, K, box; CUtensorMap map; };
+    constexpr int kEntries = 64;
+    static Entry cache[kEntries];
+    static int fill = 0, next = 0;
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < fill; ++i) {
+        const Entry& e = cache[i];
+        if (e.dev == dev && e.base == base && e.rows == rows && e.K == K && e.box == box_rows) {
+            *map = e.map;
+            return true;
+        }
+    }
+    if (!encode_map(map, base, rows, K, box_rows)) return false;
+    Entry& e = cache[next];
+    e = Entry{dev, base, rows, K, box_rows, *map};
+    next = (next + 1) % kEntries;
+    if (fill < kEntries) ++fill;
+    return true;
+}
+
 int num_sms_current_device();
 bool set_smem_attr_once(const void* func, int bytes, int slot);
 
@@ -339,7 +429,8 @@ static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, c
     if (!make_map(&ma, A, p.M, p.K, GM_BM) || !make_map(&mb, BT, p.N, p.K, BN)) return B2_ERR_CUDA;
     auto kfn = int8_gemm_tc_kernel<BN, EPI, S32>;
     if (!set_smem_attr_once((const void*)kfn, C::SMEM, slot)) return B2_ERR_CUDA;
-    dim3 grid((p.N + BN - 1) / BN, (p.M + GM_BM - 1) / GM_BM);
+    const int tiles = ((p.N + BN - 1) / BN) * ((p.M + GM_BM - 1) / GM_BM);
+    const int grid = std::min(tiles, num_sms_current_device());
     kfn<<<grid, GM_THREADS, C::SMEM, st>>>(ma, mb, p);
     return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
