@@ -130,7 +130,8 @@ struct GemmCfg {
     static constexpr int OFF_BAR = STAGES * STAGE;
     // full[S], empty[S], acc_full[2], acc_empty[2]
     static constexpr int NBAR = 2 * STAGES + 4;
-    static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + 1 KB for alignment
+    static constexpr int OFF_COL = OFF_BAR + NBAR * 8 + 16;      // f32 [2][BN]: scale_B, bias of the tile
+    static constexpr int SMEM = OFF_COL + 2 * BN * 4 + 1024;     // + 1 KB for alignment
     static constexpr uint32_t ACC_COLS = BN < 32 ? 32 : BN;      // one accumulator
     static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;          // double-buffered
 };
@@ -149,8 +150,11 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 }
 
 // Dequantise + epilogue for 16 consecutive columns [n, n+16) of one row, then store.
+// sBs / bis point at the tile's column scales / biases staged in shared memory (index
+// relative to n); rs holds the residual values when EPI needs them.
 template <int EPI, bool S32>
-__device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n, float sa, const GemmParams& p) {
+__device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n, float sa, const float* sBs,
+                                        const float* bis, const float (&rs)[16], const GemmParams& p) {
     if constexpr (S32) {
         int32_t* Crow = static_cast<int32_t*>(p.C) + (size_t)row * p.N;
         if (n + 16 <= p.N && (p.N & 3) == 0) {
@@ -164,36 +168,34 @@ __device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n,
         }
     } else {
         float* Crow = static_cast<float*>(p.C) + (size_t)row * p.N;
-        const float* Rrow = (EPI == B2_EPI_BIAS_RESIDUAL) ? p.residual + (size_t)row * p.N : nullptr;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            v[j] = epilogue<EPI>((int32_t)r[j], sa, sBs[j], EPI != B2_EPI_PLAIN ? bis[j] : 0.f, rs[j]);
         if (n + 16 <= p.N && (p.N & 3) == 0) {
-            float rs[16];
-            if constexpr (EPI == B2_EPI_BIAS_RESIDUAL) {
-#pragma unroll
-                for (int j = 0; j < 16; j += 4) {
-                    const float4 t = __ldg(reinterpret_cast<const float4*>(Rrow + n + j));
-                    rs[j] = t.x; rs[j + 1] = t.y; rs[j + 2] = t.z; rs[j + 3] = t.w;
-                }
-            }
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float sb = __ldg(p.scale_B + n + j);
-                const float bi = (EPI != B2_EPI_PLAIN) ? __ldg(p.bias + n + j) : 0.f;
-                v[j] = epilogue<EPI>((int32_t)r[j], sa, sb, bi, EPI == B2_EPI_BIAS_RESIDUAL ? rs[j] : 0.f);
-            }
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
                 *reinterpret_cast<float4*>(Crow + n + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                if (n + j < p.N) {
-                    const float bi = (EPI != B2_EPI_PLAIN) ? p.bias[n + j] : 0.f;
-                    const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? Rrow[n + j] : 0.f;
-                    Crow[n + j] = epilogue<EPI>((int32_t)r[j], sa, p.scale_B[n + j], bi, rs);
-                }
-            }
+            for (int j = 0; j < 16; ++j)
+                if (n + j < p.N) Crow[n + j] = v[j];
         }
+    }
+}
+
+// Residual values [n, n+16) of one row (zeros past N).
+__device__ __forceinline__ void load_res16(const GemmParams& p, int row, int n, float (&rs)[16]) {
+    const float* R = p.residual + (size_t)row * p.N + n;
+    if (n + 16 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(R + j));
+            rs[j] = t.x; rs[j + 1] = t.y; rs[j + 2] = t.z; rs[j + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) rs[j] = (n + j < p.N) ? R[j] : 0.f;
     }
 }
 
@@ -308,28 +310,53 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     } else {
         // -------------------------------------------------------------------- epilogue
         const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int et = threadIdx.x - 64;  // 0..127 across the epilogue warps
+        float* sB_s = reinterpret_cast<float*>(smem + C::OFF_COL);
+        float* bias_s = sB_s + BN;
         int j = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
             const int a = j & 1, u = j >> 1;
-            if (*abort_flag || !mbar_wait(accf_bar(a), u & 1, p.err)) { *abort_flag = 1; break; }
-            tc_fence_after();
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, mt, nt);
+            // stage this tile's column scales and biases while the MMAs run
+            if constexpr (!S32) {
+                for (int c = et; c < BN; c += 128) {
+                    const int n = nt * BN + c;
+                    sB_s[c] = n < p.N ? __ldg(p.scale_B + n) : 0.f;
+                    if (EPI != B2_EPI_PLAIN) bias_s[c] = n < p.N ? __ldg(p.bias + n) : 0.f;
+                }
+            }
+            named_barrier(2, 128);
+            // after a timed-out wait the warps keep taking the named barriers but do no work
+            const bool ok = !*abort_flag && mbar_wait(accf_bar(a), u & 1, p.err);
+            if (!ok) *abort_flag = 1;
+            tc_fence_after();
             const int row = mt * GM_BM + quad * 32 + lane;
-            const bool row_ok = row < p.M;
+            const bool row_ok = ok && row < p.M;
             const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
             const uint32_t tbase = tmem + a * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
-            for (int c = 0; c < BN / 16; ++c) {
-                uint32_t r[16];
-                tmem_ld16(tbase + (uint32_t)(c * 16), r);
-                tmem_ld_wait();
+            for (int c = 0; c < BN / 16; c += 2) {
                 const int n = nt * BN + c * 16;
-                if (row_ok && n < p.N) store16<EPI, S32>(r, row, n, sa, p);
+                float rs0[16], rs1[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { rs0[i] = 0.f; rs1[i] = 0.f; }
+                if constexpr (EPI == B2_EPI_BIAS_RESIDUAL && !S32) {
+                    if (row_ok && n < p.N) load_res16(p, row, n, rs0);
+                    if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
+                }
+                uint32_t r0[16], r1[16];
+                tmem_ld16(tbase + (uint32_t)(c * 16), r0);
+                tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
+                tmem_ld_wait();
+                if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
+                if (row_ok && n + 16 < p.N)
+                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
+            named_barrier(2, 128);  // staged columns are free for the next tile
         }
     }
 
