@@ -299,3 +299,133 @@ def int8_gemm_s32(A_packed, BT_packed, C=None, stream=None):
     _check(load_library().b2_int8_gemm_s32(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(C), _stream(stream)),
            "b2_int8_gemm_s32")
     return C
+
+
+# ---------------------------------------------------------------- GPT-2 decode engine (include/b2engine.h)
+class GPT2Config(ctypes.Structure):
+    """Mirror of ``b2_gpt2_config`` (the reference's GPT2Config, include/gpt2_types.cuh:6-14)."""
+
+    _fields_ = [(n, ctypes.c_int) for n in
+                ("n_layers", "n_heads", "d_model", "d_ff", "vocab_size", "max_seq_len", "d_head")]
+
+
+ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
+                  "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps",
+                  "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions"]
+
+
+def _engine_lib():
+    lib = load_library()
+    if getattr(lib, "_engine_ready", False):
+        return lib
+    vp, i, u64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64
+    pe = ctypes.POINTER(vp)
+    lib.b2_engine_create_random.argtypes = [ctypes.POINTER(GPT2Config), i, i, u64, pe]
+    lib.b2_engine_load.argtypes = [ctypes.c_char_p, i, i, pe]
+    lib.b2_engine_export.argtypes = [vp, ctypes.c_char_p]
+    lib.b2_engine_destroy.argtypes = [vp]
+    lib.b2_engine_destroy.restype = None
+    lib.b2_engine_config.argtypes = [vp, ctypes.POINTER(GPT2Config)]
+    lib.b2_engine_start.argtypes = [vp, i, vp, vp, i, i, u64]
+    lib.b2_engine_step.argtypes = [vp, vp]
+    lib.b2_engine_run_steps.argtypes = [vp, i, vp]
+    lib.b2_engine_read_tokens.argtypes = [vp, vp, i]
+    lib.b2_engine_keep_logits.argtypes = [vp, i, ctypes.POINTER(vp)]
+    lib.b2_engine_read_logits.argtypes = [vp, vp]
+    lib.b2_engine_positions.argtypes = [vp, vp]
+    for n in ENGINE_SYMBOLS:
+        if n != "b2_engine_destroy":
+            getattr(lib, n).restype = i
+    lib._engine_ready = True
+    return lib
+
+
+class Engine:
+    """Batched GPT-2 INT8 decode engine: one greedy token per sequence per step, on the GPU.
+
+    Engine.random(cfg, max_batch) builds seeded N(0, 0.02) weights; Engine.load(dir) reads the
+    reference's model directory format; start() sets prompts; step()/run_steps() decode."""
+
+    def __init__(self, handle):
+        self._h = handle
+        self._lib = _engine_lib()
+        c = GPT2Config()
+        _check(self._lib.b2_engine_config(self._h, ctypes.byref(c)), "b2_engine_config")
+        self.cfg = {n: getattr(c, n) for n, _ in GPT2Config._fields_}
+        self.batch = 0
+
+    @classmethod
+    def random(cls, cfg: dict, max_batch: int, kv_dtype: int = B2_KV_F32, seed: int = 0):
+        lib = _engine_lib()
+        c = GPT2Config(**cfg)
+        h = ctypes.c_void_p()
+        _check(lib.b2_engine_create_random(ctypes.byref(c), max_batch, kv_dtype, seed, ctypes.byref(h)),
+               "b2_engine_create_random")
+        return cls(h)
+
+    @classmethod
+    def load(cls, model_dir: str, max_batch: int, kv_dtype: int = B2_KV_F32):
+        lib = _engine_lib()
+        h = ctypes.c_void_p()
+        _check(lib.b2_engine_load(model_dir.encode(), max_batch, kv_dtype, ctypes.byref(h)), "b2_engine_load")
+        return cls(h)
+
+    def export(self, model_dir: str):
+        _check(self._lib.b2_engine_export(self._h, model_dir.encode()), "b2_engine_export")
+
+    def start(self, prompts, max_new_tokens: int, seed: int = 0):
+        """prompts: list of token-id lists (one per sequence)."""
+        import numpy as np
+
+        B = len(prompts)
+        stride = max(len(p) for p in prompts)
+        arr = np.zeros((B, stride), np.int32)
+        for b, p in enumerate(prompts):
+            arr[b, : len(p)] = p
+        lens = np.array([len(p) for p in prompts], np.int32)
+        _check(self._lib.b2_engine_start(self._h, B, arr.ctypes.data, lens.ctypes.data, stride, max_new_tokens, seed),
+               "b2_engine_start")
+        self.batch = B
+        self._stride = stride + max_new_tokens + 1
+
+    def step(self, stream=None):
+        _check(self._lib.b2_engine_step(self._h, _stream(stream)), "b2_engine_step")
+
+    def run_steps(self, steps: int, stream=None):
+        _check(self._lib.b2_engine_run_steps(self._h, steps, _stream(stream)), "b2_engine_run_steps")
+
+    def keep_logits(self, enable: bool = True):
+        _check(self._lib.b2_engine_keep_logits(self._h, 1 if enable else 0, None), "b2_engine_keep_logits")
+
+    def logits(self):
+        import numpy as np
+
+        out = np.zeros((self.batch, self.cfg["vocab_size"]), np.float32)
+        _check(self._lib.b2_engine_read_logits(self._h, out.ctypes.data), "b2_engine_read_logits")
+        return out
+
+    def tokens(self):
+        """[batch, stride] greedy token chosen after the step at position p-1 (-1: none yet)."""
+        import numpy as np
+
+        out = np.zeros((self.batch, self._stride), np.int32)
+        _check(self._lib.b2_engine_read_tokens(self._h, out.ctypes.data, self._stride), "b2_engine_read_tokens")
+        return out
+
+    def positions(self):
+        import numpy as np
+
+        out = np.zeros(self.batch, np.int32)
+        _check(self._lib.b2_engine_positions(self._h, out.ctypes.data), "b2_engine_positions")
+        return out
+
+    def close(self):
+        if self._h:
+            self._lib.b2_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,580 @@
+// Batched GPT-2 INT8 decode engine (include/b2engine.h): weights, paged KV pool, block
+// allocator, the decode step as a fixed launch sequence, and its CUDA-graph replay.
+#include "common.cuh"
+#include "engine_kernels.cuh"
+#include "b2engine.h"
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+#include <sys/stat.h>
+
+namespace b2 {
+
+int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counters_zeroed, cudaStream_t st);
+size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size, int max_splits,
+                                  int kv_bytes);
+int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st);
+int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
+                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st);
+
+constexpr int kBlock = 16;        // KV block size (reference engine: block_size_ = 16)
+constexpr float kLnEps = 1e-5f;   // reference LayerNorm eps (15_layernorm_residual.cuh default)
+
+// Device linear layer in the reference's QuantWeight format + bias.
+struct QLinear {
+    int32_t* w = nullptr;  // [N, K/4]
+    float* s = nullptr;    // [N]
+    float* bias = nullptr; // [N]
+    int N = 0, K = 0;
+};
+
+struct Layer {
+    float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+    QLinear qkv, out, up, down;
+};
+
+// Counter-based normal generator (SplitMix64 hash + Box-Muller), for seeded random weights.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void randn_kernel(float* out, size_t n, uint64_t seed, float stddev) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t r = mix64(seed * 0x100000001B3ull + i);
+        const float u1 = ((uint32_t)(r >> 40) + 1u) * (1.0f / 16777217.0f);  // (0, 1]
+        const float u2 = (uint32_t)(r & 0xFFFFFFu) * (1.0f / 16777216.0f);
+        out[i] = stddev * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    }
+}
+
+__global__ void fill_kernel(float* out, size_t n, float v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = v;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+struct b2_engine {
+    b2_gpt2_config cfg{};
+    int max_batch = 0, kv_dtype = B2_KV_F32;
+    int device = 0;
+    std::vector<void*> allocs;  // every device allocation, freed by the destructor
+    float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
+    std::vector<Layer> layers;
+    // paged KV pool: per layer [P, 16, H, d_head]
+    int num_blocks = 0, blocks_per_seq = 0;
+    void* k_pool = nullptr;
+    void* v_pool = nullptr;
+    size_t layer_stride = 0;  // elements per layer in a pool
+    std::vector<int> free_blocks;
+    // per-sequence state (device)
+    int batch = 0, out_stride = 0;
+    int *tokens = nullptr, *pos = nullptr, *ctx = nullptr, *block_table = nullptr;
+    int *forced = nullptr, *forced_len = nullptr, *out_tokens = nullptr;
+    int forced_stride = 0;
+    unsigned long long* keys = nullptr;
+    // activations
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *hbuf = nullptr, *xf = nullptr;
+    float* logits = nullptr;
+    bool keep_logits = false;
+    int32_t* xq = nullptr;
+    float* xs = nullptr;
+    void* attn_ws = nullptr;
+    size_t attn_ws_bytes = 0;
+    // CUDA graph of one step
+    cudaGraphExec_t graph = nullptr;
+    bool graph_dirty = true;
+    bool failed = false;  // a device allocation failed
+
+    ~b2_engine();
+    template <typename T>
+    T* alloc(size_t n) {
+        void* p = nullptr;
+        if (n == 0) n = 1;
+        if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) {
+            failed = true;
+            return nullptr;
+        }
+        allocs.push_back(p);
+        return static_cast<T*>(p);
+    }
+};
+
+b2_engine::~b2_engine() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    if (graph) cudaGraphExecDestroy(graph);
+    for (void* p : allocs) cudaFree(p);
+    cudaSetDevice(cur);
+}
+
+namespace {
+
+bool valid_config(const b2_gpt2_config& c) {
+    return c.n_layers > 0 && c.n_heads > 0 && c.d_head > 0 && c.d_model == c.n_heads * c.d_head &&
+           (c.d_head == 64 || c.d_head == 128) && c.d_ff > 0 && c.vocab_size > 0 && c.max_seq_len > 0 &&
+           c.d_model % 16 == 0 && c.d_ff % 16 == 0 && c.d_model <= 8192;
+}
+
+// Device buffers that do not depend on the weights' source.
+int alloc_runtime(b2_engine* e) {
+    const b2_gpt2_config& c = e->cfg;
+    const int B = e->max_batch, d = c.d_model;
+    e->blocks_per_seq = (c.max_seq_len + kBlock - 1) / kBlock;
+    e->num_blocks = B * e->blocks_per_seq;
+    const size_t kvb = e->kv_dtype == B2_KV_F32 ? 4 : 2;
+    e->layer_stride = (size_t)e->num_blocks * kBlock * d;
+    const size_t pool_bytes = (size_t)c.n_layers * e->layer_stride * kvb;
+    e->k_pool = e->alloc<unsigned char>(pool_bytes);
+    e->v_pool = e->alloc<unsigned char>(pool_bytes);
+    e->tokens = e->alloc<int>(B);
+    e->pos = e->alloc<int>(B);
+    e->ctx = e->alloc<int>(B);
+    e->block_table = e->alloc<int>((size_t)B * e->blocks_per_seq);
+    e->keys = e->alloc<unsigned long long>(B);
+    e->x = e->alloc<float>((size_t)B * d);
+    e->qkv = e->alloc<float>((size_t)B * 3 * d);
+    e->q = e->alloc<float>((size_t)B * d);
+    e->attn = e->alloc<float>((size_t)B * d);
+    e->hbuf = e->alloc<float>((size_t)B * c.d_ff);
+    e->xf = e->alloc<float>((size_t)B * d);
+    e->logits = e->alloc<float>((size_t)B * c.vocab_size);
+    e->xq = e->alloc<int32_t>((size_t)B * std::max(d, c.d_ff) / 4);
+    e->xs = e->alloc<float>(B);
+    e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, c.n_heads, c.n_heads, c.d_head,
+                                                                         c.max_seq_len, kBlock, 64, 4));
+    e->attn_ws = e->alloc<unsigned char>(e->attn_ws_bytes);
+    if (e->failed) return B2_ERR_CUDA;
+    if (!e->k_pool || !e->v_pool || !e->attn_ws || !e->logits) return B2_ERR_CUDA;
+    if (cudaMemset(e->attn_ws, 0, e->attn_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
+    if (cudaMemset(e->k_pool, 0, pool_bytes) != cudaSuccess || cudaMemset(e->v_pool, 0, pool_bytes) != cudaSuccess)
+        return B2_ERR_CUDA;
+    e->free_blocks.resize(e->num_blocks);
+    std::iota(e->free_blocks.begin(), e->free_blocks.end(), 0);
+    return B2_OK;
+}
+
+int alloc_weights(b2_engine* e) {
+    const b2_gpt2_config& c = e->cfg;
+    const int d = c.d_model, ff = c.d_ff;
+    e->wte = e->alloc<float>((size_t)c.vocab_size * d);
+    e->wpe = e->alloc<float>((size_t)c.max_seq_len * d);
+    e->lnf_g = e->alloc<float>(d);
+    e->lnf_b = e->alloc<float>(d);
+    e->layers.resize(c.n_layers);
+    auto lin = [&](QLinear& L, int N, int K) {
+        L.N = N;
+        L.K = K;
+        L.w = e->alloc<int32_t>((size_t)N * K / 4);
+        L.s = e->alloc<float>(N);
+        L.bias = e->alloc<float>(N);
+        return L.w && L.s && L.bias;
+    };
+    for (Layer& l : e->layers) {
+        l.ln1_g = e->alloc<float>(d);
+        l.ln1_b = e->alloc<float>(d);
+        l.ln2_g = e->alloc<float>(d);
+        l.ln2_b = e->alloc<float>(d);
+        if (!lin(l.qkv, 3 * d, d) || !lin(l.out, d, d) || !lin(l.up, ff, d) || !lin(l.down, d, ff)) return B2_ERR_CUDA;
+        if (!l.ln1_g || !l.ln1_b || !l.ln2_g || !l.ln2_b) return B2_ERR_CUDA;
+    }
+    return (e->wte && e->wpe && e->lnf_g && e->lnf_b) ? B2_OK : B2_ERR_CUDA;
+}
+
+void randn(float* p, size_t n, uint64_t seed, float sd) { randn_kernel<<<1184, 256>>>(p, n, seed, sd); }
+void fill(float* p, size_t n, float v) { fill_kernel<<<592, 256>>>(p, n, v); }
+
+// fp32 [N, K] weight drawn N(0, 0.02), then quantised per row in place of the reference's
+// offline exporter (python/export_gpt2.py:10-40, same arithmetic as the GPU quantiser).
+int random_linear(QLinear& L, uint64_t seed, float* tmp) {
+    randn(tmp, (size_t)L.N * L.K, seed, 0.02f);
+    int st = quantize_launch(L.N, L.K, tmp, L.w, L.s, 0);
+    if (st != B2_OK) return st;
+    randn(L.bias, L.N, seed ^ 0xB1A5ull, 0.02f);
+    return B2_OK;
+}
+
+// ---- reference on-disk format (src/gpt2_engine.cu:19-112, python/export_gpt2.py:59-187)
+bool read_file(const std::string& path, void* host, size_t bytes) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) return false;
+    f.read(static_cast<char*>(host), (std::streamsize)bytes);
+    return (size_t)f.gcount() == bytes;  // a short file is an error (the reference does not check)
+}
+bool load_dev(const std::string& path, void* dev, size_t bytes) {
+    std::vector<char> h(bytes);
+    if (!read_file(path, h.data(), bytes)) return false;
+    return cudaMemcpy(dev, h.data(), bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+bool write_file(const std::string& path, const void* host, size_t bytes) {
+    std::ofstream f(path, std::ios::binary);
+    if (!f) return false;
+    f.write(static_cast<const char*>(host), (std::streamsize)bytes);
+    return (bool)f;
+}
+bool save_dev(const std::string& path, const void* dev, size_t bytes) {
+    std::vector<char> h(bytes);
+    if (cudaMemcpy(h.data(), dev, bytes, cudaMemcpyDeviceToHost) != cudaSuccess) return false;
+    return write_file(path, h.data(), bytes);
+}
+
+// config.json with the reference's seven integer keys (parse: find key, atoi after ':').
+bool parse_config(const std::string& path, b2_gpt2_config& c) {
+    std::ifstream f(path);
+    if (!f) return false;
+    std::string s((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    auto get = [&](const char* key, int& out) {
+        size_t p = s.find(std::string("\"") + key + "\"");
+        if (p == std::string::npos) return false;
+        p = s.find(':', p);
+        if (p == std::string::npos) return false;
+        out = atoi(s.c_str() + p + 1);
+        return true;
+    };
+    return get("n_layers", c.n_layers) && get("n_heads", c.n_heads) && get("d_model", c.d_model) &&
+           get("d_ff", c.d_ff) && get("vocab_size", c.vocab_size) && get("max_seq_len", c.max_seq_len) &&
+           get("d_head", c.d_head);
+}
+
+int mkdir_p(const std::string& dir) {
+    for (size_t i = 1; i <= dir.size(); ++i) {
+        if (i == dir.size() || dir[i] == '/') {
+            const std::string sub = dir.substr(0, i);
+            struct stat sb;
+            if (stat(sub.c_str(), &sb) != 0 && mkdir(sub.c_str(), 0755) != 0) return -1;
+        }
+    }
+    return 0;
+}
+
+std::string layer_dir(const std::string& root, int i) {
+    char buf[32];
+    snprintf(buf, sizeof(buf), "/layer_%02d", i);
+    return root + buf;
+}
+
+}  // namespace
+
+namespace {
+
+// One decode step: a fixed sequence of launches on `st` (capturable as a CUDA graph).
+int enqueue_step(b2_engine* e, cudaStream_t st) {
+    const b2_gpt2_config& c = e->cfg;
+    const int B = e->batch, d = c.d_model, ff = c.d_ff, H = c.n_heads, dh = c.d_head;
+    const size_t kvb = e->kv_dtype == B2_KV_F32 ? 4 : 2;
+    int r;
+#define B2_TRY(x) do { if ((r = (x)) != B2_OK) return r; } while (0)
+    B2_TRY(launch_embed(B, d, e->tokens, e->pos, e->wte, e->wpe, e->x, e->ctx, e->keys, st));
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer& L = e->layers[l];
+        unsigned char* kc = static_cast<unsigned char*>(e->k_pool) + (size_t)l * e->layer_stride * kvb;
+        unsigned char* vc = static_cast<unsigned char*>(e->v_pool) + (size_t)l * e->layer_stride * kvb;
+        // attention sub-block (pre-norm; x stays the residual and is updated in place)
+        B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
+        B2_TRY(gemm_launch(B, 3 * d, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
+                           false, st));
+        B2_TRY(launch_qkv_scatter(B, d, H, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
+                                  vc, e->kv_dtype, st));
+        b2_decode_attn_args a{};
+        a.B = B; a.H_q = H; a.H_kv = H; a.head_dim = dh;
+        a.Q = e->q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;
+        a.block_table = e->block_table; a.context_lens = e->ctx;
+        a.max_context_len = c.max_seq_len; a.block_size = kBlock; a.num_blocks_per_seq = e->blocks_per_seq;
+        a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = e->attn;
+        a.workspace = e->attn_ws; a.workspace_bytes = e->attn_ws_bytes;
+        B2_TRY(decode_attn_launch(&a, 64, true, st));
+        B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
+        B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+                           false, st));
+        // MLP sub-block
+        B2_TRY(launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st));
+        B2_TRY(gemm_launch(B, ff, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
+                           false, st));
+        B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
+        B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
+                           B2_EPI_BIAS_RESIDUAL, false, st));
+    }
+    B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, e->xf, st));
+    B2_TRY(launch_vocab_argmax(B, c.vocab_size, d, e->xf, e->wte, e->keep_logits ? e->logits : nullptr, e->keys, st));
+    B2_TRY(launch_advance(B, e->keys, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
+                          e->out_stride, c.max_seq_len, st));
+#undef B2_TRY
+    return B2_OK;
+}
+
+int finish_create(b2_engine* e, b2_engine** out) {
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        delete e;
+        return B2_ERR_CUDA;
+    }
+    *out = e;
+    return B2_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed, b2_engine** out) {
+    if (!cfg || !out || max_batch <= 0 || !valid_config(*cfg)) return B2_ERR_INVALID;
+    if (kv_dtype != B2_KV_F32 && kv_dtype != B2_KV_BF16) return B2_ERR_UNSUPPORTED;
+    b2_engine* e = new b2_engine();
+    e->cfg = *cfg;
+    e->max_batch = max_batch;
+    e->kv_dtype = kv_dtype;
+    cudaGetDevice(&e->device);
+    int st = alloc_weights(e);
+    if (st == B2_OK) st = alloc_runtime(e);
+    if (st != B2_OK) {
+        delete e;
+        return st;
+    }
+    const b2_gpt2_config& c = e->cfg;
+    const int d = c.d_model;
+    float* tmp = e->alloc<float>((size_t)std::max(3 * d, c.d_ff) * std::max(d, c.d_ff));
+    if (!tmp) {
+        delete e;
+        return B2_ERR_CUDA;
+    }
+    randn(e->wte, (size_t)c.vocab_size * d, seed * 16 + 1, 0.02f);
+    randn(e->wpe, (size_t)c.max_seq_len * d, seed * 16 + 2, 0.02f);
+    fill(e->lnf_g, d, 1.f);
+    fill(e->lnf_b, d, 0.f);
+    for (int l = 0; l < c.n_layers; ++l) {
+        Layer& L = e->layers[l];
+        fill(L.ln1_g, d, 1.f);
+        fill(L.ln1_b, d, 0.f);
+        fill(L.ln2_g, d, 1.f);
+        fill(L.ln2_b, d, 0.f);
+        const uint64_t s = seed * 1000003ull + 97ull * (l + 1);
+        if (random_linear(L.qkv, s + 1, tmp) || random_linear(L.out, s + 2, tmp) || random_linear(L.up, s + 3, tmp) ||
+            random_linear(L.down, s + 4, tmp)) {
+            delete e;
+            return B2_ERR_CUDA;
+        }
+    }
+    return finish_create(e, out);
+}
+
+int b2_engine_load(const char* model_dir, int max_batch, int kv_dtype, b2_engine** out) {
+    if (!model_dir || !out || max_batch <= 0) return B2_ERR_INVALID;
+    if (kv_dtype != B2_KV_F32 && kv_dtype != B2_KV_BF16) return B2_ERR_UNSUPPORTED;
+    b2_gpt2_config c{};
+    const std::string root(model_dir);
+    if (!parse_config(root + "/config.json", c) || !valid_config(c)) return B2_ERR_INVALID;
+    b2_engine* e = new b2_engine();
+    e->cfg = c;
+    e->max_batch = max_batch;
+    e->kv_dtype = kv_dtype;
+    cudaGetDevice(&e->device);
+    int st = alloc_weights(e);
+    if (st == B2_OK) st = alloc_runtime(e);
+    const int d = c.d_model;
+    bool ok = st == B2_OK;
+    auto f32 = [&](const std::string& path, float* dev, size_t n) { ok = ok && load_dev(path, dev, n * 4); };
+    auto qlin = [&](const std::string& dir, const char* name, QLinear& L) {
+        ok = ok && load_dev(dir + "/" + name + "_weight.bin", L.w, (size_t)L.N * L.K) &&
+             load_dev(dir + "/" + name + "_scale.bin", L.s, (size_t)L.N * 4) &&
+             load_dev(dir + "/" + name + "_bias.bin", L.bias, (size_t)L.N * 4);
+    };
+    f32(root + "/wte.bin", e->wte, (size_t)c.vocab_size * d);
+    f32(root + "/wpe.bin", e->wpe, (size_t)c.max_seq_len * d);
+    f32(root + "/ln_f_gamma.bin", e->lnf_g, d);
+    f32(root + "/ln_f_beta.bin", e->lnf_b, d);
+    for (int l = 0; ok && l < c.n_layers; ++l) {
+        const std::string ld = layer_dir(root, l);
+        Layer& L = e->layers[l];
+        f32(ld + "/ln1_gamma.bin", L.ln1_g, d);
+        f32(ld + "/ln1_beta.bin", L.ln1_b, d);
+        f32(ld + "/ln2_gamma.bin", L.ln2_g, d);
+        f32(ld + "/ln2_beta.bin", L.ln2_b, d);
+        qlin(ld, "qkv", L.qkv);
+        qlin(ld, "out", L.out);
+        qlin(ld, "ffn_up", L.up);
+        qlin(ld, "ffn_down", L.down);
+    }
+    if (!ok) {
+        delete e;
+        return st != B2_OK ? st : B2_ERR_INVALID;
+    }
+    return finish_create(e, out);
+}
+
+int b2_engine_export(const b2_engine* e, const char* model_dir) {
+    if (!e || !model_dir) return B2_ERR_INVALID;
+    const b2_gpt2_config& c = e->cfg;
+    const std::string root(model_dir);
+    char js[512];
+    snprintf(js, sizeof(js),
+             "{\n  \"n_layers\": %d,\n  \"n_heads\": %d,\n  \"d_model\": %d,\n  \"d_ff\": %d,\n  \"vocab_size\": %d,\n"
+             "  \"max_seq_len\": %d,\n  \"d_head\": %d\n}\n",
+             c.n_layers, c.n_heads, c.d_model, c.d_ff, c.vocab_size, c.max_seq_len, c.d_head);
+    bool ok = mkdir_p(root) == 0 && write_file(root + "/config.json", js, strlen(js));
+    const int d = c.d_model;
+    auto f32 = [&](const std::string& path, const float* dev, size_t n) { ok = ok && save_dev(path, dev, n * 4); };
+    auto qlin = [&](const std::string& dir, const char* name, const QLinear& L) {
+        ok = ok && save_dev(dir + "/" + name + "_weight.bin", L.w, (size_t)L.N * L.K) &&
+             save_dev(dir + "/" + name + "_scale.bin", L.s, (size_t)L.N * 4) &&
+             save_dev(dir + "/" + name + "_bias.bin", L.bias, (size_t)L.N * 4);
+    };
+    f32(root + "/wte.bin", e->wte, (size_t)c.vocab_size * d);
+    f32(root + "/wpe.bin", e->wpe, (size_t)c.max_seq_len * d);
+    f32(root + "/ln_f_gamma.bin", e->lnf_g, d);
+    f32(root + "/ln_f_beta.bin", e->lnf_b, d);
+    for (int l = 0; ok && l < c.n_layers; ++l) {
+        const std::string ld = layer_dir(root, l);
+        if (mkdir_p(ld) != 0) return B2_ERR_INVALID;
+        const Layer& L = e->layers[l];
+        f32(ld + "/ln1_gamma.bin", L.ln1_g, d);
+        f32(ld + "/ln1_beta.bin", L.ln1_b, d);
+        f32(ld + "/ln2_gamma.bin", L.ln2_g, d);
+        f32(ld + "/ln2_beta.bin", L.ln2_b, d);
+        qlin(ld, "qkv", L.qkv);
+        qlin(ld, "out", L.out);
+        qlin(ld, "ffn_up", L.up);
+        qlin(ld, "ffn_down", L.down);
+    }
+    return ok ? B2_OK : B2_ERR_INVALID;
+}
+
+void b2_engine_destroy(b2_engine* e) { delete e; }
+
+int b2_engine_config(const b2_engine* e, b2_gpt2_config* out) {
+    if (!e || !out) return B2_ERR_INVALID;
+    *out = e->cfg;
+    return B2_OK;
+}
+
+int b2_engine_start(b2_engine* e, int batch, const int32_t* prompts_host, const int32_t* prompt_lens_host,
+                    int prompt_stride, int max_new_tokens, uint64_t seed) {
+    if (!e || !prompts_host || !prompt_lens_host || batch <= 0 || batch > e->max_batch || max_new_tokens < 0 ||
+        prompt_stride <= 0)
+        return B2_ERR_INVALID;
+    const b2_gpt2_config& c = e->cfg;
+    int max_total = 0;
+    for (int b = 0; b < batch; ++b) {
+        const int pl = prompt_lens_host[b];
+        if (pl < 1 || pl > prompt_stride || pl + max_new_tokens > c.max_seq_len) return B2_ERR_INVALID;
+        for (int i = 0; i < pl; ++i)
+            if (prompts_host[(size_t)b * prompt_stride + i] < 0 || prompts_host[(size_t)b * prompt_stride + i] >= c.vocab_size)
+                return B2_ERR_INVALID;
+        max_total = std::max(max_total, pl + max_new_tokens);
+    }
+    // block allocator: return every block to the free list, shuffle it (seeded) so block
+    // tables are non-contiguous, then hand each sequence the blocks it can ever need
+    e->free_blocks.resize(e->num_blocks);
+    std::iota(e->free_blocks.begin(), e->free_blocks.end(), 0);
+    std::mt19937_64 rng(seed);
+    std::shuffle(e->free_blocks.begin(), e->free_blocks.end(), rng);
+    std::vector<int> bt((size_t)batch * e->blocks_per_seq, 0);
+    for (int b = 0; b < batch; ++b) {
+        // every sequence owns blocks for the whole max_seq_len, so a step past the requested
+        // length can never touch another sequence's blocks
+        const int need = e->blocks_per_seq;
+        if ((int)e->free_blocks.size() < need) return B2_ERR_INVALID;
+        for (int j = 0; j < need; ++j) {
+            bt[(size_t)b * e->blocks_per_seq + j] = e->free_blocks.back();
+            e->free_blocks.pop_back();
+        }
+    }
+    // forced (prompt) tokens and the output record live in one allocation per start
+    const int stride = prompt_stride;
+    const int ostride = max_total + 1;
+    if (!e->forced || e->forced_stride < stride || e->batch < batch || e->out_stride < ostride) {
+        e->forced = e->alloc<int>((size_t)e->max_batch * stride);
+        e->forced_len = e->alloc<int>(e->max_batch);
+        e->out_tokens = e->alloc<int>((size_t)e->max_batch * ostride);
+        if (e->failed) return B2_ERR_CUDA;
+    }
+    e->forced_stride = stride;
+    e->out_stride = ostride;
+    e->batch = batch;
+    std::vector<int> tok(batch), zero(batch, 0);
+    for (int b = 0; b < batch; ++b) tok[b] = prompts_host[(size_t)b * stride];
+    bool ok = cudaMemcpy(e->block_table, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(e->forced, prompts_host, (size_t)batch * stride * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(e->forced_len, prompt_lens_host, (size_t)batch * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(e->tokens, tok.data(), (size_t)batch * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(e->pos, zero.data(), (size_t)batch * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemset(e->out_tokens, 0xff, (size_t)batch * ostride * 4) == cudaSuccess;
+    e->graph_dirty = true;  // the batch size or buffers may have changed
+    return ok ? B2_OK : B2_ERR_CUDA;
+}
+
+int b2_engine_step(b2_engine* e, b2_stream_t stream) {
+    if (!e || e->batch <= 0) return B2_ERR_INVALID;
+    return enqueue_step(e, static_cast<cudaStream_t>(stream));
+}
+
+int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream) {
+    if (!e || e->batch <= 0 || steps < 0) return B2_ERR_INVALID;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (e->graph_dirty || !e->graph) {
+        if (e->graph) {
+            cudaGraphExecDestroy(e->graph);
+            e->graph = nullptr;
+        }
+        // capture on a private stream so the caller's stream may be the legacy default one
+        cudaStream_t cap;
+        if (cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking) != cudaSuccess) return B2_ERR_CUDA;
+        cudaGraph_t g = nullptr;
+        int r = B2_OK;
+        if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) r = B2_ERR_CUDA;
+        if (r == B2_OK) r = enqueue_step(e, cap);
+        if (cudaStreamEndCapture(cap, &g) != cudaSuccess && r == B2_OK) r = B2_ERR_CUDA;
+        if (r == B2_OK && cudaGraphInstantiate(&e->graph, g, 0) != cudaSuccess) r = B2_ERR_CUDA;
+        if (g) cudaGraphDestroy(g);
+        cudaStreamDestroy(cap);
+        if (r != B2_OK) return r;
+        e->graph_dirty = false;
+    }
+    for (int i = 0; i < steps; ++i)
+        if (cudaGraphLaunch(e->graph, st) != cudaSuccess) return B2_ERR_CUDA;
+    return B2_OK;
+}
+
+int b2_engine_read_tokens(const b2_engine* e, int32_t* out_host, int out_stride) {
+    if (!e || !out_host || e->batch <= 0 || out_stride <= 0) return B2_ERR_INVALID;
+    std::vector<int> buf((size_t)e->batch * e->out_stride);
+    if (cudaMemcpy(buf.data(), e->out_tokens, buf.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return B2_ERR_CUDA;
+    for (int b = 0; b < e->batch; ++b)
+        for (int p = 0; p < out_stride; ++p)
+            out_host[(size_t)b * out_stride + p] = p < e->out_stride ? buf[(size_t)b * e->out_stride + p] : -1;
+    return B2_OK;
+}
+
+int b2_engine_keep_logits(b2_engine* e, int enable, const float** logits) {
+    if (!e) return B2_ERR_INVALID;
+    if (e->keep_logits != (enable != 0)) e->graph_dirty = true;
+    e->keep_logits = enable != 0;
+    if (logits) *logits = e->keep_logits ? e->logits : nullptr;
+    return B2_OK;
+}
+
+int b2_engine_read_logits(const b2_engine* e, float* out_host) {
+    if (!e || !out_host || e->batch <= 0 || !e->keep_logits) return B2_ERR_INVALID;
+    return cudaMemcpy(out_host, e->logits, (size_t)e->batch * e->cfg.vocab_size * 4, cudaMemcpyDeviceToHost) ==
+                   cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
+}
+
+int b2_engine_positions(const b2_engine* e, int32_t* pos_host) {
+    if (!e || !pos_host || e->batch <= 0) return B2_ERR_INVALID;
+    return cudaMemcpy(pos_host, e->pos, (size_t)e->batch * 4, cudaMemcpyDeviceToHost) == cudaSuccess ? B2_OK
+                                                                                                       : B2_ERR_CUDA;
+}
+
+}  // extern "C"

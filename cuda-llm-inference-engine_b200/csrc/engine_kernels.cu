@@ -1,0 +1,260 @@
+// Small kernels of the batched GPT-2 decode step (one token per sequence per step).
+//
+// Reference semantics (mohith-suresh/CUDA-LLM-Inference-Engine):
+//   embedding           kernels/layernorm/15_embed.cu:4-22      x = wte[id] + wpe[pos]
+//   LayerNorm           kernels/layernorm/15_layernorm_residual.cu:59-103
+//                       mean = sum/cols; var = sumsq/cols - mean^2; inv = rsqrtf(var + eps);
+//                       y = gamma (x - mean) inv + beta
+//   QKV split + KV write src/gpt2_engine.cu:292-346             Q||K||V per token; K,V to
+//                       cache[((bt[pos/bs]*bs + pos%bs)*H + h)*dh + i]
+//   vocab projection    src/gpt2_engine.cu:391-403              logits[v] = sum_k h[k] wte[v,k]
+//   greedy sampling     src/sampler.cu:10-14                    argmax, lowest index on ties
+// B200 changes: the step is batched over B sequences with per-sequence positions held on
+// the device; LayerNorm is fused with the per-row int8 quantiser that follows it in every
+// use (src/gpt2_engine.cu:460-463, 516-520); the QKV split is fused with the KV-cache write;
+// the vocab projection is a tiled fp32 kernel over the whole batch fused with the argmax
+// (64-bit atomicMax on an order-preserving key), so no logits leave the GPU; positions,
+// context lengths and the next input token advance on the device, so a whole step is a
+// fixed sequence of launches that a CUDA graph can replay.
+#include "common.cuh"
+#include "engine_kernels.cuh"
+#include <cuda_bf16.h>
+
+namespace b2 {
+
+// ------------------------------------------------------------------ embedding
+__global__ void embed_kernel(int d, const int* __restrict__ tokens, const int* __restrict__ pos,
+                             const float* __restrict__ wte, const float* __restrict__ wpe, float* __restrict__ x,
+                             int* __restrict__ ctx_lens, unsigned long long* __restrict__ argmax_keys) {
+    const int b = blockIdx.x;
+    const int tok = tokens[b];
+    const int p = pos[b];
+    const float* e = wte + (size_t)tok * d;
+    const float* w = wpe + (size_t)p * d;
+    float* o = x + (size_t)b * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) o[i] = e[i] + w[i];
+    if (threadIdx.x == 0) {
+        ctx_lens[b] = p + 1;     // attention of this step covers positions [0, p]
+        argmax_keys[b] = 0ull;   // reset the greedy-sampling reduction for this step
+    }
+}
+
+// ------------------------------------------------------------------ LayerNorm + int8 quantise
+// One CTA per row; the row stays in registers (cols <= LNQ_THREADS * LNQ_MAX_PER_THREAD).
+constexpr int LNQ_THREADS = 256;
+constexpr int LNQ_MAX_PER_THREAD = 32;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < LNQ_THREADS / 32; ++w) t += red[w];
+    __syncthreads();
+    return t;
+}
+
+__global__ void __launch_bounds__(LNQ_THREADS)
+ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__ gamma,
+                const float* __restrict__ beta, float eps, int32_t* __restrict__ q_out,
+                float* __restrict__ scale_out, float* __restrict__ y_out) {
+    __shared__ float red[LNQ_THREADS / 32];
+    const int row = blockIdx.x;
+    const float* xr = x + (size_t)row * cols;
+    float v[LNQ_MAX_PER_THREAD];
+    float s = 0.f, ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
+        const int c = threadIdx.x + k * LNQ_THREADS;
+        v[k] = c < cols ? xr[c] : 0.f;
+        s += v[k];
+        ss = fmaf(v[k], v[k], ss);
+    }
+    const float mean = block_sum(s, red) / cols;
+    const float var = block_sum(ss, red) / cols - mean * mean;
+    const float inv = rsqrtf(var + eps);
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
+        const int c = threadIdx.x + k * LNQ_THREADS;
+        if (c < cols) {
+            v[k] = fmaf(gamma[c] * (v[k] - mean), inv, beta[c]);
+            amax = fmaxf(amax, fabsf(v[k]));
+        }
+    }
+    if (!q_out) {  // plain LayerNorm (final ln_f feeding the fp32 vocab projection)
+#pragma unroll
+        for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
+            const int c = threadIdx.x + k * LNQ_THREADS;
+            if (c < cols) y_out[(size_t)row * cols + c] = v[k];
+        }
+        return;
+    }
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < LNQ_THREADS / 32; ++w) amax = fmaxf(amax, red[w]);
+    // quantiser semantics of kernels/quantization/14_int8_gemm.cu:36-58
+    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float invs = __fdiv_rn(1.0f, scale);
+    if (threadIdx.x == 0) scale_out[row] = scale;
+    int8_t* qb = reinterpret_cast<int8_t*>(q_out) + (size_t)row * cols;
+#pragma unroll
+    for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
+        const int c = threadIdx.x + k * LNQ_THREADS;
+        if (c < cols) {
+            const float qf = fminf(fmaxf(rintf(__fmul_rn(v[k], invs)), -128.f), 127.f);
+            qb[c] = (int8_t)(int)qf;
+            if (y_out) y_out[(size_t)row * cols + c] = v[k];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ QKV split + paged KV write
+template <typename KV>
+__device__ __forceinline__ KV to_kv(float v);
+template <>
+__device__ __forceinline__ float to_kv<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_kv<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename KV>
+__global__ void qkv_scatter_kernel(int d, int H, int dh, int block_size, int nbps, const float* __restrict__ qkv,
+                                   const int* __restrict__ pos, const int* __restrict__ block_table,
+                                   float* __restrict__ q, KV* __restrict__ k_cache, KV* __restrict__ v_cache) {
+    const int b = blockIdx.x;
+    const int p = pos[b];
+    const int phys = block_table[(size_t)b * nbps + p / block_size];
+    const size_t slot = ((size_t)phys * block_size + p % block_size) * H * dh;  // token row base
+    const float* src = qkv + (size_t)b * 3 * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        q[(size_t)b * d + i] = src[i];
+        k_cache[slot + i] = to_kv<KV>(src[d + i]);
+        v_cache[slot + i] = to_kv<KV>(src[2 * d + i]);
+    }
+}
+
+// ------------------------------------------------------------------ vocab projection + argmax
+// logits[b, v] = sum_k h[b,k] * wte[v,k] for a 64 x 64 (batch x vocab) tile per CTA, fp32 FMA
+// in the reference's k order per output; then the tile's per-row maxima go to a 64-bit
+// atomicMax whose key orders by value, then by lowest vocab index.
+constexpr int VP_TB = 64, VP_TV = 64, VP_TK = 32, VP_THREADS = 256;
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
+__global__ void __launch_bounds__(VP_THREADS)
+vocab_argmax_kernel(int B, int V, int d, const float* __restrict__ h, const float* __restrict__ wte,
+                    float* __restrict__ logits, unsigned long long* __restrict__ keys) {
+    __shared__ float hs[VP_TK][VP_TB + 4];
+    __shared__ float ws[VP_TK][VP_TV + 4];
+    __shared__ unsigned long long best[VP_TB];
+    const int v0 = blockIdx.x * VP_TV;
+    const int b0 = blockIdx.y * VP_TB;
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // 16 x 16 threads, 4 x 4 outputs each
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < d; k0 += VP_TK) {
+        for (int i = threadIdx.x; i < VP_TK * VP_TB; i += VP_THREADS) {
+            const int r = i / VP_TK, c = i % VP_TK;
+            const int bb = b0 + r, kk = k0 + c;
+            hs[c][r] = (bb < B && kk < d) ? h[(size_t)bb * d + kk] : 0.f;
+            const int vv = v0 + r;
+            ws[c][r] = (vv < V && kk < d) ? wte[(size_t)vv * d + kk] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int c = 0; c < VP_TK; ++c) {
+            float a[4], w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { a[i] = hs[c][ty * 4 + i]; w[i] = ws[c][tx * 4 + i]; }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x < VP_TB) best[threadIdx.x] = 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int bb = b0 + ty * 4 + i;
+        unsigned long long m = 0ull;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int vv = v0 + tx * 4 + j;
+            if (bb < B && vv < V) {
+                if (logits) logits[(size_t)bb * V + vv] = acc[i][j];
+                const unsigned long long key = argmax_key(acc[i][j], vv);
+                m = key > m ? key : m;
+            }
+        }
+        if (bb < B) atomicMax(&best[ty * 4 + i], m);
+    }
+    __syncthreads();
+    if (threadIdx.x < VP_TB && b0 + threadIdx.x < B) atomicMax(&keys[b0 + threadIdx.x], best[threadIdx.x]);
+}
+
+// next token = argmax (or the forced prompt token while the prompt lasts); advance positions
+__global__ void advance_kernel(int B, const unsigned long long* __restrict__ keys, int* __restrict__ tokens,
+                               int* __restrict__ pos, const int* __restrict__ forced, const int* __restrict__ forced_len,
+                               int forced_stride, int* __restrict__ out_tokens, int out_stride, int max_pos) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int next = (int)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull));
+    const int p = min(pos[b] + 1, max_pos - 1);
+    int tok = next;
+    if (forced && p < forced_len[b]) tok = forced[(size_t)b * forced_stride + p];
+    if (out_tokens && p < out_stride) out_tokens[(size_t)b * out_stride + p] = next;
+    tokens[b] = tok;
+    pos[b] = p;
+}
+
+// ------------------------------------------------------------------ launchers
+int launch_embed(int B, int d, const int* tokens, const int* pos, const float* wte, const float* wpe, float* x,
+                 int* ctx_lens, unsigned long long* keys, cudaStream_t st) {
+    embed_kernel<<<B, 256, 0, st>>>(d, tokens, pos, wte, wpe, x, ctx_lens, keys);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
+                    int32_t* q, float* scale, float* y, cudaStream_t st) {
+    if (cols > LNQ_THREADS * LNQ_MAX_PER_THREAD || (cols & 3)) return B2_ERR_UNSUPPORTED;
+    ln_quant_kernel<<<rows, LNQ_THREADS, 0, st>>>(cols, x, gamma, beta, eps, q, scale, y);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+int launch_qkv_scatter(int B, int d, int H, int dh, int block_size, int nbps, const float* qkv, const int* pos,
+                       const int* block_table, float* q, void* k_cache, void* v_cache, int kv_dtype, cudaStream_t st) {
+    if (kv_dtype == B2_KV_F32)
+        qkv_scatter_kernel<float><<<B, 256, 0, st>>>(d, H, dh, block_size, nbps, qkv, pos, block_table, q,
+                                                     static_cast<float*>(k_cache), static_cast<float*>(v_cache));
+    else
+        qkv_scatter_kernel<__nv_bfloat16><<<B, 256, 0, st>>>(d, H, dh, block_size, nbps, qkv, pos, block_table, q,
+                                                             static_cast<__nv_bfloat16*>(k_cache),
+                                                             static_cast<__nv_bfloat16*>(v_cache));
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, float* logits,
+                        unsigned long long* keys, cudaStream_t st) {
+    dim3 grid((V + VP_TV - 1) / VP_TV, (B + VP_TB - 1) / VP_TB);
+    vocab_argmax_kernel<<<grid, VP_THREADS, 0, st>>>(B, V, d, h, wte, logits, keys);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+int launch_advance(int B, const unsigned long long* keys, int* tokens, int* pos, const int* forced,
+                   const int* forced_len, int forced_stride, int* out_tokens, int out_stride, int max_pos,
+                   cudaStream_t st) {
+    advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(B, keys, tokens, pos, forced, forced_len, forced_stride,
+                                                     out_tokens, out_stride, max_pos);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+}  // namespace b2

@@ -1,0 +1,18 @@
+// Launchers of the batched decode-step kernels (engine_kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace b2 {
+int launch_embed(int B, int d, const int* tokens, const int* pos, const float* wte, const float* wpe, float* x,
+                 int* ctx_lens, unsigned long long* keys, cudaStream_t st);
+int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
+                    int32_t* q, float* scale, float* y, cudaStream_t st);
+int launch_qkv_scatter(int B, int d, int H, int dh, int block_size, int nbps, const float* qkv, const int* pos,
+                       const int* block_table, float* q, void* k_cache, void* v_cache, int kv_dtype, cudaStream_t st);
+int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, float* logits,
+                        unsigned long long* keys, cudaStream_t st);
+int launch_advance(int B, const unsigned long long* keys, int* tokens, int* pos, const int* forced,
+                   const int* forced_len, int forced_stride, int* out_tokens, int out_stride, int max_pos,
+                   cudaStream_t st);
+}  // namespace b2

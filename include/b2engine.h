@@ -1,0 +1,89 @@
+/*
+ * b2engine.h — C ABI of the batched GPT-2 INT8 decode engine on B200.
+ *
+ * Replaces the decode path of the reference's GPT2Engine (src/gpt2_engine.cuh:9-92,
+ * src/gpt2_engine.cu:447-528 forward_layer, :716-776 decode loop), which runs one sequence,
+ * blocks on host<->device copies several times per layer and samples on the host. Here one
+ * decode step advances every sequence of a batch by one token entirely on the device:
+ * embedding, per layer [LayerNorm+quantise, INT8 QKV (+bias), QKV split + paged KV write,
+ * K13 decode attention, quantise, INT8 out-proj (+bias+residual), LayerNorm+quantise, INT8
+ * FC1 (+bias+GELU), quantise, INT8 FC2 (+bias+residual)], final LayerNorm, tied fp32 vocab
+ * projection with a GPU argmax (lowest index on ties, like the reference's std::max_element,
+ * src/sampler.cu:10-14), and the position advance. A step is a fixed launch sequence, so
+ * b2_engine_run_steps replays it as a CUDA graph.
+ *
+ * Formats kept from the reference: the on-disk model directory (config.json + *.bin,
+ * python/export_gpt2.py:59-187, src/gpt2_engine.cu:41-112), QuantWeight packing
+ * (include/gpt2_types.cuh:16-21), and the paged KV layout [P, 16, H, d_head] per layer
+ * (src/gpt2_engine.cu:143-153) with per-sequence block tables.
+ */
+#ifndef B2ENGINE_H
+#define B2ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include "b2decode.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same fields and order as the reference's GPT2Config (include/gpt2_types.cuh:6-14). */
+typedef struct {
+    int n_layers, n_heads, d_model, d_ff, vocab_size, max_seq_len, d_head;
+} b2_gpt2_config;
+
+typedef struct b2_engine b2_engine;
+
+/* Engine with seeded random weights: N(0, 0.02) for wte, wpe, every linear weight (then
+ * per-row int8 quantised) and every bias; LayerNorm gamma = 1, beta = 0. max_batch
+ * sequences of up to cfg->max_seq_len tokens get KV blocks from the engine's pool. */
+int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed,
+                            b2_engine** out);
+
+/* Engine from a model directory in the reference's format (GPT2Engine::load_weights,
+ * src/gpt2_engine.cu:75-112). Any number of layers. Missing or short files are errors. */
+int b2_engine_load(const char* model_dir, int max_batch, int kv_dtype, b2_engine** out);
+
+/* Writes the engine's weights in the reference's directory format. */
+int b2_engine_export(const b2_engine* e, const char* model_dir);
+
+void b2_engine_destroy(b2_engine* e);
+
+int b2_engine_config(const b2_engine* e, b2_gpt2_config* out);
+
+/* Starts `batch` sequences: prompts_host [batch, prompt_stride] token ids, prompt_lens_host
+ * [batch] (>= 1). Frees the previous sequences' KV blocks, gives every sequence
+ * ceil(max_seq_len / 16) blocks from the pool's free list (in a seeded random order, so block
+ * tables are non-contiguous), and sets every position to 0. Positions stop at
+ * max_seq_len - 1 (further steps rewrite that slot). Steps then
+ * feed the prompt token by token through the decode path (the reference's continuation
+ * mode, src/gpt2_engine.cu:683-696) and continue greedily. Synchronous. */
+int b2_engine_start(b2_engine* e, int batch, const int32_t* prompts_host, const int32_t* prompt_lens_host,
+                    int prompt_stride, int max_new_tokens, uint64_t seed);
+
+/* One decode step for every active sequence (asynchronous on `stream`). */
+int b2_engine_step(b2_engine* e, b2_stream_t stream);
+
+/* `steps` decode steps, replayed from a CUDA graph of one step captured on first use. */
+int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream);
+
+/* Copies the greedy token chosen at each position: out_host [batch, out_stride], entry
+ * [b][p] = argmax after the step at position p-1 (-1 where no step has run). Synchronous. */
+int b2_engine_read_tokens(const b2_engine* e, int32_t* out_host, int out_stride);
+
+/* Keeps the fp32 logits [batch, vocab] of the last step on the device (tests); returns the
+ * device pointer through *logits, or NULL when disabled. */
+int b2_engine_keep_logits(b2_engine* e, int enable, const float** logits);
+
+/* Copies the last step's logits [batch, vocab] to host memory (needs keep_logits). Synchronous. */
+int b2_engine_read_logits(const b2_engine* e, float* out_host);
+
+/* Current position of every sequence (tokens already in its KV cache). Synchronous. */
+int b2_engine_positions(const b2_engine* e, int32_t* pos_host);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2ENGINE_H */

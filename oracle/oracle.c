@@ -197,3 +197,36 @@ int oracle_max_threads(void) {
     return 1;
 #endif
 }
+
+/* LayerNorm (reference kernels/layernorm/15_layernorm_residual.cu:59-103): mean = sum/cols,
+ * var = sumsq/cols - mean^2, inv = 1/sqrt(var + eps) (the GPU uses rsqrtf),
+ * y = gamma*(x-mean)*inv + beta, the last step fused as in the reference build. */
+void oracle_layernorm(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
+                      float* y) {
+    for (int r = 0; r < rows; ++r) {
+        const float* xr = x + (size_t)r * cols;
+        float s = 0.0f, ss = 0.0f;
+        for (int c = 0; c < cols; ++c) {
+            s += xr[c];
+            ss += xr[c] * xr[c];
+        }
+        const float mean = s / cols;
+        const float var = ss / cols - mean * mean;
+        const float inv = 1.0f / sqrtf(var + eps);
+        for (int c = 0; c < cols; ++c) y[(size_t)r * cols + c] = fmaf(gamma[c] * (xr[c] - mean), inv, beta[c]);
+    }
+}
+
+/* Tied fp32 vocab projection (reference src/gpt2_engine.cu:391-403): logits[b,v] = sum_k h[b,k]*wte[v,k]. */
+void oracle_vocab_proj(int B, int V, int d, const float* h, const float* wte, float* logits, int nthreads) {
+#ifdef _OPENMP
+    if (nthreads <= 0) nthreads = omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+#endif
+    for (int v = 0; v < V; ++v)
+        for (int b = 0; b < B; ++b) {
+            float sum = 0.0f;
+            for (int k = 0; k < d; ++k) sum += h[(size_t)b * d + k] * wte[(size_t)v * d + k];
+            logits[(size_t)b * V + v] = sum;
+        }
+}

@@ -38,6 +38,8 @@ def lib():
         L.oracle_int8_gemm.argtypes = [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i]
         L.oracle_epilogue.argtypes = [_i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i]
         L.oracle_max_threads.restype = _i
+        L.oracle_layernorm.argtypes = [_i, _i, _vp, _vp, _vp, ctypes.c_float, _vp]
+        L.oracle_vocab_proj.argtypes = [_i, _i, _i, _vp, _vp, _vp, _i]
         _lib = L
     return _lib
 
@@ -135,3 +137,93 @@ def ref_gqa_cpu(Q, K, V, causal=False):
     O = np.zeros_like(Q)
     ref().ref_gqa_cpu_reference(B, H_q, H_kv, N, d, qp, kp, vp, O.ctypes.data, 1 if causal else 0)
     return O
+
+
+def layernorm(x, gamma, beta, eps=1e-5):
+    x, xp = _c(x, np.float32)
+    g, gp = _c(gamma, np.float32)
+    b, bp = _c(beta, np.float32)
+    y = np.zeros_like(x)
+    lib().oracle_layernorm(x.shape[0], x.shape[1], xp, gp, bp, eps, y.ctypes.data)
+    return y
+
+
+def vocab_proj(h, wte, nthreads=0):
+    h, hp = _c(h, np.float32)
+    w, wp = _c(wte, np.float32)
+    out = np.zeros((h.shape[0], w.shape[0]), np.float32)
+    lib().oracle_vocab_proj(h.shape[0], w.shape[0], h.shape[1], hp, wp, out.ctypes.data, nthreads)
+    return out
+
+
+class GPT2Oracle:
+    """CPU restatement of the reference GPT2Engine decode step (src/gpt2_engine.cu:447-528,
+    612-620) over a model directory in the reference's format, batched over sequences with
+    their own positions. KV caches are kept paged with identity block tables."""
+
+    LINEARS = [("qkv", 3), ("out", 1), ("ffn_up", None), ("ffn_down", 1)]
+
+    def __init__(self, model_dir):
+        import json
+        import os
+
+        txt = open(os.path.join(model_dir, "config.json")).read()
+        c = json.loads(txt)
+        self.cfg = c
+        L, d, ff, V, S = c["n_layers"], c["d_model"], c["d_ff"], c["vocab_size"], c["max_seq_len"]
+        f = lambda name, n: np.fromfile(os.path.join(model_dir, name), np.float32, n)  # noqa: E731
+        i = lambda name, n: np.fromfile(os.path.join(model_dir, name), np.int32, n)  # noqa: E731
+        self.wte = f("wte.bin", V * d).reshape(V, d)
+        self.wpe = f("wpe.bin", S * d).reshape(S, d)
+        self.lnf = (f("ln_f_gamma.bin", d), f("ln_f_beta.bin", d))
+        self.layers = []
+        shapes = {"qkv": (3 * d, d), "out": (d, d), "ffn_up": (ff, d), "ffn_down": (d, ff)}
+        for l in range(L):
+            ld = "layer_%02d/" % l
+            lay = {"ln1": (f(ld + "ln1_gamma.bin", d), f(ld + "ln1_beta.bin", d)),
+                   "ln2": (f(ld + "ln2_gamma.bin", d), f(ld + "ln2_beta.bin", d))}
+            for name, (N, K) in shapes.items():
+                lay[name] = (i(ld + name + "_weight.bin", N * K // 4).reshape(N, K // 4),
+                             f(ld + name + "_scale.bin", N), f(ld + name + "_bias.bin", N))
+            self.layers.append(lay)
+
+    def reset(self, batch):
+        c = self.cfg
+        self.B = batch
+        self.nb = (c["max_seq_len"] + 15) // 16
+        shape = (c["n_layers"], batch * self.nb, 16, c["n_heads"], c["d_head"])
+        self.k = np.zeros(shape, np.float32)
+        self.v = np.zeros(shape, np.float32)
+        self.bt = np.arange(batch * self.nb, dtype=np.int32).reshape(batch, self.nb)
+
+    def step(self, tokens, pos, nthreads=0):
+        """Appends tokens[b] at position pos[b] for every sequence; returns logits [B, V]."""
+        c = self.cfg
+        d, H, dh = c["d_model"], c["n_heads"], c["d_head"]
+        tokens = np.asarray(tokens)
+        pos = np.asarray(pos)
+        x = (self.wte[tokens] + self.wpe[pos]).astype(np.float32)
+        for l, lay in enumerate(self.layers):
+            y = layernorm(x, *lay["ln1"])
+            q8, s = quantize(y)
+            w, ws, wb = lay["qkv"]
+            qkv = int8_gemm(q8, w, s, ws, wb, None, 1, nthreads)
+            for b in range(self.B):
+                p = int(pos[b])
+                blk, slot = self.bt[b, p // 16], p % 16
+                self.k[l, blk, slot] = qkv[b, d:2 * d].reshape(H, dh)
+                self.v[l, blk, slot] = qkv[b, 2 * d:].reshape(H, dh)
+            att = decode_attn(qkv[:, :d].reshape(self.B, H, dh), self.k[l], self.v[l], self.bt,
+                              (pos + 1).astype(np.int32), nthreads=nthreads).reshape(self.B, d)
+            q8, s = quantize(att)
+            w, ws, wb = lay["out"]
+            x = int8_gemm(q8, w, s, ws, wb, x, 3, nthreads)
+            y = layernorm(x, *lay["ln2"])
+            q8, s = quantize(y)
+            w, ws, wb = lay["ffn_up"]
+            h = int8_gemm(q8, w, s, ws, wb, None, 2, nthreads)
+            q8, s = quantize(h)
+            w, ws, wb = lay["ffn_down"]
+            x = int8_gemm(q8, w, s, ws, wb, x, 3, nthreads)
+        xf = layernorm(x, *self.lnf)
+        return vocab_proj(xf, self.wte, nthreads)

@@ -10,8 +10,8 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def declared_c_symbols():
-    txt = open(os.path.join(ROOT, "include", "b2decode.h")).read()
+def declared_c_symbols(header="b2decode.h"):
+    txt = open(os.path.join(ROOT, "include", header)).read()
     return sorted(set(re.findall(r"\b(b2_[a-z0-9_]+)\s*\(", txt)))
 
 
@@ -22,12 +22,13 @@ def declared_cxx_symbols():
 
 def test_header_symbol_lists_match_package(b2):
     assert declared_c_symbols() == sorted(b2.C_ABI_SYMBOLS)
+    assert declared_c_symbols("b2engine.h") == sorted(b2.ENGINE_SYMBOLS)
     assert declared_cxx_symbols() == sorted(b2._CXX)
 
 
 def test_library_exports_every_declared_symbol(b2):
     lib = b2.load_library()
-    for s in declared_c_symbols():
+    for s in declared_c_symbols() + declared_c_symbols("b2engine.h"):
         assert hasattr(lib, s), s
     out = subprocess.run(["nm", "-D", "--defined-only", b2.LIB_PATH], capture_output=True, text=True).stdout
     for name, mangled in b2._CXX.items():

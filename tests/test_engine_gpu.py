@@ -1,0 +1,110 @@
+"""Batched GPT-2 decode engine vs the CPU oracle of the reference engine's decode step.
+
+The oracle (oracle.GPT2Oracle) restates GPT2Engine::forward_layer's decode branch
+(src/gpt2_engine.cu:447-528) plus the final LayerNorm and tied vocab projection
+(:612-620) in C, fed the same tokens as the engine. LayerNorm reductions run in a different
+order on the GPU (and rsqrtf vs 1/sqrtf), so an int8 activation can land one quantisation
+step away; the bar is therefore on the logits: max |d| <= 2e-3 * max |logit| + 1e-4 per step,
+and the greedy token must equal the oracle's wherever the oracle's top-2 gap exceeds that bound.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(n_layers=2, n_heads=4, d_model=256, d_ff=1024, vocab_size=1000, max_seq_len=64, d_head=64)
+
+
+def _prompts(rng, B, vocab, lens):
+    return [list(rng.integers(0, vocab, n)) for n in lens[:B]]
+
+
+def _check_logits(got, want, tag):
+    bound = 2e-3 * np.abs(want).max() + 1e-4
+    err = np.abs(got - want).max()
+    assert err <= bound, f"{tag}: max |logit diff| {err:.3e} > {bound:.3e}"
+    top2 = np.sort(want, axis=1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > 2 * bound
+    assert np.array_equal(got.argmax(1)[clear], want.argmax(1)[clear]), tag
+    return err
+
+
+def test_engine_steps_match_oracle(b2, oracle, cuda, tmp_path):
+    rng = np.random.default_rng(1)
+    eng = b2.Engine.random(SMALL, max_batch=4, seed=7)
+    model_dir = str(tmp_path / "model")
+    eng.export(model_dir)
+    orc = oracle.GPT2Oracle(model_dir)
+    prompts = _prompts(rng, 3, SMALL["vocab_size"], [5, 9, 1])
+    new = 6
+    eng.start(prompts, new, seed=3)
+    eng.keep_logits(True)
+    orc.reset(3)
+    B = 3
+    toks = np.array([p[0] for p in prompts])
+    pos = np.zeros(B, np.int64)
+    worst = 0.0
+    for step in range(max(len(p) for p in prompts) + new - 1):
+        eng.step()
+        got = eng.logits()
+        want = orc.step(toks, pos)
+        worst = max(worst, _check_logits(got, want, f"step {step}"))
+        assert b2.device_error() == 0
+        # next inputs exactly as the engine chose them (prompt while it lasts, then greedy)
+        pos = pos + 1
+        nxt = got.argmax(1)
+        toks = np.array([prompts[b][pos[b]] if pos[b] < len(prompts[b]) else nxt[b] for b in range(B)])
+    assert np.array_equal(eng.positions(), pos)
+    out = eng.tokens()
+    assert out[0, 1] == got.argmax(1)[0] or out[0, 1] >= 0
+    print("max |logit diff| over all steps:", worst)
+
+
+def test_graph_replay_equals_eager_and_export_roundtrip(b2, cuda, tmp_path):
+    rng = np.random.default_rng(2)
+    cfg = dict(SMALL, n_layers=3)
+    prompts = _prompts(rng, 4, cfg["vocab_size"], [3, 7, 2, 4])
+    e1 = b2.Engine.random(cfg, max_batch=4, seed=11)
+    e1.start(prompts, 12, seed=5)
+    for _ in range(18):
+        e1.step()
+    t1 = e1.tokens()
+    e1.start(prompts, 12, seed=9)  # different block placement, graph path
+    e1.run_steps(18)
+    t2 = e1.tokens()
+    assert np.array_equal(t1, t2)
+    d = str(tmp_path / "m")
+    e1.export(d)
+    e2 = b2.Engine.load(d, max_batch=4)
+    e2.start(prompts, 12, seed=5)
+    e2.run_steps(18)
+    assert np.array_equal(e2.tokens(), t1)
+    assert (t1[:, 1:19] >= 0).all()
+
+
+def test_bf16_kv_close_to_fp32(b2, cuda):
+    rng = np.random.default_rng(3)
+    prompts = _prompts(rng, 2, SMALL["vocab_size"], [6, 6])
+    e32 = b2.Engine.random(SMALL, max_batch=2, seed=21)
+    e16 = b2.Engine.random(SMALL, max_batch=2, kv_dtype=b2.B2_KV_BF16, seed=21)
+    for e in (e32, e16):
+        e.start(prompts, 4, seed=1)
+        e.keep_logits(True)
+        for _ in range(5):  # stay inside the (forced) prompt so both see the same tokens
+            e.step()
+    a, b = e32.logits(), e16.logits()
+    assert np.abs(a - b).max() <= 2e-2 * np.abs(a).max()
+
+
+def test_engine_rejects_bad_inputs(b2, cuda, tmp_path):
+    with pytest.raises(b2.B2Error):
+        b2.Engine.random(dict(SMALL, d_head=96, d_model=384), max_batch=1)
+    with pytest.raises(b2.B2Error):
+        b2.Engine.load(str(tmp_path / "missing"), max_batch=1)
+    e = b2.Engine.random(SMALL, max_batch=2)
+    with pytest.raises(b2.B2Error):
+        e.start([[1, 2], [3], [4]], 4)                       # batch > max_batch
+    with pytest.raises(b2.B2Error):
+        e.start([[SMALL["vocab_size"]]], 4)                  # token id out of range
+    with pytest.raises(b2.B2Error):
+        e.start([[1] * 60], 10)                              # beyond max_seq_len
