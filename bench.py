@@ -395,11 +395,58 @@ def secondary(torch, b2, np, args, kc, vc, q, btd, lensd, lens, bt, P, hbm_peak,
     out["mha_config1"] = {"gbs": round(by1 / (ms / n1 * 1e-3) / 1e9, 1), "us_per_call": round(ms / n1 * 1e3, 2),
                           "algorithmic_bytes": by1, "l2": "40 rotated copies (250 MB)"}
     del sets
+    out["gpt2_small_config4"] = gpt2_config4(torch, b2, np, hbm_peak)
     peak_int8 = 2.0 * bf16_peak  # dense int8 rate is twice the bf16 rate on the same tensor cores
     for (M, N, K) in [(2048, 2048, 2048), (64, 3072, 768), (8192, 8192, 8192)]:
         out[f"int8_gemm_{M}x{N}x{K}"] = gemm_secondary(torch, b2, M, N, K, args.steps, peak_int8)
     out["int8_peak_tops"] = peak_int8
     return out
+
+
+GPT2_SMALL = dict(n_layers=12, n_heads=12, d_model=768, d_ff=3072, vocab_size=50257, max_seq_len=1024, d_head=64)
+
+
+def gpt2_step_bytes(cfg, B, ctx_mean):
+    """Algorithmic HBM bytes of one batched decode step: int8 weights + scales + biases, the
+    fp32 tied embedding (vocab projection), LayerNorm vectors, and the live fp32 K/V."""
+    d, ff, L, V = cfg["d_model"], cfg["d_ff"], cfg["n_layers"], cfg["vocab_size"]
+    lin = L * (3 * d * d + d * d + ff * d + d * ff)
+    vec = L * (8 * (3 * d + d + ff + d) + 4 * 4 * d)
+    kv = B * ctx_mean * L * 2 * d * 4
+    return lin + vec + V * d * 4 + kv
+
+
+def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
+    """GPT-2 Small INT8, batch 64, 128-token prompts fed through the decode
+    path, then 128 greedy steps (CUDA-graph replays); tok/s of the generation steps."""
+    cfg = GPT2_SMALL
+    eng = b2.Engine.random(cfg, max_batch=B, seed=SEED)
+    rng = np.random.default_rng(SEED)
+    prompts = [list(map(int, rng.integers(0, cfg["vocab_size"], prompt_len))) for _ in range(B)]
+    eng.start(prompts, steps_new, seed=SEED)
+    st = torch.cuda.current_stream()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(st)
+    eng.run_steps(prompt_len - 1, stream=st)      # positions 0..126: the prompt
+    e1.record(st)
+    eng.run_steps(steps_new, stream=st)           # positions 127..254: 128 generated tokens
+    e2.record(st)
+    torch.cuda.synchronize()
+    assert b2.device_error() == 0
+    gen_ms = e1.elapsed_time(e2)
+    pre_ms = e0.elapsed_time(e1)
+    ctx_mean = prompt_len + (steps_new - 1) / 2.0 + 0.5
+    by = gpt2_step_bytes(cfg, B, ctx_mean)
+    step_s = gen_ms / steps_new * 1e-3
+    toks = eng.tokens()
+    eng.close()
+    return {"tok_s": round(B * steps_new / (gen_ms * 1e-3), 1), "ms_per_step": round(gen_ms / steps_new, 4),
+            "prefill_tok_s": round(B * (prompt_len - 1) / (pre_ms * 1e-3), 1),
+            "step_bytes": int(by), "gbs": round(by / step_s / 1e9, 1),
+            "frac_of_hbm_bound": round(by / step_s / 1e9 / hbm_peak, 4),
+            "hbm_bound_tok_s": round(B / (by / (hbm_peak * 1e9)), 1),
+            "generated_tokens_valid": bool((toks[:, prompt_len:prompt_len + steps_new] >= 0).all()),
+            "timing": "CUDA graph replays of one decode step"}
 
 
 def cpu_baseline(torch, q, kc, vc, bt, lens):
@@ -481,6 +528,12 @@ def run_only(args):
     b2 = importlib.import_module("cuda-llm-inference-engine_b200")
     b2.load_library()
     dev = torch.device("cuda", 0)
+    if args.only == "gpt2":
+        import numpy as np
+
+        r = gpt2_config4(torch, b2, np, measured_peaks()[0], steps_new=max(1, args.steps), prompt_len=128)
+        print(f"gpt2: {json.dumps(r)} (not a bench value)", flush=True)
+        return
     if args.only.startswith("attn"):
         dt = torch.bfloat16 if args.only == "attn_bf16" else torch.float32
         lens, bt, P = workload_meta()
@@ -511,7 +564,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
-    ap.add_argument("--only", default=None, choices=["attn", "attn_bf16", "gemm2048", "gemm8192", "gemm_rect"],
+    ap.add_argument("--only", default=None,
+                    choices=["attn", "attn_bf16", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
                     help="run one workload for a few steps with no JSON line (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -46,7 +46,7 @@ _CXX = {
 # Every symbol include/*.h declares (checked by the CPU tests).
 C_ABI_SYMBOLS = [
     "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_decode_attn_noalloc", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
-    "b2_int8_gemm_s32", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
+    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
 ]
 
 
@@ -91,6 +91,10 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     lib.b2_quantize_fp32_to_int8.restype = i
     lib.b2_int8_gemm.argtypes = [i, i, i, vp, vp, vp, vp, vp, vp, vp, i, vp]
     lib.b2_int8_gemm.restype = i
+    lib.b2_int8_gemm_workspace_size.argtypes = [i, i, i]
+    lib.b2_int8_gemm_workspace_size.restype = sz
+    lib.b2_int8_gemm_ws.argtypes = [i, i, i, vp, vp, vp, vp, vp, vp, vp, i, vp, sz, vp]
+    lib.b2_int8_gemm_ws.restype = i
     lib.b2_int8_gemm_s32.argtypes = [i, i, i, vp, vp, vp, vp]
     lib.b2_int8_gemm_s32.restype = i
     lib.b2_get_device_error.argtypes = [i]
@@ -276,17 +280,34 @@ def quantize_fp32_to_int8(x, out=None, scales=None, stream=None):
 
 
 def int8_gemm(A_packed, BT_packed, scale_A, scale_B, bias=None, residual=None, epilogue=EPI_PLAIN, C=None,
-              stream=None):
+              stream=None, workspace=None):
+    """INT8 GEMM; with ``workspace`` (make_gemm_workspace) skinny shapes are split along K."""
     import torch
 
     M, K4 = A_packed.shape
     N = BT_packed.shape[0]
     if C is None:
         C = torch.empty(M, N, dtype=torch.float32, device=A_packed.device)
-    _check(load_library().b2_int8_gemm(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A), _ptr(scale_B),
-                                       _ptr(bias), _ptr(residual), _ptr(C), epilogue, _stream(stream)),
-           "b2_int8_gemm")
+    lib = load_library()
+    if workspace is None:
+        _check(lib.b2_int8_gemm(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A), _ptr(scale_B),
+                                _ptr(bias), _ptr(residual), _ptr(C), epilogue, _stream(stream)), "b2_int8_gemm")
+    else:
+        _check(lib.b2_int8_gemm_ws(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(scale_A), _ptr(scale_B),
+                                   _ptr(bias), _ptr(residual), _ptr(C), epilogue, _ptr(workspace),
+                                   workspace.numel() * workspace.element_size(), _stream(stream)), "b2_int8_gemm_ws")
     return C
+
+
+def int8_gemm_workspace_size(M, N, K) -> int:
+    return int(load_library().b2_int8_gemm_workspace_size(M, N, K))
+
+
+def make_gemm_workspace(M, N, K, device=None):
+    """Allocates (torch) and zeroes a split-K workspace for ``int8_gemm(..., workspace=...)``."""
+    import torch
+
+    return torch.zeros(max(256, int8_gemm_workspace_size(M, N, K)), dtype=torch.uint8, device=device or "cuda")
 
 
 def int8_gemm_s32(A_packed, BT_packed, C=None, stream=None):

@@ -14,7 +14,9 @@ size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, 
                                   int kv_bytes);
 int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st);
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
-                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st);
+                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
+                void* ws = nullptr, size_t ws_bytes = 0);
+size_t gemm_workspace_size(int M, int N, int K);
 
 constexpr int kMaxDevices = 64;
 constexpr int kMaxSlots = 64;
@@ -91,6 +93,19 @@ int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT
                  b2_stream_t stream) {
     return gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C, epilogue, false,
                        static_cast<cudaStream_t>(stream));
+}
+
+size_t b2_int8_gemm_workspace_size(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return gemm_workspace_size(M, N, K);
+}
+
+int b2_int8_gemm_ws(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, const float* scale_A,
+                    const float* scale_B, const float* bias, const float* residual, float* C, int epilogue,
+                    void* workspace, size_t workspace_bytes, b2_stream_t stream) {
+    if (workspace && ((uintptr_t)workspace & 255)) return B2_ERR_INVALID;
+    return gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C, epilogue, false,
+                       static_cast<cudaStream_t>(stream), workspace, workspace_bytes);
 }
 
 int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, int32_t* C_acc,

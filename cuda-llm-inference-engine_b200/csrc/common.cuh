@@ -115,7 +115,7 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     return p;
 }
 
-// 2-D tiled TMA load (no multicast). c0 is the innermost coordinate (bytes for u8 maps).
+// 2-D tiled TMA load into this CTA's shared memory. c0 is the innermost coordinate (bytes for u8 maps).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
                                             uint32_t bar, uint64_t policy) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"

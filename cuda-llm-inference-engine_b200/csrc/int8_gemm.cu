@@ -119,6 +119,11 @@ struct GemmParams {
     const float* residual;
     void* C;  // float* or int32_t*
     unsigned int* err;
+    // split-K (decode-size GEMMs): k_splits ranges of kb_per_split k-blocks per tile; int32
+    // partials in ws [k_splits][M][N]; counters [tiles] arrival tickets, zero at rest
+    int k_splits, kb_per_split;
+    int32_t* ws;
+    unsigned int* counters;
 };
 
 template <int BN>
@@ -226,6 +231,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     const int m_tiles = (p.M + GM_BM - 1) / GM_BM;
     const int n_tiles = (p.N + BN - 1) / BN;
     const int num_tiles = m_tiles * n_tiles;
+    const int num_units = num_tiles * p.k_splits;  // work unit = (tile, k range)
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&mapA);
@@ -255,10 +261,13 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             // ---------------------------------------------------------------- TMA producer
             const uint64_t pol = policy_evict_last();
             int it = 0;  // k-block counter across all tiles of this CTA
-            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+            for (int w = blockIdx.x; w < num_units && !*abort_flag; w += gridDim.x) {
+                const int t = w / p.k_splits;
+                const int kb0 = (w % p.k_splits) * p.kb_per_split;
+                const int kb1 = min(nk, kb0 + p.kb_per_split);
                 int mt, nt;
                 tile_coords(t, m_tiles, n_tiles, mt, nt);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (it >= C::STAGES) {
                         if (*abort_flag || !mbar_wait(empty_bar(s), ((it / C::STAGES) - 1) & 1, p.err)) {
@@ -280,12 +289,14 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             // ---------------------------------------------------------------- MMA issuer
             constexpr uint32_t idesc = idesc_i8(GM_BM, BN);
             int it = 0, j = 0;  // k-block counter, local tile counter
-            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++j) {
+            for (int w = blockIdx.x; w < num_units && !*abort_flag; w += gridDim.x, ++j) {
+                const int kb0 = (w % p.k_splits) * p.kb_per_split;
+                const int kb1 = min(nk, kb0 + p.kb_per_split);
                 const int a = j & 1, u = j >> 1;
                 if (u >= 1 && !mbar_wait(acce_bar(a), (u - 1) & 1, p.err)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + a * C::ACC_COLS;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (*abort_flag || !mbar_wait(full_bar(s), (it / C::STAGES) & 1, p.err)) {
                         *abort_flag = 1;
@@ -299,7 +310,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
 #pragma unroll
                     for (int k = 0; k < GM_BK / 32; ++k) {
                         // advance 32 bytes of K inside the swizzle atom: +2 in the 16-byte address field
-                        mma_i8(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                        mma_i8(d_tmem, da + 2 * k, db + 2 * k, idesc, ((kb - kb0) | k) != 0 ? 1u : 0u);
                     }
                     mma_commit(empty_bar(s));  // ring slot free once these MMAs have read it
                 }
@@ -314,7 +325,9 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         float* sB_s = reinterpret_cast<float*>(smem + C::OFF_COL);
         float* bias_s = sB_s + BN;
         int j = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
+        for (int w = blockIdx.x; w < num_units; w += gridDim.x, ++j) {
+            const int t = w / p.k_splits;
+            const int ksi = w % p.k_splits;
             const int a = j & 1, u = j >> 1;
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, mt, nt);
@@ -335,8 +348,8 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             const bool row_ok = ok && row < p.M;
             const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
             const uint32_t tbase = tmem + a * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
-#pragma unroll 1
-            for (int c = 0; c < BN / 16; c += 2) {
+            // final dequantise/epilogue/store of columns [n, n+32) from accumulators r0, r1
+            auto finish32 = [&](const uint32_t (&r0)[16], const uint32_t (&r1)[16], int c) {
                 const int n = nt * BN + c * 16;
                 float rs0[16], rs1[16];
 #pragma unroll
@@ -345,17 +358,112 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     if (row_ok && n < p.N) load_res16(p, row, n, rs0);
                     if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
                 }
-                uint32_t r0[16], r1[16];
-                tmem_ld16(tbase + (uint32_t)(c * 16), r0);
-                tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
-                tmem_ld_wait();
                 if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
                 if (row_ok && n + 16 < p.N)
                     store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
+            };
+            if (p.k_splits == 1) {
+#pragma unroll 1
+                for (int c = 0; c < BN / 16; c += 2) {
+                    uint32_t r0[16], r1[16];
+                    tmem_ld16(tbase + (uint32_t)(c * 16), r0);
+                    tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
+                    tmem_ld_wait();
+                    finish32(r0, r1, c);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
+            } else {
+                // split-K: park this k range's int32 partial, then the last of the k_splits
+                // arrivals for these 32 rows sums the partials (exact) and runs the epilogue
+                int32_t* part = p.ws + (size_t)ksi * p.M * p.N;
+#pragma unroll 1
+                for (int c = 0; c < BN / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tbase + (uint32_t)(c * 16), r);
+                    tmem_ld_wait();
+                    const int n = nt * BN + c * 16;
+                    if (row_ok && n < p.N) {
+                        int32_t* dst = part + (size_t)row * p.N + n;
+                        if (n + 16 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+                            for (int q = 0; q < 16; q += 4)
+                                __stcg(reinterpret_cast<int4*>(dst + q), make_int4(r[q], r[q + 1], r[q + 2], r[q + 3]));
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q)
+                                if (n + q < p.N) __stcg(dst + q, (int32_t)r[q]);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acce_bar(a));  // TMEM read out: accumulator a is free
+                __threadfence();
+                named_barrier(2, 128);  // all four warps have parked their rows
+                volatile uint32_t* tk = tmem_slot + 2;
+                unsigned int* ctr = p.counters + t;
+                if (et == 0) *tk = atomicAdd(ctr, 1u);
+                named_barrier(2, 128);
+                if (*tk == (unsigned)(p.k_splits - 1)) {
+                    // last k range of this tile: the 128 epilogue threads sum the partials with
+                    // coalesced 16-byte loads (k ranges unrolled 4 deep) and run the epilogue
+                    __threadfence();
+                    const int r0 = mt * GM_BM;
+                    const int rows = min(GM_BM, p.M - r0);
+                    constexpr int C4 = BN / 4;
+                    const bool vec = (p.N & 3) == 0;
+                    for (int u = et; u < rows * C4; u += 128) {
+                        const int row_i = r0 + u / C4;
+                        const int cl = (u % C4) * 4;
+                        const int n = nt * BN + cl;
+                        if (n >= p.N) continue;
+                        int acc4[4] = {0, 0, 0, 0};
+                        const int32_t* src = p.ws + (size_t)row_i * p.N + n;
+                        const size_t kstride = (size_t)p.M * p.N;
+                        if (vec) {
+                            int ks = 0;
+                            for (; ks + 4 <= p.k_splits; ks += 4) {
+                                int4 v[4];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) v[q] = __ldcg(reinterpret_cast<const int4*>(src + (ks + q) * kstride));
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    acc4[0] += v[q].x; acc4[1] += v[q].y; acc4[2] += v[q].z; acc4[3] += v[q].w;
+                                }
+                            }
+                            for (; ks < p.k_splits; ++ks) {
+                                const int4 v = __ldcg(reinterpret_cast<const int4*>(src + ks * kstride));
+                                acc4[0] += v.x; acc4[1] += v.y; acc4[2] += v.z; acc4[3] += v.w;
+                            }
+                        } else {
+                            for (int ks = 0; ks < p.k_splits; ++ks)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    if (n + q < p.N) acc4[q] += __ldcg(src + ks * kstride + q);
+                        }
+                        const float sa_i = __ldg(p.scale_A + row_i);
+                        float* Crow = static_cast<float*>(p.C) + (size_t)row_i * p.N;
+                        float o[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            if (n + q < p.N) {
+                                const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? p.residual[(size_t)row_i * p.N + n + q] : 0.f;
+                                o[q] = epilogue<EPI>(acc4[q], sa_i, sB_s[cl + q], EPI != B2_EPI_PLAIN ? bias_s[cl + q] : 0.f, rs);
+                            }
+                        }
+                        if (vec && n + 4 <= p.N) {
+                            *reinterpret_cast<float4*>(Crow + n) = make_float4(o[0], o[1], o[2], o[3]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                if (n + q < p.N) Crow[n + q] = o[q];
+                        }
+                    }
+                    if (et == 0) *ctr = 0u;  // every k range has arrived: reusable
+                }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
             named_barrier(2, 128);  // staged columns are free for the next tile
         }
     }
@@ -457,13 +565,36 @@ static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, c
     auto kfn = int8_gemm_tc_kernel<BN, EPI, S32>;
     if (!set_smem_attr_once((const void*)kfn, C::SMEM, slot)) return B2_ERR_CUDA;
     const int tiles = ((p.N + BN - 1) / BN) * ((p.M + GM_BM - 1) / GM_BM);
-    const int grid = std::min(tiles, num_sms_current_device());
+    const int grid = std::min(tiles * p.k_splits, num_sms_current_device());
     kfn<<<grid, GM_THREADS, C::SMEM, st>>>(ma, mb, p);
     return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
+// Split-K plan for GEMMs whose tiles cannot fill the GPU (decode: M = batch <= 128): the
+// workspace holds [tiles] u32 tickets (zero at rest), then [k_splits][M][N] int32 partials.
+static void plan_split(GemmParams& p, int tiles, void* ws, size_t ws_bytes, int sms) {
+    p.k_splits = 1;
+    p.kb_per_split = (p.K + GM_BK - 1) / GM_BK;
+    p.ws = nullptr;
+    p.counters = nullptr;
+    const int nk = p.kb_per_split;
+    if (!ws || tiles >= sms || nk < 2) return;
+    int ks = std::min(std::min(nk, sms / std::max(1, tiles)), 32);
+    if (ks < 2) return;
+    const int kbps = (nk + ks - 1) / ks;
+    ks = (nk + kbps - 1) / kbps;
+    const size_t ctr_bytes = (((size_t)tiles * sizeof(unsigned int)) + 255) & ~(size_t)255;
+    const size_t need = ctr_bytes + (size_t)ks * p.M * p.N * sizeof(int32_t);
+    if (ks < 2 || need > ws_bytes) return;
+    p.k_splits = ks;
+    p.kb_per_split = kbps;
+    p.counters = static_cast<unsigned int*>(ws);
+    p.ws = reinterpret_cast<int32_t*>(static_cast<char*>(ws) + ctr_bytes);
+}
+
 template <int EPI, bool S32>
-static int gemm_dispatch(const GemmParams& p, const int32_t* A, const int32_t* BT, cudaStream_t st) {
+static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, void* ws, size_t ws_bytes,
+                         cudaStream_t st) {
     // K == 0 (empty contraction, acc = 0) and K % 16 != 0 take the SIMT kernel
     if (p.K == 0 || (p.K & 15) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)BT & 15)) {
         dim3 grid((p.N + 255) / 256, p.M);
@@ -471,16 +602,36 @@ static int gemm_dispatch(const GemmParams& p, const int32_t* A, const int32_t* B
         return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
     }
     const int sms = num_sms_current_device();
-    const long long mt = (p.M + GM_BM - 1) / GM_BM;
-    // widest tile that still gives every SM a tile; otherwise the narrowest
+    const int mt = (p.M + GM_BM - 1) / GM_BM;
+    // widest tile that still gives every SM a tile; otherwise the narrowest, split along K
     const int slot_base = (EPI + (S32 ? 4 : 0)) * 3;
-    if (mt * ((p.N + 255) / 256) >= sms) return launch_tc<256, EPI, S32>(p, A, BT, st, slot_base + 0);
-    if (mt * ((p.N + 127) / 128) >= sms) return launch_tc<128, EPI, S32>(p, A, BT, st, slot_base + 1);
+    const int t256 = mt * ((p.N + 255) / 256), t128 = mt * ((p.N + 127) / 128), t64 = mt * ((p.N + 63) / 64);
+    if (t256 >= sms) {
+        plan_split(p, t256, nullptr, 0, sms);
+        return launch_tc<256, EPI, S32>(p, A, BT, st, slot_base + 0);
+    }
+    if (t128 >= sms) {
+        plan_split(p, t128, nullptr, 0, sms);
+        return launch_tc<128, EPI, S32>(p, A, BT, st, slot_base + 1);
+    }
+    plan_split(p, t64, S32 ? nullptr : ws, ws_bytes, sms);  // the raw-int32 view is never split
     return launch_tc<64, EPI, S32>(p, A, BT, st, slot_base + 2);
 }
 
+// Workspace bytes that let gemm_launch split K for these shapes (0 when it would not split).
+size_t gemm_workspace_size(int M, int N, int K) {
+    const int sms = num_sms_current_device();
+    const int mt = (M + GM_BM - 1) / GM_BM;
+    const int tiles = mt * ((N + 63) / 64);
+    const int nk = (K + GM_BK - 1) / GM_BK;
+    if (mt * ((N + 127) / 128) >= sms || tiles >= sms || nk < 2) return 0;
+    const size_t ctr_bytes = (((size_t)tiles * sizeof(unsigned int)) + 255) & ~(size_t)255;
+    return ctr_bytes + (size_t)std::min(std::min(nk, sms / std::max(1, tiles)), 32) * M * N * sizeof(int32_t);
+}
+
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
-                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st) {
+                const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
+                void* ws, size_t ws_bytes) {
     if (M < 0 || N < 0 || K < 0 || (K & 3)) return B2_ERR_INVALID;
     if (M == 0 || N == 0) return B2_OK;
     if (!A || !BT || !C) return B2_ERR_INVALID;
@@ -490,13 +641,13 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
         if (epi != B2_EPI_PLAIN && !bias) return B2_ERR_INVALID;
         if (epi == B2_EPI_BIAS_RESIDUAL && !residual) return B2_ERR_INVALID;
     }
-    GemmParams p{M, N, K, sA, sB, bias, residual, C, device_error_ptr()};
-    if (s32) return gemm_dispatch<B2_EPI_PLAIN, true>(p, A, BT, st);
+    GemmParams p{M, N, K, sA, sB, bias, residual, C, device_error_ptr(), 1, 0, nullptr, nullptr};
+    if (s32) return gemm_dispatch<B2_EPI_PLAIN, true>(p, A, BT, ws, ws_bytes, st);
     switch (epi) {
-        case B2_EPI_PLAIN: return gemm_dispatch<B2_EPI_PLAIN, false>(p, A, BT, st);
-        case B2_EPI_BIAS: return gemm_dispatch<B2_EPI_BIAS, false>(p, A, BT, st);
-        case B2_EPI_BIAS_GELU: return gemm_dispatch<B2_EPI_BIAS_GELU, false>(p, A, BT, st);
-        default: return gemm_dispatch<B2_EPI_BIAS_RESIDUAL, false>(p, A, BT, st);
+        case B2_EPI_PLAIN: return gemm_dispatch<B2_EPI_PLAIN, false>(p, A, BT, ws, ws_bytes, st);
+        case B2_EPI_BIAS: return gemm_dispatch<B2_EPI_BIAS, false>(p, A, BT, ws, ws_bytes, st);
+        case B2_EPI_BIAS_GELU: return gemm_dispatch<B2_EPI_BIAS_GELU, false>(p, A, BT, ws, ws_bytes, st);
+        default: return gemm_dispatch<B2_EPI_BIAS_RESIDUAL, false>(p, A, BT, ws, ws_bytes, st);
     }
 }
 

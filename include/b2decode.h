@@ -128,6 +128,21 @@ int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT
                  const float* scale_A, const float* scale_B, const float* bias,
                  const float* residual, float* C, int epilogue, b2_stream_t stream);
 
+/* Bytes of workspace that let b2_int8_gemm_ws split the K dimension across CTAs for shapes
+ * whose output tiles cannot fill the GPU (decode: M = batch); 0 when it would not split.
+ * No counterpart in the reference (its dp4a kernel has a fixed 64x64 tile grid). */
+size_t b2_int8_gemm_workspace_size(int M, int N, int K);
+
+/* b2_int8_gemm with a caller workspace for split-K: each CTA contracts a K range into
+ * exact int32 partials, and the last CTA of each tile sums them and runs the epilogue, so
+ * results are bit-identical to b2_int8_gemm. The workspace must be zeroed once before first
+ * use; every call leaves its arrival counters zero again. Calls sharing a workspace must not
+ * overlap on the GPU. */
+int b2_int8_gemm_ws(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                    const float* scale_A, const float* scale_B, const float* bias,
+                    const float* residual, float* C, int epilogue, void* workspace,
+                    size_t workspace_bytes, b2_stream_t stream);
+
 /* Raw int32 accumulators C_acc[M,N] = sum_k A[m,k] * BT[n,k] (no dequantisation): the
  * bit-exact view of the contraction inside the reference's int8_gemm_dp4a_kernel
  * (kernels/quantization/14_int8_gemm.cu:96-140), which the reference never exposes. */

@@ -151,3 +151,40 @@ def test_gemm_invalid_args(b2, cuda):
         b2.int8_gemm(A, A, s, s, epilogue=b2.EPI_BIAS)  # bias missing
     with pytest.raises(b2.B2Error, match="invalid"):
         b2.int8_gemm(A, A, s, s, torch.zeros(4, device=cuda), epilogue=b2.EPI_BIAS_RESIDUAL)
+
+
+SPLIT_SHAPES = [(64, 768, 3072), (64, 2304, 768), (64, 3072, 768), (1, 768, 3072), (128, 768, 4096),
+                (100, 200, 1024), (3, 50, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K", SPLIT_SHAPES)
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_gemm_split_k_bit_exact(b2, oracle, cuda, M, N, K, epi):
+    """Split-K (workspace) path: int32 partials summed exactly, so the output equals the
+    unsplit kernel bit for bit and the oracle as in test_gemm_epilogues; repeated calls reuse
+    the workspace (its tickets return to zero)."""
+    import torch
+
+    assert b2.int8_gemm_workspace_size(M, N, K) > 0
+    rng = np.random.default_rng(M * 7 + N + K + epi)
+    A, Bt = quantized_pair(rng, M, N, K)
+    Ap, sA = oracle.quantize(A)
+    Bp, sB = oracle.quantize(Bt)
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    want = oracle.epilogue(oracle.int8_gemm_s32(Ap, Bp, nthreads=0), sA, sB, bias, res, epi)
+    t = {k: dev(torch, v, cuda) for k, v in dict(Ap=Ap, Bp=Bp, sA=sA, sB=sB, bias=bias, res=res).items()}
+    ws = b2.make_gemm_workspace(M, N, K, device=cuda)
+    args = (t["Ap"], t["Bp"], t["sA"], t["sB"], t["bias"] if epi else None, t["res"] if epi == 3 else None)
+    plain = b2.int8_gemm(*args, epilogue=epi)
+    for _ in range(2):
+        got = b2.int8_gemm(*args, epilogue=epi, workspace=ws)
+        torch.cuda.synchronize()
+        assert b2.device_error() == 0
+        assert torch.equal(got, plain)
+    g = got.cpu().numpy()
+    if epi == 2:
+        np.testing.assert_allclose(g, want, rtol=1e-4, atol=1e-6)
+    else:
+        np.testing.assert_array_equal(g.view(np.uint32), want.view(np.uint32))
+    assert int(ws[:256].view(torch.int32).abs().sum()) == 0  # tickets back to zero
