@@ -59,6 +59,11 @@ unsigned int* device_error_ptr() {
     return cache[dev];
 }
 
+bool& pdl_enabled() {
+    static thread_local bool on = false;
+    return on;
+}
+
 constexpr int kAbiMaxSplits = 64;
 // The reference workspace holds DA_MAX_SPLITS rows per head; the drop-in wrapper keeps one
 // row's worth for the arrival counters.

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <cuda.h>
 #include <cstdint>
+#include <utility>
 #include "b2decode.h"
 
 #ifndef B2_WAIT_NS
@@ -234,6 +235,38 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while the previous
+// kernel on the stream is still running. Everything before griddep_wait() must touch only
+// data the previous kernel does not write (constant weights, this CTA's shared memory);
+// griddep_wait() returns once the previous grid has completed and its writes are visible.
+// griddep_launch() lets the next such kernel start; kernels here issue it after their wait,
+// so a kernel starting early can rely on every grid before its predecessor being complete.
+// Both are no-ops for a kernel launched normally.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: whether launches made by this thread use programmatic dependent launch (set by the
+// decode engine around its step, whose data dependencies it knows).
+bool& pdl_enabled();
+
+// Host: launch `kern` on `st`, with programmatic stream serialisation when pdl_enabled().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // Host: address of the device error word on the current device (cached per device).

@@ -156,6 +156,8 @@ decode_attn_kernel(const DecodeAttnParams p) {
     const int warp = tid >> 5;
     const int lane = tid & 31;
 
+    griddep_wait();
+    griddep_launch();
     // ---- this CTA's token range (whole blocks, as the reference splits, 13_decode_attn.cu:63-65)
     int ctx = p.context_lens[b];
     const int cap = p.num_blocks_per_seq * p.block_size;
@@ -490,8 +492,7 @@ static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int B, cuda
     constexpr int slot = 32 + (G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3) + (D == 64 ? 0 : 4) + (sizeof(KV) == 4 ? 0 : 8);
     if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV>, C::SMEM, slot)) return cudaErrorInvalidValue;
     dim3 grid(prm.num_splits, prm.H_kv, B);
-    decode_attn_kernel<G, D, KV><<<grid, DA_NT, C::SMEM, st>>>(prm);
-    return cudaGetLastError();
+    return launch_kernel(decode_attn_kernel<G, D, KV>, grid, dim3(DA_NT), (size_t)C::SMEM, st, prm);
 }
 
 template <int D, typename KV>

@@ -93,8 +93,6 @@ struct b2_engine {
     float* xs = nullptr;
     void* attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
-    void* gemm_ws = nullptr;  // split-K partials + tickets, shared by the step's sequential GEMMs
-    size_t gemm_ws_bytes = 0;
     // CUDA graph of one step
     cudaGraphExec_t graph = nullptr;
     bool graph_dirty = true;
@@ -159,14 +157,9 @@ int alloc_runtime(b2_engine* e) {
     e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, c.n_heads, c.n_heads, c.d_head,
                                                                          c.max_seq_len, kBlock, 64, 4));
     e->attn_ws = e->alloc<unsigned char>(e->attn_ws_bytes);
-    e->gemm_ws_bytes = 256;
-    e->gemm_ws_bytes = std::max({e->gemm_ws_bytes, gemm_workspace_size(B, 3 * d, d), gemm_workspace_size(B, d, d),
-                                 gemm_workspace_size(B, c.d_ff, d), gemm_workspace_size(B, d, c.d_ff)});
-    e->gemm_ws = e->alloc<unsigned char>(e->gemm_ws_bytes);
     if (e->failed) return B2_ERR_CUDA;
     if (!e->k_pool || !e->v_pool || !e->attn_ws || !e->logits) return B2_ERR_CUDA;
     if (cudaMemset(e->attn_ws, 0, e->attn_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
-    if (cudaMemset(e->gemm_ws, 0, e->gemm_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
     if (cudaMemset(e->k_pool, 0, pool_bytes) != cudaSuccess || cudaMemset(e->v_pool, 0, pool_bytes) != cudaSuccess)
         return B2_ERR_CUDA;
     e->free_blocks.resize(e->num_blocks);
@@ -278,7 +271,16 @@ std::string layer_dir(const std::string& root, int i) {
 namespace {
 
 // One decode step: a fixed sequence of launches on `st` (capturable as a CUDA graph).
+// Enables programmatic dependent launch for the launches of one decode step: every kernel in
+// the step reads only constant weights before its griddep_wait().
+struct PdlScope {
+    bool saved;
+    PdlScope() : saved(pdl_enabled()) { pdl_enabled() = true; }
+    ~PdlScope() { pdl_enabled() = saved; }
+};
+
 int enqueue_step(b2_engine* e, cudaStream_t st) {
+    PdlScope pdl;
     const b2_gpt2_config& c = e->cfg;
     const int B = e->batch, d = c.d_model, ff = c.d_ff, H = c.n_heads, dh = c.d_head;
     const size_t kvb = e->kv_dtype == B2_KV_F32 ? 4 : 2;
@@ -292,7 +294,7 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         // attention sub-block (pre-norm; x stays the residual and is updated in place)
         B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
         B2_TRY(gemm_launch(B, 3 * d, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
-                           false, st, e->gemm_ws, e->gemm_ws_bytes));
+                           false, st));
         B2_TRY(launch_qkv_scatter(B, d, H, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
                                   vc, e->kv_dtype, st));
         b2_decode_attn_args a{};
@@ -305,14 +307,14 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         B2_TRY(decode_attn_launch(&a, 64, true, st));
         B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
         B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
-                           false, st, e->gemm_ws, e->gemm_ws_bytes));
+                           false, st));
         // MLP sub-block
         B2_TRY(launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st));
         B2_TRY(gemm_launch(B, ff, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
-                           false, st, e->gemm_ws, e->gemm_ws_bytes));
+                           false, st));
         B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
         B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
-                           B2_EPI_BIAS_RESIDUAL, false, st, e->gemm_ws, e->gemm_ws_bytes));
+                           B2_EPI_BIAS_RESIDUAL, false, st));
     }
     B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, e->xf, st));
     B2_TRY(launch_vocab_argmax(B, c.vocab_size, d, e->xf, e->wte, e->keep_logits ? e->logits : nullptr, e->keys, st));

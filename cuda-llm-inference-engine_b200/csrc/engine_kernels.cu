@@ -26,6 +26,8 @@ namespace b2 {
 __global__ void embed_kernel(int d, const int* __restrict__ tokens, const int* __restrict__ pos,
                              const float* __restrict__ wte, const float* __restrict__ wpe, float* __restrict__ x,
                              int* __restrict__ ctx_lens, unsigned long long* __restrict__ argmax_keys) {
+    griddep_wait();
+    griddep_launch();
     const int b = blockIdx.x;
     const int tok = tokens[b];
     const int p = pos[b];
@@ -60,6 +62,8 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
                 const float* __restrict__ beta, float eps, int32_t* __restrict__ q_out,
                 float* __restrict__ scale_out, float* __restrict__ y_out) {
     __shared__ float red[LNQ_THREADS / 32];
+    griddep_wait();
+    griddep_launch();
     const int row = blockIdx.x;
     const float* xr = x + (size_t)row * cols;
     float v[LNQ_MAX_PER_THREAD];
@@ -125,6 +129,8 @@ template <typename KV>
 __global__ void qkv_scatter_kernel(int d, int H, int dh, int block_size, int nbps, const float* __restrict__ qkv,
                                    const int* __restrict__ pos, const int* __restrict__ block_table,
                                    float* __restrict__ q, KV* __restrict__ k_cache, KV* __restrict__ v_cache) {
+    griddep_wait();
+    griddep_launch();
     const int b = blockIdx.x;
     const int p = pos[b];
     const int phys = block_table[(size_t)b * nbps + p / block_size];
@@ -155,6 +161,8 @@ vocab_argmax_kernel(int B, int V, int d, const float* __restrict__ h, const floa
     __shared__ float hs[VP_TK][VP_TB + 4];
     __shared__ float ws[VP_TK][VP_TV + 4];
     __shared__ unsigned long long best[VP_TB];
+    griddep_wait();
+    griddep_launch();
     const int v0 = blockIdx.x * VP_TV;
     const int b0 = blockIdx.y * VP_TB;
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // 16 x 16 threads, 4 x 4 outputs each
@@ -205,6 +213,8 @@ vocab_argmax_kernel(int B, int V, int d, const float* __restrict__ h, const floa
 __global__ void advance_kernel(int B, const unsigned long long* __restrict__ keys, int* __restrict__ tokens,
                                int* __restrict__ pos, const int* __restrict__ forced, const int* __restrict__ forced_len,
                                int forced_stride, int* __restrict__ out_tokens, int out_stride, int max_pos) {
+    griddep_wait();
+    griddep_launch();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const int next = (int)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull));
@@ -219,42 +229,50 @@ __global__ void advance_kernel(int B, const unsigned long long* __restrict__ key
 // ------------------------------------------------------------------ launchers
 int launch_embed(int B, int d, const int* tokens, const int* pos, const float* wte, const float* wpe, float* x,
                  int* ctx_lens, unsigned long long* keys, cudaStream_t st) {
-    embed_kernel<<<B, 256, 0, st>>>(d, tokens, pos, wte, wpe, x, ctx_lens, keys);
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return launch_kernel(embed_kernel, dim3(B), dim3(256), 0, st, d, tokens, pos, wte, wpe, x, ctx_lens, keys) ==
+                   cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
 }
 
 int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
                     int32_t* q, float* scale, float* y, cudaStream_t st) {
     if (cols > LNQ_THREADS * LNQ_MAX_PER_THREAD || (cols & 3)) return B2_ERR_UNSUPPORTED;
-    ln_quant_kernel<<<rows, LNQ_THREADS, 0, st>>>(cols, x, gamma, beta, eps, q, scale, y);
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return launch_kernel(ln_quant_kernel, dim3(rows), dim3(LNQ_THREADS), 0, st, cols, x, gamma, beta, eps, q, scale,
+                         y) == cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
 }
 
 int launch_qkv_scatter(int B, int d, int H, int dh, int block_size, int nbps, const float* qkv, const int* pos,
                        const int* block_table, float* q, void* k_cache, void* v_cache, int kv_dtype, cudaStream_t st) {
+    cudaError_t e;
     if (kv_dtype == B2_KV_F32)
-        qkv_scatter_kernel<float><<<B, 256, 0, st>>>(d, H, dh, block_size, nbps, qkv, pos, block_table, q,
-                                                     static_cast<float*>(k_cache), static_cast<float*>(v_cache));
+        e = launch_kernel(qkv_scatter_kernel<float>, dim3(B), dim3(256), 0, st, d, H, dh, block_size, nbps, qkv, pos,
+                          block_table, q, static_cast<float*>(k_cache), static_cast<float*>(v_cache));
     else
-        qkv_scatter_kernel<__nv_bfloat16><<<B, 256, 0, st>>>(d, H, dh, block_size, nbps, qkv, pos, block_table, q,
-                                                             static_cast<__nv_bfloat16*>(k_cache),
-                                                             static_cast<__nv_bfloat16*>(v_cache));
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+        e = launch_kernel(qkv_scatter_kernel<__nv_bfloat16>, dim3(B), dim3(256), 0, st, d, H, dh, block_size, nbps,
+                          qkv, pos, block_table, q, static_cast<__nv_bfloat16*>(k_cache),
+                          static_cast<__nv_bfloat16*>(v_cache));
+    return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
 int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, float* logits,
                         unsigned long long* keys, cudaStream_t st) {
     dim3 grid((V + VP_TV - 1) / VP_TV, (B + VP_TB - 1) / VP_TB);
-    vocab_argmax_kernel<<<grid, VP_THREADS, 0, st>>>(B, V, d, h, wte, logits, keys);
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return launch_kernel(vocab_argmax_kernel, grid, dim3(VP_THREADS), 0, st, B, V, d, h, wte, logits, keys) ==
+                   cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
 }
 
 int launch_advance(int B, const unsigned long long* keys, int* tokens, int* pos, const int* forced,
                    const int* forced_len, int forced_stride, int* out_tokens, int out_stride, int max_pos,
                    cudaStream_t st) {
-    advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(B, keys, tokens, pos, forced, forced_len, forced_stride,
-                                                     out_tokens, out_stride, max_pos);
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return launch_kernel(advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, B, keys, tokens, pos, forced,
+                         forced_len, forced_stride, out_tokens, out_stride, max_pos) == cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
 }
 
 }  // namespace b2

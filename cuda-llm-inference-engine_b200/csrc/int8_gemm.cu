@@ -33,6 +33,8 @@ constexpr int QZ_THREADS = 256;
 __global__ void __launch_bounds__(QZ_THREADS)
 quantize_rows_kernel(int cols, const float* __restrict__ in, int32_t* __restrict__ out,
                      float* __restrict__ scales) {
+    griddep_wait();
+    griddep_launch();
     const int row = blockIdx.x;
     const float* x = in + (size_t)row * cols;
     const int c4 = cols >> 2;
@@ -80,8 +82,10 @@ int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* sc
     if (rows < 0 || cols < 0 || (cols & 3)) return B2_ERR_INVALID;
     if (rows == 0) return B2_OK;
     if (!in || !out || !scales) return B2_ERR_INVALID;
-    quantize_rows_kernel<<<rows, QZ_THREADS, 0, st>>>(cols, in, out, scales);
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return launch_kernel(quantize_rows_kernel, dim3(rows), dim3(QZ_THREADS), 0, st, cols, in, out, scales) ==
+                   cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
 }
 
 // ------------------------------------------------------------------ epilogue math
@@ -260,6 +264,25 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         if (lane == 0) {
             // ---------------------------------------------------------------- TMA producer
             const uint64_t pol = policy_evict_last();
+            // The weights (B) never depend on the previous kernel: the first ring stages'
+            // B tiles are requested before waiting on it (programmatic dependent launch),
+            // the activation (A) tiles after.
+            int npre = 0;
+            if ((int)blockIdx.x < num_units) {
+                const int w = blockIdx.x;
+                const int kb0 = (w % p.k_splits) * p.kb_per_split;
+                const int kb1 = min(nk, kb0 + p.kb_per_split);
+                int mt, nt;
+                tile_coords(w / p.k_splits, m_tiles, n_tiles, mt, nt);
+                npre = min(C::STAGES, kb1 - kb0);
+                for (int i = 0; i < npre; ++i) {
+                    const uint32_t b_s = sbase + i * C::STAGE + C::A_BYTES;
+                    mbar_arrive_expect_tx(full_bar(i), C::STAGE);
+                    tma_load_2d(b_s, &mapB, (kb0 + i) * GM_BK, nt * BN, full_bar(i), pol);
+                }
+            }
+            griddep_wait();
+            griddep_launch();
             int it = 0;  // k-block counter across all tiles of this CTA
             for (int w = blockIdx.x; w < num_units && !*abort_flag; w += gridDim.x) {
                 const int t = w / p.k_splits;
@@ -269,14 +292,18 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                 tile_coords(t, m_tiles, n_tiles, mt, nt);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % C::STAGES;
+                    const uint32_t a_s = sbase + s * C::STAGE;
+                    const uint32_t b_s = a_s + C::A_BYTES;
+                    if (it < npre) {  // B already requested
+                        tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
+                        continue;
+                    }
                     if (it >= C::STAGES) {
                         if (*abort_flag || !mbar_wait(empty_bar(s), ((it / C::STAGES) - 1) & 1, p.err)) {
                             *abort_flag = 1;
                             break;
                         }
                     }
-                    const uint32_t a_s = sbase + s * C::STAGE;
-                    const uint32_t b_s = a_s + C::A_BYTES;
                     mbar_arrive_expect_tx(full_bar(s), C::STAGE);
                     tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
                     tma_load_2d(b_s, &mapB, kb * GM_BK, nt * BN, full_bar(s), pol);
@@ -322,6 +349,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         // -------------------------------------------------------------------- epilogue
         const int quad = warp & 3;  // TMEM lane quadrant this warp may access
         const int et = threadIdx.x - 64;  // 0..127 across the epilogue warps
+        griddep_wait();                   // scale_A / residual may come from the previous kernel
         float* sB_s = reinterpret_cast<float*>(smem + C::OFF_COL);
         float* bias_s = sB_s + BN;
         int j = 0;
@@ -481,6 +509,8 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
 template <int EPI, bool S32>
 __global__ void __launch_bounds__(256)
 int8_gemm_simt_kernel(const int32_t* __restrict__ A, const int32_t* __restrict__ BT, const GemmParams p) {
+    griddep_wait();
+    griddep_launch();
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int m = blockIdx.y;
     if (n >= p.N) return;
@@ -566,8 +596,9 @@ static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, c
     if (!set_smem_attr_once((const void*)kfn, C::SMEM, slot)) return B2_ERR_CUDA;
     const int tiles = ((p.N + BN - 1) / BN) * ((p.M + GM_BM - 1) / GM_BM);
     const int grid = std::min(tiles * p.k_splits, num_sms_current_device());
-    kfn<<<grid, GM_THREADS, C::SMEM, st>>>(ma, mb, p);
-    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return launch_kernel(kfn, dim3(grid), dim3(GM_THREADS), (size_t)C::SMEM, st, ma, mb, p) == cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
 }
 
 // Split-K plan for GEMMs whose tiles cannot fill the GPU (decode: M = batch <= 128): the
@@ -598,8 +629,9 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
     // K == 0 (empty contraction, acc = 0) and K % 16 != 0 take the SIMT kernel
     if (p.K == 0 || (p.K & 15) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)BT & 15)) {
         dim3 grid((p.N + 255) / 256, p.M);
-        int8_gemm_simt_kernel<EPI, S32><<<grid, 256, 0, st>>>(A, BT, p);
-        return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+        return launch_kernel(int8_gemm_simt_kernel<EPI, S32>, grid, dim3(256), 0, st, A, BT, p) == cudaSuccess
+                   ? B2_OK
+                   : B2_ERR_CUDA;
     }
     const int sms = num_sms_current_device();
     const int mt = (p.M + GM_BM - 1) / GM_BM;
