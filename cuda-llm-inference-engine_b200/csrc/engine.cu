@@ -89,6 +89,8 @@ struct b2_engine {
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *hbuf = nullptr, *xf = nullptr;
     float* logits = nullptr;
     bool keep_logits = false;
+    void *wte_hi = nullptr, *wte_lo = nullptr;  // bf16 halves of wte for the tensor-core vocab projection
+    void *xf_hi = nullptr, *xf_lo = nullptr;    // bf16 halves of the final hidden state
     int32_t* xq = nullptr;
     float* xs = nullptr;
     void* attn_ws = nullptr;
@@ -154,6 +156,10 @@ int alloc_runtime(b2_engine* e) {
     e->logits = e->alloc<float>((size_t)B * c.vocab_size);
     e->xq = e->alloc<int32_t>((size_t)B * std::max(d, c.d_ff) / 4);
     e->xs = e->alloc<float>(B);
+    e->wte_hi = e->alloc<uint16_t>((size_t)c.vocab_size * d);
+    e->wte_lo = e->alloc<uint16_t>((size_t)c.vocab_size * d);
+    e->xf_hi = e->alloc<uint16_t>((size_t)B * d);
+    e->xf_lo = e->alloc<uint16_t>((size_t)B * d);
     e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, c.n_heads, c.n_heads, c.d_head,
                                                                          c.max_seq_len, kBlock, 64, 4));
     e->attn_ws = e->alloc<unsigned char>(e->attn_ws_bytes);
@@ -316,8 +322,10 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
                            B2_EPI_BIAS_RESIDUAL, false, st));
     }
-    B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, e->xf, st));
-    B2_TRY(launch_vocab_argmax(B, c.vocab_size, d, e->xf, e->wte, e->keep_logits ? e->logits : nullptr, e->keys, st));
+    B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
+                           e->xf_lo));
+    B2_TRY(launch_vocab_bf16x3(B, c.vocab_size, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
+                               e->keep_logits ? e->logits : nullptr, e->keys, st));
     B2_TRY(launch_advance(B, e->keys, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
                           e->out_stride, c.max_seq_len, st));
 #undef B2_TRY
@@ -325,7 +333,9 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
 }
 
 int finish_create(b2_engine* e, b2_engine** out) {
-    if (cudaDeviceSynchronize() != cudaSuccess) {
+    // bf16 hi/lo halves of the tied embedding for the tensor-core vocab projection
+    if (launch_split_bf16(e->wte, e->wte_hi, e->wte_lo, (size_t)e->cfg.vocab_size * e->cfg.d_model, 0) != B2_OK ||
+        cudaDeviceSynchronize() != cudaSuccess) {
         delete e;
         return B2_ERR_CUDA;
     }

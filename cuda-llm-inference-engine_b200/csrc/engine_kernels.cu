@@ -60,7 +60,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(LNQ_THREADS)
 ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__ gamma,
                 const float* __restrict__ beta, float eps, int32_t* __restrict__ q_out,
-                float* __restrict__ scale_out, float* __restrict__ y_out) {
+                float* __restrict__ scale_out, float* __restrict__ y_out, __nv_bfloat16* __restrict__ y_hi,
+                __nv_bfloat16* __restrict__ y_lo) {
     __shared__ float red[LNQ_THREADS / 32];
     griddep_wait();
     griddep_launch();
@@ -87,11 +88,18 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
             amax = fmaxf(amax, fabsf(v[k]));
         }
     }
-    if (!q_out) {  // plain LayerNorm (final ln_f feeding the fp32 vocab projection)
+    if (!q_out) {  // plain LayerNorm (final ln_f feeding the vocab projection), fp32 and/or bf16 hi/lo
 #pragma unroll
         for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
             const int c = threadIdx.x + k * LNQ_THREADS;
-            if (c < cols) y_out[(size_t)row * cols + c] = v[k];
+            if (c < cols) {
+                if (y_out) y_out[(size_t)row * cols + c] = v[k];
+                if (y_hi) {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(v[k]);
+                    y_hi[(size_t)row * cols + c] = h;
+                    y_lo[(size_t)row * cols + c] = __float2bfloat16_rn(v[k] - __bfloat162float(h));
+                }
+            }
         }
         return;
     }
@@ -236,10 +244,10 @@ int launch_embed(int B, int d, const int* tokens, const int* pos, const float* w
 }
 
 int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
-                    int32_t* q, float* scale, float* y, cudaStream_t st) {
+                    int32_t* q, float* scale, float* y, cudaStream_t st, void* y_hi, void* y_lo) {
     if (cols > LNQ_THREADS * LNQ_MAX_PER_THREAD || (cols & 3)) return B2_ERR_UNSUPPORTED;
     return launch_kernel(ln_quant_kernel, dim3(rows), dim3(LNQ_THREADS), 0, st, cols, x, gamma, beta, eps, q, scale,
-                         y) == cudaSuccess
+                         y, static_cast<__nv_bfloat16*>(y_hi), static_cast<__nv_bfloat16*>(y_lo)) == cudaSuccess
                ? B2_OK
                : B2_ERR_CUDA;
 }

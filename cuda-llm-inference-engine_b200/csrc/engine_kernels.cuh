@@ -7,7 +7,11 @@ namespace b2 {
 int launch_embed(int B, int d, const int* tokens, const int* pos, const float* wte, const float* wpe, float* x,
                  int* ctx_lens, unsigned long long* keys, cudaStream_t st);
 int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
-                    int32_t* q, float* scale, float* y, cudaStream_t st);
+                    int32_t* q, float* scale, float* y, cudaStream_t st, void* y_hi = nullptr,
+                    void* y_lo = nullptr);
+int launch_split_bf16(const float* x, void* hi, void* lo, size_t n, cudaStream_t st);
+int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo, const void* w_hi, const void* w_lo,
+                        float* logits, unsigned long long* keys, cudaStream_t st);
 int launch_qkv_scatter(int B, int d, int H, int dh, int block_size, int nbps, const float* qkv, const int* pos,
                        const int* block_table, float* q, void* k_cache, void* v_cache, int kv_dtype, cudaStream_t st);
 int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, float* logits,
