@@ -330,7 +330,8 @@ class GPT2Config(ctypes.Structure):
                 ("n_layers", "n_heads", "d_model", "d_ff", "vocab_size", "max_seq_len", "d_head")]
 
 
-ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
+ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_nccl_unique_id", "b2_engine_create_random_tp",
+                  "b2_engine_fill_kv_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
                   "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps",
                   "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions"]
 
@@ -343,6 +344,9 @@ def _engine_lib():
     pe = ctypes.POINTER(vp)
     lib.b2_engine_create_random.argtypes = [ctypes.POINTER(GPT2Config), i, i, u64, pe]
     lib.b2_engine_load.argtypes = [ctypes.c_char_p, i, i, pe]
+    lib.b2_nccl_unique_id.argtypes = [vp, ctypes.c_size_t]
+    lib.b2_engine_create_random_tp.argtypes = [ctypes.POINTER(GPT2Config), i, i, u64, vp, i, i, pe]
+    lib.b2_engine_fill_kv_random.argtypes = [vp, i, u64]
     lib.b2_engine_export.argtypes = [vp, ctypes.c_char_p]
     lib.b2_engine_destroy.argtypes = [vp]
     lib.b2_engine_destroy.restype = None
@@ -385,6 +389,23 @@ class Engine:
         return cls(h)
 
     @classmethod
+    def random_tp(cls, cfg: dict, max_batch: int, nccl_id: bytes, rank: int, world: int, kv_dtype: int = B2_KV_F32,
+                  seed: int = 0):
+        """Tensor-parallel rank of the same seeded model (b2_engine_create_random_tp)."""
+        lib = _engine_lib()
+        c = GPT2Config(**cfg)
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(nccl_id, len(nccl_id))
+        _check(lib.b2_engine_create_random_tp(ctypes.byref(c), max_batch, kv_dtype, seed, buf, rank, world,
+                                              ctypes.byref(h)), "b2_engine_create_random_tp")
+        e = cls(h)
+        e.tp_rank, e.tp_size = rank, world
+        return e
+
+    def fill_kv_random(self, ctx_len: int, seed: int = 0):
+        _check(self._lib.b2_engine_fill_kv_random(self._h, ctx_len, seed), "b2_engine_fill_kv_random")
+
+    @classmethod
     def load(cls, model_dir: str, max_batch: int, kv_dtype: int = B2_KV_F32):
         lib = _engine_lib()
         h = ctypes.c_void_p()
@@ -419,9 +440,13 @@ class Engine:
         _check(self._lib.b2_engine_keep_logits(self._h, 1 if enable else 0, None), "b2_engine_keep_logits")
 
     def logits(self):
+        """Last step's logits [batch, vocab rows held by this rank] (all of them unless sharded)."""
         import numpy as np
 
-        out = np.zeros((self.batch, self.cfg["vocab_size"]), np.float32)
+        world = getattr(self, "tp_size", 1)
+        per = (self.cfg["vocab_size"] + world - 1) // world
+        v0 = min(self.cfg["vocab_size"], getattr(self, "tp_rank", 0) * per)
+        out = np.zeros((self.batch, max(1, min(per, self.cfg["vocab_size"] - v0))), np.float32)
         _check(self._lib.b2_engine_read_logits(self._h, out.ctypes.data), "b2_engine_read_logits")
         return out
 
@@ -450,3 +475,10 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+def nccl_unique_id() -> bytes:
+    """An NCCL unique id for Engine.random_tp (rank 0 creates it, the caller shares it)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(_engine_lib().b2_nccl_unique_id(buf, 128), "b2_nccl_unique_id")
+    return buf.raw

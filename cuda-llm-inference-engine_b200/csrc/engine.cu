@@ -3,6 +3,8 @@
 #include "common.cuh"
 #include "engine_kernels.cuh"
 #include "b2engine.h"
+#include <cuda_bf16.h>
+#include <nccl.h>
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -57,6 +59,15 @@ __global__ void randn_kernel(float* out, size_t n, uint64_t seed, float stddev) 
     }
 }
 
+__global__ void randn_bf16_kernel(__nv_bfloat16* out, size_t n, uint64_t seed) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t r = mix64(seed * 0x100000001B3ull + i);
+        const float u1 = ((uint32_t)(r >> 40) + 1u) * (1.0f / 16777217.0f);
+        const float u2 = (uint32_t)(r & 0xFFFFFFu) * (1.0f / 16777216.0f);
+        out[i] = __float2bfloat16_rn(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+    }
+}
+
 __global__ void fill_kernel(float* out, size_t n, float v) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = v;
@@ -70,6 +81,13 @@ struct b2_engine {
     b2_gpt2_config cfg{};
     int max_batch = 0, kv_dtype = B2_KV_F32;
     int device = 0;
+    // tensor parallelism: this rank holds heads [rank*Hl, (rank+1)*Hl), i.e. model columns
+    // [rank*dl, (rank+1)*dl), FFN columns [rank*ffl, ...) and vocab rows [v0, v0+Vl)
+    int tp_rank = 0, tp_size = 1;
+    int Hl = 0, dl = 0, ffl = 0, v0 = 0, Vl = 0;
+    ncclComm_t comm = nullptr;
+    float* amax = nullptr;    // [B] row absmax (row-parallel quantisation)
+    int32_t* acc32 = nullptr; // [B, d] int32 partials of the row-parallel linears
     std::vector<void*> allocs;  // every device allocation, freed by the destructor
     float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
     std::vector<Layer> layers;
@@ -119,6 +137,7 @@ b2_engine::~b2_engine() {
     cudaGetDevice(&cur);
     cudaSetDevice(device);
     if (graph) cudaGraphExecDestroy(graph);
+    if (comm) ncclCommDestroy(comm);
     for (void* p : allocs) cudaFree(p);
     cudaSetDevice(cur);
 }
@@ -138,7 +157,7 @@ int alloc_runtime(b2_engine* e) {
     e->blocks_per_seq = (c.max_seq_len + kBlock - 1) / kBlock;
     e->num_blocks = B * e->blocks_per_seq;
     const size_t kvb = e->kv_dtype == B2_KV_F32 ? 4 : 2;
-    e->layer_stride = (size_t)e->num_blocks * kBlock * d;
+    e->layer_stride = (size_t)e->num_blocks * kBlock * e->dl;
     const size_t pool_bytes = (size_t)c.n_layers * e->layer_stride * kvb;
     e->k_pool = e->alloc<unsigned char>(pool_bytes);
     e->v_pool = e->alloc<unsigned char>(pool_bytes);
@@ -148,20 +167,22 @@ int alloc_runtime(b2_engine* e) {
     e->block_table = e->alloc<int>((size_t)B * e->blocks_per_seq);
     e->keys = e->alloc<unsigned long long>(B);
     e->x = e->alloc<float>((size_t)B * d);
-    e->qkv = e->alloc<float>((size_t)B * 3 * d);
+    e->qkv = e->alloc<float>((size_t)B * 3 * e->dl);
     e->q = e->alloc<float>((size_t)B * d);
     e->attn = e->alloc<float>((size_t)B * d);
-    e->hbuf = e->alloc<float>((size_t)B * c.d_ff);
+    e->hbuf = e->alloc<float>((size_t)B * e->ffl);
+    e->amax = e->alloc<float>(B);
+    e->acc32 = e->alloc<int32_t>((size_t)B * d);
     e->xf = e->alloc<float>((size_t)B * d);
-    e->logits = e->alloc<float>((size_t)B * c.vocab_size);
+    e->logits = e->alloc<float>((size_t)B * e->Vl);
     e->xq = e->alloc<int32_t>((size_t)B * std::max(d, c.d_ff) / 4);
     e->xs = e->alloc<float>(B);
-    e->wte_hi = e->alloc<uint16_t>((size_t)c.vocab_size * d);
-    e->wte_lo = e->alloc<uint16_t>((size_t)c.vocab_size * d);
+    e->wte_hi = e->alloc<uint16_t>((size_t)e->Vl * d);
+    e->wte_lo = e->alloc<uint16_t>((size_t)e->Vl * d);
     e->xf_hi = e->alloc<uint16_t>((size_t)B * d);
     e->xf_lo = e->alloc<uint16_t>((size_t)B * d);
-    e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, c.n_heads, c.n_heads, c.d_head,
-                                                                         c.max_seq_len, kBlock, 64, 4));
+    e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, e->Hl, e->Hl, c.d_head, c.max_seq_len,
+                                                                         kBlock, 64, 4));
     e->attn_ws = e->alloc<unsigned char>(e->attn_ws_bytes);
     if (e->failed) return B2_ERR_CUDA;
     if (!e->k_pool || !e->v_pool || !e->attn_ws || !e->logits) return B2_ERR_CUDA;
@@ -175,7 +196,7 @@ int alloc_runtime(b2_engine* e) {
 
 int alloc_weights(b2_engine* e) {
     const b2_gpt2_config& c = e->cfg;
-    const int d = c.d_model, ff = c.d_ff;
+    const int d = c.d_model;
     e->wte = e->alloc<float>((size_t)c.vocab_size * d);
     e->wpe = e->alloc<float>((size_t)c.max_seq_len * d);
     e->lnf_g = e->alloc<float>(d);
@@ -194,7 +215,8 @@ int alloc_weights(b2_engine* e) {
         l.ln1_b = e->alloc<float>(d);
         l.ln2_g = e->alloc<float>(d);
         l.ln2_b = e->alloc<float>(d);
-        if (!lin(l.qkv, 3 * d, d) || !lin(l.out, d, d) || !lin(l.up, ff, d) || !lin(l.down, d, ff)) return B2_ERR_CUDA;
+        if (!lin(l.qkv, 3 * e->dl, d) || !lin(l.out, d, e->dl) || !lin(l.up, e->ffl, d) || !lin(l.down, d, e->ffl))
+            return B2_ERR_CUDA;
         if (!l.ln1_g || !l.ln1_b || !l.ln2_g || !l.ln2_b) return B2_ERR_CUDA;
     }
     return (e->wte && e->wpe && e->lnf_g && e->lnf_b) ? B2_OK : B2_ERR_CUDA;
@@ -293,39 +315,67 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
     int r;
 #define B2_TRY(x) do { if ((r = (x)) != B2_OK) return r; } while (0)
     B2_TRY(launch_embed(B, d, e->tokens, e->pos, e->wte, e->wpe, e->x, e->ctx, e->keys, st));
+    const bool tp = e->tp_size > 1;
+    const int Hl = e->Hl, dl = e->dl, ffl = e->ffl;
+    // all-reduces of the tensor-parallel step (NCCL on the step's stream; captured in the graph)
+    auto allreduce = [&](void* buf, size_t n, ncclDataType_t t, ncclRedOp_t op) {
+        return ncclAllReduce(buf, buf, n, t, op, e->comm, st) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
+    };
+    // row-parallel linear: global-scale quantisation of this rank's activation columns,
+    // local int32 GEMM over them, int32 all-reduce (exact), then the dequant epilogue
+    auto row_parallel = [&](const float* act, int kl, const QLinear& W) {
+        int r2;
+        if ((r2 = launch_rowmax(B, kl, act, e->amax, st)) != B2_OK) return r2;
+        if ((r2 = allreduce(e->amax, B, ncclFloat, ncclMax)) != B2_OK) return r2;
+        if ((r2 = launch_quantize_scaled(B, kl, act, e->amax, e->xq, e->xs, st)) != B2_OK) return r2;
+        if ((r2 = gemm_launch(B, d, kl, e->xq, W.w, nullptr, nullptr, nullptr, nullptr, e->acc32, B2_EPI_PLAIN, true,
+                              st)) != B2_OK)
+            return r2;
+        if ((r2 = allreduce(e->acc32, (size_t)B * d, ncclInt32, ncclSum)) != B2_OK) return r2;
+        return launch_dequant_residual(B, d, e->acc32, e->xs, W.s, W.bias, e->x, e->x, st);
+    };
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer& L = e->layers[l];
         unsigned char* kc = static_cast<unsigned char*>(e->k_pool) + (size_t)l * e->layer_stride * kvb;
         unsigned char* vc = static_cast<unsigned char*>(e->v_pool) + (size_t)l * e->layer_stride * kvb;
         // attention sub-block (pre-norm; x stays the residual and is updated in place)
         B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
-        B2_TRY(gemm_launch(B, 3 * d, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
+        B2_TRY(gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
                            false, st));
-        B2_TRY(launch_qkv_scatter(B, d, H, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
+        B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
                                   vc, e->kv_dtype, st));
         b2_decode_attn_args a{};
-        a.B = B; a.H_q = H; a.H_kv = H; a.head_dim = dh;
+        a.B = B; a.H_q = Hl; a.H_kv = Hl; a.head_dim = dh;
         a.Q = e->q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;
         a.block_table = e->block_table; a.context_lens = e->ctx;
         a.max_context_len = c.max_seq_len; a.block_size = kBlock; a.num_blocks_per_seq = e->blocks_per_seq;
         a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = e->attn;
         a.workspace = e->attn_ws; a.workspace_bytes = e->attn_ws_bytes;
         B2_TRY(decode_attn_launch(&a, 64, true, st));
-        B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
-        B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
-                           false, st));
+        if (tp) {
+            B2_TRY(row_parallel(e->attn, dl, L.out));
+        } else {
+            B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
+            B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+                               false, st));
+        }
         // MLP sub-block
         B2_TRY(launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st));
-        B2_TRY(gemm_launch(B, ff, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
+        B2_TRY(gemm_launch(B, ffl, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
                            false, st));
-        B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
-        B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
-                           B2_EPI_BIAS_RESIDUAL, false, st));
+        if (tp) {
+            B2_TRY(row_parallel(e->hbuf, ffl, L.down));
+        } else {
+            B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
+            B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
+                               B2_EPI_BIAS_RESIDUAL, false, st));
+        }
     }
     B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
                            e->xf_lo));
-    B2_TRY(launch_vocab_bf16x3(B, c.vocab_size, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
-                               e->keep_logits ? e->logits : nullptr, e->keys, st));
+    B2_TRY(launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
+                               e->keep_logits ? e->logits : nullptr, e->keys, st, e->v0));
+    if (tp) B2_TRY(allreduce(e->keys, B, ncclUint64, ncclMax));  // global argmax over the vocab shards
     B2_TRY(launch_advance(B, e->keys, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
                           e->out_stride, c.max_seq_len, st));
 #undef B2_TRY
@@ -334,7 +384,8 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
 
 int finish_create(b2_engine* e, b2_engine** out) {
     // bf16 hi/lo halves of the tied embedding for the tensor-core vocab projection
-    if (launch_split_bf16(e->wte, e->wte_hi, e->wte_lo, (size_t)e->cfg.vocab_size * e->cfg.d_model, 0) != B2_OK ||
+    if (launch_split_bf16(e->wte + (size_t)e->v0 * e->cfg.d_model, e->wte_hi, e->wte_lo,
+                          (size_t)e->Vl * e->cfg.d_model, 0) != B2_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         delete e;
         return B2_ERR_CUDA;
@@ -345,10 +396,49 @@ int finish_create(b2_engine* e, b2_engine** out) {
 
 }  // namespace
 
-// ------------------------------------------------------------------ C ABI
-extern "C" {
+namespace {
 
-int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed, b2_engine** out) {
+int set_tp(b2_engine* e, int rank, int world) {
+    const b2_gpt2_config& c = e->cfg;
+    if (c.n_heads % world || c.d_ff % world || ((c.d_ff / world) % 16) || ((c.n_heads / world * c.d_head) % 16))
+        return B2_ERR_UNSUPPORTED;
+    e->tp_rank = rank;
+    e->tp_size = world;
+    e->Hl = c.n_heads / world;
+    e->dl = e->Hl * c.d_head;
+    e->ffl = c.d_ff / world;
+    const int per = (c.vocab_size + world - 1) / world;
+    e->v0 = std::min(c.vocab_size, rank * per);
+    e->Vl = std::max(1, std::min(per, c.vocab_size - e->v0));
+    return B2_OK;
+}
+
+// Copies this rank's slice of a full linear: rows [r0, r0+rows) of each of `segs` equal
+// row segments (column-parallel), or every row's K columns [k0, k0+kl) (row-parallel).
+int copy_rows(QLinear& dst, const QLinear& full, int segs, int rows, int rank) {
+    const int seg_rows = full.N / segs;
+    const size_t kb = (size_t)full.K;  // int8 bytes per row
+    for (int s = 0; s < segs; ++s) {
+        const size_t src_row = (size_t)s * seg_rows + (size_t)rank * rows, dst_row = (size_t)s * rows;
+        if (cudaMemcpy(reinterpret_cast<char*>(dst.w) + dst_row * kb, reinterpret_cast<const char*>(full.w) + src_row * kb,
+                       rows * kb, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+            cudaMemcpy(dst.s + dst_row, full.s + src_row, rows * 4, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+            cudaMemcpy(dst.bias + dst_row, full.bias + src_row, rows * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+            return B2_ERR_CUDA;
+    }
+    return B2_OK;
+}
+int copy_cols(QLinear& dst, const QLinear& full, int kl, int rank) {
+    if (cudaMemcpy2D(dst.w, kl, reinterpret_cast<const char*>(full.w) + (size_t)rank * kl, full.K, kl, full.N,
+                     cudaMemcpyDeviceToDevice) != cudaSuccess ||
+        cudaMemcpy(dst.s, full.s, (size_t)full.N * 4, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+        cudaMemcpy(dst.bias, full.bias, (size_t)full.N * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+        return B2_ERR_CUDA;
+    return B2_OK;
+}
+
+int create_random_impl(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed, int rank, int world,
+                       const void* nccl_id, b2_engine** out) {
     if (!cfg || !out || max_batch <= 0 || !valid_config(*cfg)) return B2_ERR_INVALID;
     if (kv_dtype != B2_KV_F32 && kv_dtype != B2_KV_BF16) return B2_ERR_UNSUPPORTED;
     b2_engine* e = new b2_engine();
@@ -356,37 +446,81 @@ int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dty
     e->max_batch = max_batch;
     e->kv_dtype = kv_dtype;
     cudaGetDevice(&e->device);
-    int st = alloc_weights(e);
+    int st = set_tp(e, rank, world);
+    if (st == B2_OK && world > 1) {
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        if (ncclCommInitRank(&e->comm, world, id, rank) != ncclSuccess) st = B2_ERR_CUDA;
+    }
+    if (st == B2_OK) st = alloc_weights(e);
     if (st == B2_OK) st = alloc_runtime(e);
     if (st != B2_OK) {
         delete e;
         return st;
     }
     const b2_gpt2_config& c = e->cfg;
-    const int d = c.d_model;
-    float* tmp = e->alloc<float>((size_t)std::max(3 * d, c.d_ff) * std::max(d, c.d_ff));
-    if (!tmp) {
-        delete e;
-        return B2_ERR_CUDA;
-    }
+    const int d = c.d_model, ff = c.d_ff;
+    // every rank draws the full weights with the 1-GPU seeds and keeps its slice, so a
+    // tensor-parallel engine computes the same model as the unsharded one
+    const size_t maxNK = (size_t)std::max(3 * d, ff) * std::max(d, ff);
+    float* tmp = nullptr;
+    QLinear full;
+    bool ok = cudaMalloc(&tmp, maxNK * 4) == cudaSuccess && cudaMalloc(&full.w, maxNK) == cudaSuccess &&
+              cudaMalloc(&full.s, (size_t)std::max(3 * d, ff) * 4) == cudaSuccess &&
+              cudaMalloc(&full.bias, (size_t)std::max(3 * d, ff) * 4) == cudaSuccess;
     randn(e->wte, (size_t)c.vocab_size * d, seed * 16 + 1, 0.02f);
     randn(e->wpe, (size_t)c.max_seq_len * d, seed * 16 + 2, 0.02f);
     fill(e->lnf_g, d, 1.f);
     fill(e->lnf_b, d, 0.f);
-    for (int l = 0; l < c.n_layers; ++l) {
+    for (int l = 0; ok && l < c.n_layers; ++l) {
         Layer& L = e->layers[l];
         fill(L.ln1_g, d, 1.f);
         fill(L.ln1_b, d, 0.f);
         fill(L.ln2_g, d, 1.f);
         fill(L.ln2_b, d, 0.f);
-        const uint64_t s = seed * 1000003ull + 97ull * (l + 1);
-        if (random_linear(L.qkv, s + 1, tmp) || random_linear(L.out, s + 2, tmp) || random_linear(L.up, s + 3, tmp) ||
-            random_linear(L.down, s + 4, tmp)) {
-            delete e;
-            return B2_ERR_CUDA;
-        }
+        const uint64_t sd = seed * 1000003ull + 97ull * (l + 1);
+        full.N = 3 * d; full.K = d;
+        ok = ok && random_linear(full, sd + 1, tmp) == B2_OK && copy_rows(L.qkv, full, 3, e->dl, rank) == B2_OK;
+        full.N = d; full.K = d;
+        ok = ok && random_linear(full, sd + 2, tmp) == B2_OK && copy_cols(L.out, full, e->dl, rank) == B2_OK;
+        full.N = ff; full.K = d;
+        ok = ok && random_linear(full, sd + 3, tmp) == B2_OK && copy_rows(L.up, full, 1, e->ffl, rank) == B2_OK;
+        full.N = d; full.K = ff;
+        ok = ok && random_linear(full, sd + 4, tmp) == B2_OK && copy_cols(L.down, full, e->ffl, rank) == B2_OK;
+    }
+    cudaDeviceSynchronize();
+    cudaFree(tmp);
+    cudaFree(full.w);
+    cudaFree(full.s);
+    cudaFree(full.bias);
+    if (!ok) {
+        delete e;
+        return B2_ERR_CUDA;
     }
     return finish_create(e, out);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed, b2_engine** out) {
+    return create_random_impl(cfg, max_batch, kv_dtype, seed, 0, 1, nullptr, out);
+}
+
+int b2_nccl_unique_id(void* out, size_t bytes) {
+    if (!out || bytes < sizeof(ncclUniqueId)) return B2_ERR_INVALID;
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return B2_ERR_CUDA;
+    memcpy(out, &id, sizeof(id));
+    return B2_OK;
+}
+
+int b2_engine_create_random_tp(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed,
+                               const void* nccl_id, int rank, int world, b2_engine** out) {
+    if (!nccl_id || world < 1 || rank < 0 || rank >= world) return B2_ERR_INVALID;
+    return create_random_impl(cfg, max_batch, kv_dtype, seed, rank, world, nccl_id, out);
 }
 
 int b2_engine_load(const char* model_dir, int max_batch, int kv_dtype, b2_engine** out) {
@@ -400,7 +534,8 @@ int b2_engine_load(const char* model_dir, int max_batch, int kv_dtype, b2_engine
     e->max_batch = max_batch;
     e->kv_dtype = kv_dtype;
     cudaGetDevice(&e->device);
-    int st = alloc_weights(e);
+    int st = set_tp(e, 0, 1);
+    if (st == B2_OK) st = alloc_weights(e);
     if (st == B2_OK) st = alloc_runtime(e);
     const int d = c.d_model;
     bool ok = st == B2_OK;
@@ -435,6 +570,7 @@ int b2_engine_load(const char* model_dir, int max_batch, int kv_dtype, b2_engine
 
 int b2_engine_export(const b2_engine* e, const char* model_dir) {
     if (!e || !model_dir) return B2_ERR_INVALID;
+    if (e->tp_size != 1) return B2_ERR_UNSUPPORTED;  // a rank holds only its shard
     const b2_gpt2_config& c = e->cfg;
     const std::string root(model_dir);
     char js[512];
@@ -586,10 +722,26 @@ int b2_engine_keep_logits(b2_engine* e, int enable, const float** logits) {
 
 int b2_engine_read_logits(const b2_engine* e, float* out_host) {
     if (!e || !out_host || e->batch <= 0 || !e->keep_logits) return B2_ERR_INVALID;
-    return cudaMemcpy(out_host, e->logits, (size_t)e->batch * e->cfg.vocab_size * 4, cudaMemcpyDeviceToHost) ==
+    return cudaMemcpy(out_host, e->logits, (size_t)e->batch * e->Vl * 4, cudaMemcpyDeviceToHost) ==
                    cudaSuccess
                ? B2_OK
                : B2_ERR_CUDA;
+}
+
+int b2_engine_fill_kv_random(b2_engine* e, int ctx_len, uint64_t seed) {
+    if (!e || e->batch <= 0 || ctx_len < 0 || ctx_len >= e->cfg.max_seq_len) return B2_ERR_INVALID;
+    const size_t n = (size_t)e->cfg.n_layers * e->layer_stride;
+    for (int which = 0; which < 2; ++which) {
+        void* pool = which ? e->v_pool : e->k_pool;
+        const uint64_t sd = seed * 4 + which + 2ull * e->tp_rank * 0x9E37ull;
+        if (e->kv_dtype == B2_KV_F32)
+            randn_kernel<<<1184, 256>>>(static_cast<float*>(pool), n, sd, 1.0f);
+        else
+            randn_bf16_kernel<<<1184, 256>>>(static_cast<__nv_bfloat16*>(pool), n, sd);
+    }
+    std::vector<int> p(e->batch, ctx_len);
+    if (cudaMemcpy(e->pos, p.data(), (size_t)e->batch * 4, cudaMemcpyHostToDevice) != cudaSuccess) return B2_ERR_CUDA;
+    return cudaDeviceSynchronize() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
 int b2_engine_positions(const b2_engine* e, int32_t* pos_host) {

@@ -18,6 +18,8 @@
 // fixed sequence of launches that a CUDA graph can replay.
 #include "common.cuh"
 #include "engine_kernels.cuh"
+#include "epilogue.cuh"
+#include <algorithm>
 #include <cuda_bf16.h>
 
 namespace b2 {
@@ -279,6 +281,83 @@ int launch_advance(int B, const unsigned long long* keys, int* tokens, int* pos,
                    cudaStream_t st) {
     return launch_kernel(advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, B, keys, tokens, pos, forced,
                          forced_len, forced_stride, out_tokens, out_stride, max_pos) == cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
+}
+
+}  // namespace b2
+
+// ------------------------------------------------------------------ tensor-parallel helpers
+// A row-parallel linear needs the per-row scale of the FULL activation row, which is
+// sharded across ranks: each rank takes its slice's absmax, an all-reduce(max) gives the
+// global one, and every rank quantises its slice with it, so the int8 bytes equal those of
+// the unsharded quantiser (kernels/quantization/14_int8_gemm.cu:22-58).
+namespace b2 {
+
+__global__ void rowmax_kernel(int cols, const float* __restrict__ x, float* __restrict__ amax_out) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ float red[8];
+    const float* xr = x + (size_t)blockIdx.x * cols;
+    float m = 0.f;
+    for (int c = threadIdx.x; c < cols; c += 256) m = fmaxf(m, fabsf(xr[c]));
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+        m = fmaxf(m, red[0]);
+        amax_out[blockIdx.x] = m;
+    }
+}
+
+__global__ void quantize_scaled_kernel(int cols, const float* __restrict__ x, const float* __restrict__ amax,
+                                       int32_t* __restrict__ q_out, float* __restrict__ scale_out) {
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.x;
+    const float a = amax[row];
+    const float scale = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (threadIdx.x == 0) scale_out[row] = scale;
+    const float* xr = x + (size_t)row * cols;
+    int8_t* qr = reinterpret_cast<int8_t*>(q_out) + (size_t)row * cols;
+    for (int c = threadIdx.x; c < cols; c += 256)
+        qr[c] = (int8_t)(int)fminf(fmaxf(rintf(__fmul_rn(xr[c], inv)), -128.f), 127.f);
+}
+
+// out[m, n] = epilogue(acc[m, n]) after the int32 all-reduce of a row-parallel linear.
+template <int EPI>
+__global__ void dequant_kernel(int M, int N, const int32_t* __restrict__ acc, const float* __restrict__ sA,
+                               const float* __restrict__ sB, const float* __restrict__ bias,
+                               const float* __restrict__ residual, float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    const size_t total = (size_t)M * N;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / N), n = (int)(i % N);
+        const float rs = (EPI == B2_EPI_BIAS_RESIDUAL) ? residual[i] : 0.f;
+        out[i] = epilogue<EPI>(acc[i], sA[m], sB[n], EPI != B2_EPI_PLAIN ? bias[n] : 0.f, rs);
+    }
+}
+
+int launch_rowmax(int rows, int cols, const float* x, float* amax, cudaStream_t st) {
+    return launch_kernel(rowmax_kernel, dim3(rows), dim3(256), 0, st, cols, x, amax) == cudaSuccess ? B2_OK
+                                                                                                    : B2_ERR_CUDA;
+}
+
+int launch_quantize_scaled(int rows, int cols, const float* x, const float* amax, int32_t* q, float* scale,
+                           cudaStream_t st) {
+    return launch_kernel(quantize_scaled_kernel, dim3(rows), dim3(256), 0, st, cols, x, amax, q, scale) == cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
+}
+
+int launch_dequant_residual(int M, int N, const int32_t* acc, const float* sA, const float* sB, const float* bias,
+                            const float* residual, float* out, cudaStream_t st) {
+    const int blocks = (int)std::min<size_t>(((size_t)M * N + 255) / 256, 1184);
+    return launch_kernel(dequant_kernel<B2_EPI_BIAS_RESIDUAL>, dim3(blocks), dim3(256), 0, st, M, N, acc, sA, sB, bias,
+                         residual, out) == cudaSuccess
                ? B2_OK
                : B2_ERR_CUDA;
 }

@@ -11,7 +11,7 @@ int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, cons
                     void* y_lo = nullptr);
 int launch_split_bf16(const float* x, void* hi, void* lo, size_t n, cudaStream_t st);
 int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo, const void* w_hi, const void* w_lo,
-                        float* logits, unsigned long long* keys, cudaStream_t st);
+                        float* logits, unsigned long long* keys, cudaStream_t st, int n_offset = 0);
 int launch_qkv_scatter(int B, int d, int H, int dh, int block_size, int nbps, const float* qkv, const int* pos,
                        const int* block_table, float* q, void* k_cache, void* v_cache, int kv_dtype, cudaStream_t st);
 int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, float* logits,
@@ -19,4 +19,9 @@ int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, f
 int launch_advance(int B, const unsigned long long* keys, int* tokens, int* pos, const int* forced,
                    const int* forced_len, int forced_stride, int* out_tokens, int out_stride, int max_pos,
                    cudaStream_t st);
+int launch_rowmax(int rows, int cols, const float* x, float* amax, cudaStream_t st);
+int launch_quantize_scaled(int rows, int cols, const float* x, const float* amax, int32_t* q, float* scale,
+                           cudaStream_t st);
+int launch_dequant_residual(int M, int N, const int32_t* acc, const float* sA, const float* sB, const float* bias,
+                            const float* residual, float* out, cudaStream_t st);
 }  // namespace b2

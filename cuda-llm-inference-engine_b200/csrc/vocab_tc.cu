@@ -58,7 +58,8 @@ __device__ __forceinline__ unsigned long long vt_key(float v, int idx) {
 }
 
 struct VocabParams {
-    int M, N, K;               // batch, vocab, d_model
+    int M, N, K;               // batch, vocab rows held here, d_model
+    int n_offset;              // global index of this shard's first vocab row (tensor parallel)
     float* logits;             // [M, N] or null
     unsigned long long* keys;  // [M] argmax keys (reset by the caller before the step)
     unsigned int* err;
@@ -210,7 +211,7 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
                     const int n = n0 + q;
                     const float v = __uint_as_float(q < 16 ? r0[q] : r1[q - 16]);
                     if (n < p.N) {
-                        const unsigned long long key = vt_key(v, n);
+                        const unsigned long long key = vt_key(v, p.n_offset + n);
                         best = key > best ? key : best;
                         if (p.logits) p.logits[(size_t)row * p.N + n] = v;
                     }
@@ -273,7 +274,7 @@ int launch_split_bf16(const float* x, void* hi, void* lo, size_t n, cudaStream_t
 
 // logits/argmax of h [M, K] (as bf16 hi/lo) against W [N, K] (bf16 hi/lo). K % 8 == 0.
 int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo, const void* w_hi, const void* w_lo,
-                        float* logits, unsigned long long* keys, cudaStream_t st) {
+                        float* logits, unsigned long long* keys, cudaStream_t st, int n_offset) {
     if ((K & 7) || M <= 0 || N <= 0) return B2_ERR_UNSUPPORTED;
     CUtensorMap ah, al, wh, wl;
     if (!encode_bf16(&ah, h_hi, M, K, VT_BM) || !encode_bf16(&al, h_lo, M, K, VT_BM) ||
@@ -281,7 +282,7 @@ int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo,
         return B2_ERR_CUDA;
     if (!set_smem_attr_once((const void*)vocab_bf16x3_kernel, VT_SMEM, 60)) return B2_ERR_CUDA;
     const int tiles = ((M + VT_BM - 1) / VT_BM) * ((N + VT_BN - 1) / VT_BN);
-    VocabParams p{M, N, K, logits, keys, device_error_ptr()};
+    VocabParams p{M, N, K, n_offset, logits, keys, device_error_ptr()};
     const int grid = std::min(tiles, num_sms_current_device());
     return launch_kernel(vocab_bf16x3_kernel, dim3(grid), dim3(VT_THREADS), (size_t)VT_SMEM, st, ah, al, wh, wl, p) ==
                    cudaSuccess

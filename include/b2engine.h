@@ -41,6 +41,21 @@ typedef struct b2_engine b2_engine;
 int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed,
                             b2_engine** out);
 
+/* Writes an NCCL unique id (ncclGetUniqueId) for b2_engine_create_random_tp into out[bytes >= 128]. */
+int b2_nccl_unique_id(void* out, size_t bytes);
+
+/* Tensor-parallel engine, rank `rank` of `world` (one process per GPU, the GPU current when
+ * called): heads, QKV and FC1 output columns and vocab rows are split across ranks; out-proj
+ * and FC2 are row-parallel. Every rank draws the full model with the same seeds as
+ * b2_engine_create_random and keeps its slice, so the sharded engine computes the same model.
+ * The row-parallel inputs are quantised with the global row scale (all-reduce max of the
+ * per-rank absmax), the int32 partial products are all-reduced exactly before the
+ * dequantisation epilogue, and the greedy argmax is an all-reduce(max) of 64-bit keys, so the
+ * int8 bytes and int32 accumulators equal the single-GPU ones. nccl_id comes from rank 0's
+ * b2_nccl_unique_id, shared by the caller. Requires n_heads and d_ff divisible by world. */
+int b2_engine_create_random_tp(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, uint64_t seed,
+                               const void* nccl_id, int rank, int world, b2_engine** out);
+
 /* Engine from a model directory in the reference's format (GPT2Engine::load_weights,
  * src/gpt2_engine.cu:75-112). Any number of layers. Missing or short files are errors. */
 int b2_engine_load(const char* model_dir, int max_batch, int kv_dtype, b2_engine** out);
@@ -78,6 +93,11 @@ int b2_engine_keep_logits(b2_engine* e, int enable, const float** logits);
 
 /* Copies the last step's logits [batch, vocab] to host memory (needs keep_logits). Synchronous. */
 int b2_engine_read_logits(const b2_engine* e, float* out_host);
+
+/* Synthetic context: fills the whole KV pool with seeded N(0,1) values and moves every
+ * sequence to position ctx_len (< max_seq_len), as if ctx_len tokens had been decoded. For
+ * benchmarks of long contexts without a prefill. Synchronous. */
+int b2_engine_fill_kv_random(b2_engine* e, int ctx_len, uint64_t seed);
 
 /* Current position of every sequence (tokens already in its KV cache). Synchronous. */
 int b2_engine_positions(const b2_engine* e, int32_t* pos_host);
