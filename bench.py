@@ -336,6 +336,11 @@ def run_gpu(args):
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if world > 1 and os.environ.get("B2_BENCH_SKIP_TP") != "1":
+        del kc, vc
+        torch.cuda.empty_cache()
+        r5 = tp_config5(torch, b2, np, dist, rank, world, hbm_peak)
+        line["secondary"] = {"tp_decode_config5": r5}
     if world == 1 and rank == 0:
         line["secondary"] = secondary(torch, b2, np, args, kc, vc, q, btd, lensd, lens, bt, P, hbm_peak, bf16_peak)
         line["cpu_baseline"] = cpu_baseline(torch, q, kc, vc, bt, lens)
@@ -447,6 +452,53 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
             "hbm_bound_tok_s": round(B / (by / (hbm_peak * 1e9)), 1),
             "generated_tokens_valid": bool((toks[:, prompt_len:prompt_len + steps_new] >= 0).all()),
             "timing": "CUDA graph replays of one decode step"}
+
+
+WIDE = dict(n_layers=32, n_heads=32, d_model=4096, d_ff=16384, vocab_size=50257, max_seq_len=4096 + 64 + 1,
+            d_head=128)
+
+
+def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B=128):
+    """the widened GPT-2 (32 L, d 4096, 32 x 128 heads, d_ff 16384) decoding
+    a batch of 128 at context 4096 for 64 greedy steps, bf16 KV, tensor-parallel over the
+    ranks. The 4096-token context is a seeded synthetic KV fill (no prefill); timed with CUDA
+    events over CUDA-graph replays, max over ranks."""
+    cfg = WIDE
+    nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        nid.copy_(torch.frombuffer(bytearray(b2.nccl_unique_id()), dtype=torch.uint8))
+    dist.broadcast(nid, 0)
+    eng = b2.Engine.random_tp(cfg, B, bytes(nid.cpu().numpy().tobytes()), rank, world, kv_dtype=b2.B2_KV_BF16,
+                              seed=SEED)
+    rng = np.random.default_rng(SEED)
+    eng.start([[int(t)] for t in rng.integers(0, cfg["vocab_size"], B)], steps + 1, seed=SEED)
+    eng.fill_kv_random(ctx, seed=SEED)
+    st = torch.cuda.current_stream()
+    eng.run_steps(2, stream=st)  # warm-up (captures the graph); positions ctx, ctx+1
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    eng.run_steps(steps, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    assert b2.device_error() == 0
+    d, L = cfg["d_model"], cfg["n_layers"]
+    ctx_mean = ctx + 2 + (steps - 1) / 2.0 + 1
+    lin = L * (3 * d * d + d * d + 2 * cfg["d_ff"] * d)
+    kv = B * ctx_mean * L * 2 * d * 2
+    by_total = lin + 2 * cfg["vocab_size"] * d * 2 + kv  # int8 weights + bf16 vocab halves + bf16 K/V
+    step_s = ms / steps * 1e-3
+    eng.close()
+    return {"tok_s": round(B * steps / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 3),
+            "step_bytes_all_ranks": int(by_total), "gbs_all_ranks": round(by_total / step_s / 1e9, 1),
+            "frac_of_hbm_bound": round(by_total / step_s / 1e9 / (hbm_peak * world), 4),
+            "hbm_bound_tok_s": round(B / (by_total / (hbm_peak * 1e9 * world)), 1),
+            "parallelism": f"tensor-parallel x{world} (NCCL all-reduce after proj and FC2)",
+            "context": "seeded synthetic KV fill of 4096 tokens, then 2 warm-up + 64 timed steps"}
 
 
 def cpu_baseline(torch, q, kc, vc, bt, lens):
