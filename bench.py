@@ -586,7 +586,25 @@ def run_only(args):
         r = gpt2_config4(torch, b2, np, measured_peaks()[0], steps_new=max(1, args.steps), prompt_len=128)
         print(f"gpt2: {json.dumps(r)} (not a bench value)", flush=True)
         return
-    if args.only.startswith("attn"):
+    if args.only == "attn_wide":
+        # config 5's per-layer attention shape on one GPU: MHA 32 x 128, bf16 KV, context 4096
+        # (batch 32 of the 128, so the case stays near 2 GB for profiling)
+        import numpy as np
+
+        Bw, Hw, ctxw = 32, 32, 4096
+        nb = ctxw // BS
+        P = Bw * nb
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        kc = torch.randn(P, BS, Hw, D, generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn(P, BS, Hw, D, generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randn(Bw, Hw, D, device=dev)
+        O = torch.empty_like(q)
+        btd = torch.randperm(P, generator=g, device=dev).to(torch.int32).view(Bw, nb)
+        lensd = torch.full((Bw,), ctxw, dtype=torch.int32, device=dev)
+        ws = b2.make_decode_workspace(Bw, Hw, Hw, D, ctxw, BS, device=dev)
+        fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, ctxw, O=O, workspace=ws)  # noqa: E731
+        by = attn_alg_bytes(np.full(Bw, ctxw), Hw, Hw, D, 2, nb)
+    elif args.only.startswith("attn"):
         dt = torch.bfloat16 if args.only == "attn_bf16" else torch.float32
         lens, bt, P = workload_meta()
         kc, vc = make_kv_shard(torch, P, 0, H_KV, dt, dev)
@@ -617,7 +635,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--only", default=None,
-                    choices=["attn", "attn_bf16", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
+                    choices=["attn", "attn_bf16", "attn_wide", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
                     help="run one workload for a few steps with no JSON line (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -483,6 +483,187 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     }
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM (cta_group::2)
+// For large GEMMs: a cluster of 2 CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256 split across the pair's TMEM, N = 256). Each CTA loads
+// 128 rows of A and 128 of the 256 B rows per stage (32 KB), so an SM moves 2/3 of the
+// operand bytes of a 128 x 256 single-CTA tile per MAC, and the ring is 6 stages deep. Both
+// CTAs' TMA bytes land on the even CTA's full barrier; the even CTA issues the MMAs and
+// commits to both CTAs' barriers; every epilogue warp of the pair releases the even CTA's
+// accumulator barrier. No load uses cluster multicast.
+constexpr int P2_ROWS = 128;                       // A rows and B rows per CTA per stage
+constexpr int P2_STAGE = 2 * P2_ROWS * GM_BK;      // 32 KB
+constexpr int P2_STAGES = 6;
+constexpr int P2_BN = 256;                         // accumulator columns per CTA
+constexpr int P2_OFF_BAR = P2_STAGES * P2_STAGE;
+constexpr int P2_NBAR = 2 * P2_STAGES + 4;
+constexpr int P2_OFF_COL = P2_OFF_BAR + P2_NBAR * 8 + 16;
+constexpr int P2_SMEM = P2_OFF_COL + 2 * P2_BN * 4 + 1024;
+constexpr uint32_t P2_TMEM_COLS = 2 * P2_BN;
+
+template <int EPI, bool S32>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                     const GemmParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + P2_OFF_BAR;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (P2_STAGES + s); };
+    auto accf_bar = [&](int a) { return bar0 + 8u * (2 * P2_STAGES + a); };
+    auto acce_bar = [&](int a) { return bar0 + 8u * (2 * P2_STAGES + 2 + a); };
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + P2_OFF_BAR + P2_NBAR * 8);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int nk = (p.K + GM_BK - 1) / GM_BK;
+    const int m_tiles = (p.M + 2 * P2_ROWS - 1) / (2 * P2_ROWS);
+    const int n_tiles = (p.N + P2_BN - 1) / P2_BN;
+    const int num_tiles = m_tiles * n_tiles;
+
+    if (threadIdx.x == 0) {
+        prefetch_tensormap(&mapA);
+        prefetch_tensormap(&mapB);
+        for (int s = 0; s < P2_STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(accf_bar(a), 1);
+            mbar_init(acce_bar(a), 8);  // 4 epilogue warps x 2 CTAs
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(const_cast<uint32_t*>(tmem_slot)), P2_TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    griddep_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_last();
+            int it = 0;
+            for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+                int mt, nt;
+                tile_coords(t, m_tiles, n_tiles, mt, nt);
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % P2_STAGES;
+                    if (it >= P2_STAGES) {
+                        if (*abort_flag || !mbar_wait(empty_bar(s), ((it / P2_STAGES) - 1) & 1, p.err)) {
+                            *abort_flag = 1;
+                            break;
+                        }
+                    }
+                    const uint32_t a_s = sbase + s * P2_STAGE;
+                    const uint32_t b_s = a_s + P2_ROWS * GM_BK;
+                    if (rank == 0) mbar_arrive_expect_tx(full_bar(s), 2 * P2_STAGE);  // both CTAs' bytes
+                    const uint32_t lead_full = mapa_shared(full_bar(s), 0);
+                    tma_load_2d_pair(a_s, &mapA, kb * GM_BK, mt * 2 * P2_ROWS + (int)rank * P2_ROWS, lead_full, pol);
+                    tma_load_2d_pair(b_s, &mapB, kb * GM_BK, nt * P2_BN + (int)rank * P2_ROWS, lead_full, pol);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_i8(2 * P2_ROWS, P2_BN);
+            int it = 0, j = 0;
+            for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, ++j) {
+                const int a = j & 1, u = j >> 1;
+                if (u >= 1 && !mbar_wait(acce_bar(a), (u - 1) & 1, p.err)) { *abort_flag = 1; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + a * P2_BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % P2_STAGES;
+                    if (*abort_flag || !mbar_wait(full_bar(s), (it / P2_STAGES) & 1, p.err)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_s = sbase + s * P2_STAGE;
+                    const uint64_t da = smem_desc_sw128(a_s);
+                    const uint64_t db = smem_desc_sw128(a_s + P2_ROWS * GM_BK);
+#pragma unroll
+                    for (int k = 0; k < GM_BK / 32; ++k)
+                        mma_i8_pair(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    mma_commit_pair(mapa_shared(empty_bar(s), 0));
+                    mma_commit_pair(mapa_shared(empty_bar(s), 1));
+                }
+                mma_commit_pair(mapa_shared(accf_bar(a), 0));
+                mma_commit_pair(mapa_shared(accf_bar(a), 1));
+            }
+        }
+        __syncwarp();
+    } else {
+        const int quad = warp & 3;
+        const int et = threadIdx.x - 64;
+        float* sB_s = reinterpret_cast<float*>(smem + P2_OFF_COL);
+        float* bias_s = sB_s + P2_BN;
+        const uint32_t lead_acce0 = mapa_shared(acce_bar(0), 0), lead_acce1 = mapa_shared(acce_bar(1), 0);
+        int j = 0;
+        for (int t = pair; t < num_tiles; t += npairs, ++j) {
+            const int a = j & 1, u = j >> 1;
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, mt, nt);
+            if constexpr (!S32) {
+                for (int c = et; c < P2_BN; c += 128) {
+                    const int n = nt * P2_BN + c;
+                    sB_s[c] = n < p.N ? __ldg(p.scale_B + n) : 0.f;
+                    if (EPI != B2_EPI_PLAIN) bias_s[c] = n < p.N ? __ldg(p.bias + n) : 0.f;
+                }
+            }
+            named_barrier(2, 128);
+            const bool ok = !*abort_flag && mbar_wait(accf_bar(a), u & 1, p.err);
+            if (!ok) *abort_flag = 1;
+            tc_fence_after();
+            const int row = mt * 2 * P2_ROWS + (int)rank * P2_ROWS + quad * 32 + lane;
+            const bool row_ok = ok && row < p.M;
+            const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
+            const uint32_t tbase = tmem + a * P2_BN + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < P2_BN / 16; c += 2) {
+                uint32_t r0[16], r1[16];
+                tmem_ld16(tbase + (uint32_t)(c * 16), r0);
+                tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
+                tmem_ld_wait();
+                const int n = nt * P2_BN + c * 16;
+                float rs0[16], rs1[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { rs0[i] = 0.f; rs1[i] = 0.f; }
+                if constexpr (EPI == B2_EPI_BIAS_RESIDUAL && !S32) {
+                    if (row_ok && n < p.N) load_res16(p, row, n, rs0);
+                    if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
+                }
+                if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
+                if (row_ok && n + 16 < p.N)
+                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(a ? lead_acce1 : lead_acce0);
+            named_barrier(2, 128);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the even CTA's last commits target this CTA's barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, P2_TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------ SIMT path for K % 16 != 0
 // (the tensor-map row stride must be a multiple of 16 bytes). Plain exact int32 dot products.
 template <int EPI, bool S32>
@@ -580,6 +761,9 @@ static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, c
                : B2_ERR_CUDA;
 }
 
+// CTA-pair path switch (a test hook compares it with the single-CTA path).
+bool g_gemm_pairs = true;
+
 // Split-K plan for GEMMs whose tiles cannot fill the GPU (decode: M = batch <= 128): the
 // workspace holds [tiles] u32 tickets (zero at rest), then [k_splits][M][N] int32 partials.
 static void plan_split(GemmParams& p, int tiles, void* ws, size_t ws_bytes, int sms) {
@@ -603,6 +787,29 @@ static void plan_split(GemmParams& p, int tiles, void* ws, size_t ws_bytes, int 
 }
 
 template <int EPI, bool S32>
+static int launch_tc2(const GemmParams& p, const int32_t* A, const int32_t* BT, cudaStream_t st, int slot) {
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, A, p.M, p.K, P2_ROWS) || !make_map(&mb, BT, p.N, p.K, P2_ROWS)) return B2_ERR_CUDA;
+    auto kfn = int8_gemm_tc2_kernel<EPI, S32>;
+    if (!set_smem_attr_once((const void*)kfn, P2_SMEM, slot)) return B2_ERR_CUDA;
+    const int tiles = ((p.N + P2_BN - 1) / P2_BN) * ((p.M + 2 * P2_ROWS - 1) / (2 * P2_ROWS));
+    const int pairs = std::min(tiles, num_sms_current_device() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(GM_THREADS);
+    cfg.dynamicSmemBytes = P2_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kfn, ma, mb, p) == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+template <int EPI, bool S32>
 static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, void* ws, size_t ws_bytes,
                          cudaStream_t st) {
     // K == 0 (empty contraction, acc = 0) and K % 16 != 0 take the SIMT kernel
@@ -617,6 +824,12 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
     // widest tile that still gives every SM a tile; otherwise the narrowest, split along K
     const int slot_base = (EPI + (S32 ? 4 : 0)) * 3;
     const int t256 = mt * ((p.N + 255) / 256), t128 = mt * ((p.N + 127) / 128), t64 = mt * ((p.N + 63) / 64);
+    // CTA pairs with 256 x 256 tiles once there are enough of them to occupy most SM pairs
+    const int pair_tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+    if (g_gemm_pairs && pair_tiles * 2 >= (sms * 3) / 4) {
+        plan_split(p, pair_tiles, nullptr, 0, sms);
+        return launch_tc2<EPI, S32>(p, A, BT, st, 40 + EPI + (S32 ? 4 : 0));
+    }
     if (t256 >= sms) {
         plan_split(p, t256, nullptr, 0, sms);
         return launch_tc<256, EPI, S32>(p, A, BT, st, slot_base + 0);

@@ -53,6 +53,7 @@ def test_quantizer_bit_exact(b2, oracle, cuda, rows, cols):
 GEMM_SHAPES = [
     (256, 256, 256), (512, 512, 512), (1024, 1024, 1024), (512, 1024, 256),  # reference test shapes
     (2048, 2048, 2048),
+    (2000, 2100, 272), (4096, 1024, 512),                                     # CTA-pair path, ragged
     (64, 3072, 768),                                                          # config 2 rectangular
     (64, 2304, 768), (128, 768, 3072),                                        # decode-step linears
     (100, 200, 48), (1, 16, 16), (130, 17, 4096), (129, 300, 144),            # ragged edges
@@ -77,7 +78,8 @@ def test_gemm_s32_bit_exact(b2, oracle, cuda, M, N, K):
     np.testing.assert_array_equal(got.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (2048, 2048, 2048), (64, 3072, 768), (100, 200, 48), (5, 7, 20)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (2048, 2048, 2048), (2000, 2100, 272), (64, 3072, 768),
+                                   (100, 200, 48), (5, 7, 20)])
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 def test_gemm_epilogues(b2, oracle, cuda, M, N, K, epi):
     import torch
