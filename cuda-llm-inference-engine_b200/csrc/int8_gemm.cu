@@ -493,18 +493,21 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
 // accumulator barrier. No load uses cluster multicast.
 constexpr int P2_ROWS = 128;                       // A rows and B rows per CTA per stage
 constexpr int P2_STAGE = 2 * P2_ROWS * GM_BK;      // 32 KB
-constexpr int P2_STAGES = 6;
+constexpr int P2_STAGES = 5;
 constexpr int P2_BN = 256;                         // accumulator columns per CTA
 constexpr int P2_OFF_BAR = P2_STAGES * P2_STAGE;
 constexpr int P2_NBAR = 2 * P2_STAGES + 4;
 constexpr int P2_OFF_COL = P2_OFF_BAR + P2_NBAR * 8 + 16;
-constexpr int P2_SMEM = P2_OFF_COL + 2 * P2_BN * 4 + 1024;
+// epilogue staging: per epilogue warp 2 buffers of 32 rows x 32 fp32 (128-byte swizzled)
+constexpr int P2_OFF_EPI = (P2_OFF_COL + 2 * P2_BN * 4 + 1023) & ~1023;
+constexpr int P2_EPI_BUF = 32 * 32 * 4;
+constexpr int P2_SMEM = P2_OFF_EPI + 4 * 2 * P2_EPI_BUF + 1024;
 constexpr uint32_t P2_TMEM_COLS = 2 * P2_BN;
 
 template <int EPI, bool S32>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap mapC, const GemmParams p, const int c_tma) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -631,6 +634,8 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
             const bool row_ok = ok && row < p.M;
             const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
             const uint32_t tbase = tmem + a * P2_BN + ((uint32_t)(quad * 32) << 16);
+            const int row0 = mt * 2 * P2_ROWS + (int)rank * P2_ROWS + quad * 32;  // this warp's first row
+            unsigned char* stage_w = smem + P2_OFF_EPI + (warp - 2) * 2 * P2_EPI_BUF;
 #pragma unroll 1
             for (int c = 0; c < P2_BN / 16; c += 2) {
                 uint32_t r0[16], r1[16];
@@ -645,9 +650,39 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
                     if (row_ok && n < p.N) load_res16(p, row, n, rs0);
                     if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
                 }
-                if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
-                if (row_ok && n + 16 < p.N)
-                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
+                if (c_tma) {
+                    // 32 x 32 block of this warp through swizzled shared memory, stored by TMA
+                    // (rows >= M and columns >= N are clipped by the tensor map)
+                    unsigned char* buf = stage_w + ((c >> 1) & 1) * P2_EPI_BUF;
+                    if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
+                    __syncwarp();
+                    uint32_t w[32];
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) {
+                        const uint32_t acc = q < 16 ? r0[q] : r1[q - 16];
+                        if constexpr (S32) {
+                            w[q] = acc;
+                        } else {
+                            w[q] = __float_as_uint(epilogue<EPI>((int32_t)acc, sa, sB_s[c * 16 + q],
+                                                                 EPI != B2_EPI_PLAIN ? bias_s[c * 16 + q] : 0.f,
+                                                                 q < 16 ? rs0[q] : rs1[q - 16]));
+                        }
+                    }
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch)
+                        *reinterpret_cast<uint4*>(buf + lane * 128 + ((ch ^ (lane & 7)) * 16)) =
+                            make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0 && ok) {
+                        tma_store_2d(&mapC, smem_u32(buf), n, row0);
+                        bulk_commit();
+                    }
+                } else {
+                    if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
+                    if (row_ok && n + 16 < p.N)
+                        store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -655,6 +690,7 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
             named_barrier(2, 128);
         }
     }
+    if (warp >= 2 && lane == 0) bulk_wait_all();  // epilogue stores complete before exit
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // the even CTA's last commits target this CTA's barriers
@@ -788,8 +824,22 @@ static void plan_split(GemmParams& p, int tiles, void* ws, size_t ws_bytes, int 
 
 template <int EPI, bool S32>
 static int launch_tc2(const GemmParams& p, const int32_t* A, const int32_t* BT, cudaStream_t st, int slot) {
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mc;
     if (!make_map(&ma, A, p.M, p.K, P2_ROWS) || !make_map(&mb, BT, p.N, p.K, P2_ROWS)) return B2_ERR_CUDA;
+    // fp32 / int32 output map with 32 x 32 boxes in the 128-byte swizzle, when the row pitch
+    // and base allow TMA (else the kernel stores directly)
+    int c_tma = ((p.N & 3) == 0 && ((uintptr_t)p.C & 15) == 0) ? 1 : 0;
+    if (c_tma) {
+        EncodeTiledFn enc = get_encode_fn();
+        cuuint64_t dims[2] = {(cuuint64_t)p.N, (cuuint64_t)p.M};
+        cuuint64_t strides[1] = {(cuuint64_t)p.N * 4};
+        cuuint32_t box[2] = {32, 32};
+        cuuint32_t estr[2] = {1, 1};
+        c_tma = enc && enc(&mc, S32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.C, dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    if (!c_tma) memset(&mc, 0, sizeof(mc));
     auto kfn = int8_gemm_tc2_kernel<EPI, S32>;
     if (!set_smem_attr_once((const void*)kfn, P2_SMEM, slot)) return B2_ERR_CUDA;
     const int tiles = ((p.N + P2_BN - 1) / P2_BN) * ((p.M + 2 * P2_ROWS - 1) / (2 * P2_ROWS));
@@ -806,7 +856,7 @@ static int launch_tc2(const GemmParams& p, const int32_t* A, const int32_t* BT, 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kfn, ma, mb, p) == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return cudaLaunchKernelEx(&cfg, kfn, ma, mb, mc, p, c_tma) == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
 template <int EPI, bool S32>
