@@ -73,7 +73,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
                 print(err)
     if force or jobs or _stale(LIB, objs):
         run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
-             *objs, "-o", LIB, "-lcudart", "-lnccl"])
+             *objs, "-o", LIB, "-lcudart", "-ldl"])
     return LIB
 
 

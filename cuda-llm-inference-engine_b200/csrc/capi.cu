@@ -3,6 +3,8 @@
 #include "common.cuh"
 #include "b2_reference_api.h"
 #include <mutex>
+#include <set>
+#include <utility>
 
 namespace b2 {
 
@@ -19,7 +21,6 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
 size_t gemm_workspace_size(int M, int N, int K);
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxSlots = 64;
 
 int num_sms_current_device() {
     static int cache[kMaxDevices] = {0};
@@ -33,17 +34,17 @@ int num_sms_current_device() {
     return cache[dev];
 }
 
-// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel slot, device).
-bool set_smem_attr_once(const void* func, int bytes, int slot) {
-    static unsigned long long done[kMaxDevices] = {0};
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device). `slot` is
+// unused (kept for call-site compatibility); the kernel's address identifies it.
+bool set_smem_attr_once(const void* func, int bytes, int /*slot*/) {
+    static std::set<std::pair<int, const void*>> done;
     static std::mutex mu;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= kMaxSlots)
-        return false;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
     std::lock_guard<std::mutex> lk(mu);
-    if (done[dev] & (1ull << slot)) return true;
+    if (done.count({dev, func})) return true;
     if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
-    done[dev] |= 1ull << slot;
+    done.insert({dev, func});
     return true;
 }
 

@@ -5,6 +5,7 @@
 #include "b2engine.h"
 #include <cuda_bf16.h>
 #include <nccl.h>
+#include <dlfcn.h>
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -13,6 +14,7 @@
 #include <random>
 #include <string>
 #include <vector>
+#include <mutex>
 #include <sys/stat.h>
 
 namespace b2 {
@@ -25,6 +27,34 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
                 const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
                 void* ws = nullptr, size_t ws_bytes = 0);
 size_t gemm_workspace_size(int M, int N, int K);
+
+// NCCL is resolved at run time, only when tensor parallelism is used, preferring a
+// libnccl.so.2 the process already loaded (e.g. PyTorch's), so loading this library never
+// forces a second NCCL version into a process.
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    bool ok = false;
+};
+
+const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
+        api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy;
+    });
+    return api;
+}
 
 constexpr int kBlock = 16;        // KV block size (reference engine: block_size_ = 16)
 constexpr float kLnEps = 1e-5f;   // reference LayerNorm eps (15_layernorm_residual.cuh default)
@@ -137,7 +167,7 @@ b2_engine::~b2_engine() {
     cudaGetDevice(&cur);
     cudaSetDevice(device);
     if (graph) cudaGraphExecDestroy(graph);
-    if (comm) ncclCommDestroy(comm);
+    if (comm) nccl().CommDestroy(comm);
     for (void* p : allocs) cudaFree(p);
     cudaSetDevice(cur);
 }
@@ -303,10 +333,18 @@ namespace {
 // the step reads only constant weights before its griddep_wait().
 struct PdlScope {
     bool saved;
+#ifdef B2_EXP_NOPDL
+    PdlScope() : saved(pdl_enabled()) { pdl_enabled() = false; }
+#else
     PdlScope() : saved(pdl_enabled()) { pdl_enabled() = true; }
+#endif
     ~PdlScope() { pdl_enabled() = saved; }
 };
 
+#ifndef B2_EXP_SKIP
+#define B2_EXP_SKIP 0
+#endif
+#define B2_X(bit, call) ((B2_EXP_SKIP & (bit)) ? B2_OK : (call))
 int enqueue_step(b2_engine* e, cudaStream_t st) {
     PdlScope pdl;
     const b2_gpt2_config& c = e->cfg;
@@ -319,7 +357,7 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
     const int Hl = e->Hl, dl = e->dl, ffl = e->ffl;
     // all-reduces of the tensor-parallel step (NCCL on the step's stream; captured in the graph)
     auto allreduce = [&](void* buf, size_t n, ncclDataType_t t, ncclRedOp_t op) {
-        return ncclAllReduce(buf, buf, n, t, op, e->comm, st) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
+        return nccl().AllReduce(buf, buf, n, t, op, e->comm, st) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
     };
     // row-parallel linear: global-scale quantisation of this rank's activation columns,
     // local int32 GEMM over them, int32 all-reduce (exact), then the dequant epilogue
@@ -339,11 +377,11 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         unsigned char* kc = static_cast<unsigned char*>(e->k_pool) + (size_t)l * e->layer_stride * kvb;
         unsigned char* vc = static_cast<unsigned char*>(e->v_pool) + (size_t)l * e->layer_stride * kvb;
         // attention sub-block (pre-norm; x stays the residual and is updated in place)
-        B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
-        B2_TRY(gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
-                           false, st));
-        B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
-                                  vc, e->kv_dtype, st));
+        B2_TRY(B2_X(4, launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st)));
+        B2_TRY(B2_X(16, gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
+                           false, st)));
+        B2_TRY(B2_X(1, launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
+                                  vc, e->kv_dtype, st)));
         b2_decode_attn_args a{};
         a.B = B; a.H_q = Hl; a.H_kv = Hl; a.head_dim = dh;
         a.Q = e->q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;
@@ -351,30 +389,30 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         a.max_context_len = c.max_seq_len; a.block_size = kBlock; a.num_blocks_per_seq = e->blocks_per_seq;
         a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = e->attn;
         a.workspace = e->attn_ws; a.workspace_bytes = e->attn_ws_bytes;
-        B2_TRY(decode_attn_launch(&a, 64, true, st));
+        B2_TRY(B2_X(8, decode_attn_launch(&a, 64, true, st)));
         if (tp) {
             B2_TRY(row_parallel(e->attn, dl, L.out));
         } else {
-            B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
-            B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
-                               false, st));
+            B2_TRY(B2_X(2, quantize_launch(B, d, e->attn, e->xq, e->xs, st)));
+            B2_TRY(B2_X(16, gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+                               false, st)));
         }
         // MLP sub-block
-        B2_TRY(launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st));
-        B2_TRY(gemm_launch(B, ffl, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
-                           false, st));
+        B2_TRY(B2_X(4, launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st)));
+        B2_TRY(B2_X(16, gemm_launch(B, ffl, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
+                           false, st)));
         if (tp) {
             B2_TRY(row_parallel(e->hbuf, ffl, L.down));
         } else {
-            B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
-            B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
-                               B2_EPI_BIAS_RESIDUAL, false, st));
+            B2_TRY(B2_X(2, quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st)));
+            B2_TRY(B2_X(16, gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
+                               B2_EPI_BIAS_RESIDUAL, false, st)));
         }
     }
     B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
                            e->xf_lo));
-    B2_TRY(launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
-                               e->keep_logits ? e->logits : nullptr, e->keys, st, e->v0));
+    B2_TRY(B2_X(32, launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
+                               e->keep_logits ? e->logits : nullptr, e->keys, st, e->v0)));
     if (tp) B2_TRY(allreduce(e->keys, B, ncclUint64, ncclMax));  // global argmax over the vocab shards
     B2_TRY(launch_advance(B, e->keys, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
                           e->out_stride, c.max_seq_len, st));
@@ -450,7 +488,7 @@ int create_random_impl(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, u
     if (st == B2_OK && world > 1) {
         ncclUniqueId id;
         memcpy(&id, nccl_id, sizeof(id));
-        if (ncclCommInitRank(&e->comm, world, id, rank) != ncclSuccess) st = B2_ERR_CUDA;
+        if (!nccl().ok || nccl().CommInitRank(&e->comm, world, id, rank) != ncclSuccess) st = B2_ERR_CUDA;
     }
     if (st == B2_OK) st = alloc_weights(e);
     if (st == B2_OK) st = alloc_runtime(e);
@@ -512,7 +550,7 @@ int b2_engine_create_random(const b2_gpt2_config* cfg, int max_batch, int kv_dty
 int b2_nccl_unique_id(void* out, size_t bytes) {
     if (!out || bytes < sizeof(ncclUniqueId)) return B2_ERR_INVALID;
     ncclUniqueId id;
-    if (ncclGetUniqueId(&id) != ncclSuccess) return B2_ERR_CUDA;
+    if (!nccl().ok || nccl().GetUniqueId(&id) != ncclSuccess) return B2_ERR_CUDA;
     memcpy(out, &id, sizeof(id));
     return B2_OK;
 }

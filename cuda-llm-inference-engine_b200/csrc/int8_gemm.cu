@@ -107,6 +107,10 @@ struct GemmParams {
     int k_splits, kb_per_split;
     int32_t* ws;
     unsigned int* counters;
+    // rows of A each stage loads (box height of A's tensor map): 128, or M rounded up to 8
+    // when the output has a single 128-row tile (rows past it hold stale data whose
+    // accumulator rows the epilogue never stores)
+    int a_rows;
 };
 
 template <int BN>
@@ -256,7 +260,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                 npre = min(C::STAGES, kb1 - kb0);
                 for (int i = 0; i < npre; ++i) {
                     const uint32_t b_s = sbase + i * C::STAGE + C::A_BYTES;
-                    mbar_arrive_expect_tx(full_bar(i), C::STAGE);
+                    mbar_arrive_expect_tx(full_bar(i), p.a_rows * GM_BK + C::B_BYTES);
                     tma_load_2d(b_s, &mapB, (kb0 + i) * GM_BK, nt * BN, full_bar(i), pol);
                 }
             }
@@ -283,7 +287,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                             break;
                         }
                     }
-                    mbar_arrive_expect_tx(full_bar(s), C::STAGE);
+                    mbar_arrive_expect_tx(full_bar(s), p.a_rows * GM_BK + C::B_BYTES);
                     tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
                     tma_load_2d(b_s, &mapB, kb * GM_BK, nt * BN, full_bar(s), pol);
                 }
@@ -787,7 +791,7 @@ template <int BN, int EPI, bool S32>
 static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, cudaStream_t st, int slot) {
     using C = GemmCfg<BN>;
     CUtensorMap ma, mb;
-    if (!make_map(&ma, A, p.M, p.K, GM_BM) || !make_map(&mb, BT, p.N, p.K, BN)) return B2_ERR_CUDA;
+    if (!make_map(&ma, A, p.M, p.K, p.a_rows) || !make_map(&mb, BT, p.N, p.K, BN)) return B2_ERR_CUDA;
     auto kfn = int8_gemm_tc_kernel<BN, EPI, S32>;
     if (!set_smem_attr_once((const void*)kfn, C::SMEM, slot)) return B2_ERR_CUDA;
     const int tiles = ((p.N + BN - 1) / BN) * ((p.M + GM_BM - 1) / GM_BM);
@@ -888,6 +892,12 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
         plan_split(p, t128, nullptr, 0, sms);
         return launch_tc<128, EPI, S32>(p, A, BT, st, slot_base + 1);
     }
+    // skinny outputs (decode: M = batch): 32-column tiles double the CTAs streaming the weights
+    const int t32 = mt * ((p.N + 31) / 32);
+    if (!ws && t64 * 2 <= sms && t32 <= sms) {
+        plan_split(p, t32, nullptr, 0, sms);
+        return launch_tc<32, EPI, S32>(p, A, BT, st, 48 + EPI + (S32 ? 4 : 0));
+    }
     plan_split(p, t64, S32 ? nullptr : ws, ws_bytes, sms);  // the raw-int32 view is never split
     return launch_tc<64, EPI, S32>(p, A, BT, st, slot_base + 2);
 }
@@ -915,7 +925,8 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
         if (epi != B2_EPI_PLAIN && !bias) return B2_ERR_INVALID;
         if (epi == B2_EPI_BIAS_RESIDUAL && !residual) return B2_ERR_INVALID;
     }
-    GemmParams p{M, N, K, sA, sB, bias, residual, C, device_error_ptr(), 1, 0, nullptr, nullptr};
+    GemmParams p{M, N, K, sA, sB, bias, residual, C, device_error_ptr(), 1, 0, nullptr, nullptr,
+                 M <= GM_BM ? ((M + 7) & ~7) : GM_BM};
     if (s32) return gemm_dispatch<B2_EPI_PLAIN, true>(p, A, BT, ws, ws_bytes, st);
     switch (epi) {
         case B2_EPI_PLAIN: return gemm_dispatch<B2_EPI_PLAIN, false>(p, A, BT, ws, ws_bytes, st);

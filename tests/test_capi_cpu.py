@@ -4,6 +4,7 @@ import ctypes
 import os
 import re
 import subprocess
+import sys
 
 import pytest
 
@@ -75,3 +76,13 @@ def test_workspace_size_query(b2):
 def test_missing_library_fails_loudly(b2, tmp_path):
     with pytest.raises(b2.B2Error, match="no CPU fallback"):
         b2.load_library(str(tmp_path / "nope.so"))
+
+
+def test_library_before_torch_keeps_torch_importable():
+    """Loading the library first must not pull a second NCCL into the process (NCCL is
+    resolved at run time only for tensor parallelism), so torch still imports afterwards."""
+    code = ("import sys, importlib; sys.path.insert(0, %r); "
+            "b2 = importlib.import_module('cuda-llm-inference-engine_b200'); b2.load_library(); "
+            "import torch; print('ok')" % ROOT)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
