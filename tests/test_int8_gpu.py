@@ -190,3 +190,49 @@ def test_gemm_split_k_bit_exact(b2, oracle, cuda, M, N, K, epi):
     else:
         np.testing.assert_array_equal(g.view(np.uint32), want.view(np.uint32))
     assert int(ws[:256].view(torch.int32).abs().sum()) == 0  # tickets back to zero
+
+
+# Decode-size GEMMs (M <= 128: one row tile, skinny 32-column tiles, A boxes trimmed to the
+# batch rows): every epilogue and the raw int32 view, ragged M and N, K tails.
+DECODE_SHAPES = [
+    (64, 768, 3072),     # GPT-2 FC2
+    (64, 2304, 768),     # GPT-2 QKV
+    (1, 768, 768),       # one sequence
+    (33, 1000, 640),     # ragged last tile
+    (7, 130, 1040),      # N % 4 != 0 (scalar stores), K tail of 16 past the last full k-block
+    (128, 2048, 4096),   # config-5 shard: full 128-row tile
+    (100, 200, 48),      # one k-block
+    (120, 4100, 272),    # wide N, 3 k-blocks
+]
+
+
+@pytest.mark.parametrize("M,N,K", DECODE_SHAPES)
+@pytest.mark.parametrize("epi", [0, 1, 2, 3, "s32"])
+def test_gemm_decode_shapes_bit_exact(b2, oracle, cuda, M, N, K, epi):
+    import torch
+
+    rng = np.random.default_rng(M * 13 + N * 5 + K)
+    A, Bt = quantized_pair(rng, M, N, K)
+    Ap, sA = oracle.quantize(A)
+    Bp, sB = oracle.quantize(Bt)
+    acc = oracle.int8_gemm_s32(Ap, Bp, nthreads=0)
+    t = {k: dev(torch, v, cuda) for k, v in dict(Ap=Ap, Bp=Bp, sA=sA, sB=sB).items()}
+    if epi == "s32":
+        for _ in range(2):  # repeated launches: nothing is left behind between calls
+            got = b2.int8_gemm_s32(t["Ap"], t["Bp"])
+            torch.cuda.synchronize()
+            assert b2.device_error() == 0
+            np.testing.assert_array_equal(got.cpu().numpy(), acc)
+        return
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    want = oracle.epilogue(acc, sA, sB, bias, res, epi)
+    got = b2.int8_gemm(t["Ap"], t["Bp"], t["sA"], t["sB"], dev(torch, bias, cuda) if epi else None,
+                       dev(torch, res, cuda) if epi == 3 else None, epilogue=epi)
+    torch.cuda.synchronize()
+    assert b2.device_error() == 0
+    g = got.cpu().numpy()
+    if epi == 2:
+        np.testing.assert_allclose(g, want, rtol=1e-4, atol=1e-6)
+    else:
+        np.testing.assert_array_equal(g.view(np.uint32), want.view(np.uint32))
