@@ -466,13 +466,20 @@ struct SplitPlan {
 };
 
 // Split policy: enough CTAs to fill the GPU a few times over, and no CTA streaming more
-// than ~512 KB of K+V, so ragged batches balance; capped by max_splits.
+// than ~512 KB of K+V, so ragged batches balance; capped by max_splits. When the
+// (sequence, KV head) pairs cannot fill the SMs (a shard of the heads on one of several
+// GPUs), CTAs shrink (down to 256 tokens) so that the upper bound B * H_kv * max_ctx of the
+// work spans ~4 waves of 3 CTAs per SM.
 static SplitPlan plan_splits(int B, int H_kv, int head_dim, int kv_bytes, int max_ctx, int block_size,
                              int max_splits, int num_sms) {
     const int max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
     const long long pairs = (long long)B * H_kv;
     const long long row_bytes = 2LL * head_dim * kv_bytes;           // K + V bytes per token
-    const long long tok_per_cta = std::max<long long>(64, (512LL * 1024) / row_bytes);
+    const long long cap_tok = (512LL * 1024) / row_bytes;
+    const long long waves_tok = pairs * max_ctx / (4LL * DA_MINB * num_sms);
+    const long long tok_per_cta =
+        pairs >= num_sms ? std::max<long long>(64, cap_tok)
+                         : std::max<long long>(256, std::min<long long>(waves_tok, cap_tok));
     long long want = std::max<long long>((4LL * num_sms + pairs - 1) / pairs,
                                          ((long long)max_ctx + tok_per_cta - 1) / tok_per_cta);
     // at least 2 blocks (32 tokens) of work per split
