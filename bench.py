@@ -444,6 +444,7 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
     by = gpt2_step_bytes(cfg, B, ctx_mean)
     step_s = gen_ms / steps_new * 1e-3
     toks = eng.tokens()
+    breakdown = parse_profile(eng.profile_step())
     eng.close()
     return {"tok_s": round(B * steps_new / (gen_ms * 1e-3), 1), "ms_per_step": round(gen_ms / steps_new, 4),
             "prefill_tok_s": round(B * (prompt_len - 1) / (pre_ms * 1e-3), 1),
@@ -451,11 +452,22 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
             "frac_of_hbm_bound": round(by / step_s / 1e9 / hbm_peak, 4),
             "hbm_bound_tok_s": round(B / (by / (hbm_peak * 1e9)), 1),
             "generated_tokens_valid": bool((toks[:, prompt_len:prompt_len + steps_new] >= 0).all()),
-            "timing": "CUDA graph replays of one decode step"}
+            "timing": "CUDA graph replays of one decode step", "step_breakdown": breakdown}
 
 
 WIDE = dict(n_layers=32, n_heads=32, d_model=4096, d_ff=16384, vocab_size=50257, max_seq_len=4096 + 64 + 1,
             d_head=128)
+
+
+def parse_profile(text):
+    """Engine.profile_step() report -> {"step_us": T, "us": {kernel class: total µs}} (eager
+    step with an event before every launch: a breakdown, not a timing of record)."""
+    lines = text.strip().splitlines()
+    out = {"step_us": float(lines[0].split()[1]), "us": {}}
+    for ln in lines[1:]:
+        f = ln.split()
+        out["us"][f[0]] = float(f[2])
+    return out
 
 
 def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B=128):
@@ -486,6 +498,7 @@ def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
     assert b2.device_error() == 0
+    breakdown = parse_profile(eng.profile_step())  # every rank takes part (collectives inside)
     d, L = cfg["d_model"], cfg["n_layers"]
     ctx_mean = ctx + 2 + (steps - 1) / 2.0 + 1
     lin = L * (3 * d * d + d * d + 2 * cfg["d_ff"] * d)
@@ -497,8 +510,11 @@ def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B
             "step_bytes_all_ranks": int(by_total), "gbs_all_ranks": round(by_total / step_s / 1e9, 1),
             "frac_of_hbm_bound": round(by_total / step_s / 1e9 / (hbm_peak * world), 4),
             "hbm_bound_tok_s": round(B / (by_total / (hbm_peak * 1e9 * world)), 1),
-            "parallelism": f"tensor-parallel x{world} (NCCL all-reduce after proj and FC2)",
-            "context": "seeded synthetic KV fill of 4096 tokens, then 2 warm-up + 64 timed steps"}
+            "parallelism": f"tensor-parallel x{world} (row-parallel out-proj and FC2: "
+                           + ("NCCL all-reduces" if os.environ.get("B2_TP_COLLECTIVES") == "nccl"
+                              else "peer-memory scale exchange and int32 reduce kernels over NVLink") + ")",
+            "context": "seeded synthetic KV fill of 4096 tokens, then 2 warm-up + 64 timed steps",
+            "step_breakdown_rank0": breakdown}
 
 
 def cpu_baseline(torch, q, kc, vc, bt, lens):

@@ -333,7 +333,8 @@ class GPT2Config(ctypes.Structure):
 ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_nccl_unique_id", "b2_engine_create_random_tp",
                   "b2_engine_fill_kv_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
                   "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps",
-                  "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions"]
+                  "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions",
+                  "b2_engine_profile_step"]
 
 
 def _engine_lib():
@@ -354,6 +355,7 @@ def _engine_lib():
     lib.b2_engine_start.argtypes = [vp, i, vp, vp, i, i, u64]
     lib.b2_engine_step.argtypes = [vp, vp]
     lib.b2_engine_run_steps.argtypes = [vp, i, vp]
+    lib.b2_engine_profile_step.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
     lib.b2_engine_read_tokens.argtypes = [vp, vp, i]
     lib.b2_engine_keep_logits.argtypes = [vp, i, ctypes.POINTER(vp)]
     lib.b2_engine_read_logits.argtypes = [vp, vp]
@@ -435,6 +437,13 @@ class Engine:
 
     def run_steps(self, steps: int, stream=None):
         _check(self._lib.b2_engine_run_steps(self._h, steps, _stream(stream)), "b2_engine_run_steps")
+
+    def profile_step(self) -> str:
+        """One eager step with a CUDA event before every launch; returns the per-kernel-class
+        breakdown (b2_engine_profile_step). Under tensor parallelism every rank must call it."""
+        buf = ctypes.create_string_buffer(8192)
+        _check(self._lib.b2_engine_profile_step(self._h, buf, ctypes.sizeof(buf)), "b2_engine_profile_step")
+        return buf.value.decode()
 
     def keep_logits(self, enable: bool = True):
         _check(self._lib.b2_engine_keep_logits(self._h, 1 if enable else 0, None), "b2_engine_keep_logits")

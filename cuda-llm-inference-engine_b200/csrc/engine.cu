@@ -1,6 +1,7 @@
 // Batched GPT-2 INT8 decode engine (include/b2engine.h): weights, paged KV pool, block
 // allocator, the decode step as a fixed launch sequence, and its CUDA-graph replay.
 #include "common.cuh"
+#include "tp_collectives.cuh"
 #include "engine_kernels.cuh"
 #include "b2engine.h"
 #include <cuda_bf16.h>
@@ -37,6 +38,7 @@ struct NcclApi {
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     bool ok = false;
 };
 
@@ -51,7 +53,8 @@ const NcclApi& nccl() {
         api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
         api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
-        api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy;
+        api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+        api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy && api.AllGather;
     });
     return api;
 }
@@ -116,6 +119,12 @@ struct b2_engine {
     int tp_rank = 0, tp_size = 1;
     int Hl = 0, dl = 0, ffl = 0, v0 = 0, Vl = 0;
     ncclComm_t comm = nullptr;
+    // peer-memory collectives (tp_collectives.cu): every rank's x, acc32 and exchange region
+    // mapped into this process; p2p = false falls back to NCCL all-reduces
+    bool p2p = false;
+    TpPeers peers{};
+    unsigned char* xchg = nullptr;
+    std::vector<void*> ipc_opened;
     float* amax = nullptr;    // [B] row absmax (row-parallel quantisation)
     int32_t* acc32 = nullptr; // [B, d] int32 partials of the row-parallel linears
     std::vector<void*> allocs;  // every device allocation, freed by the destructor
@@ -167,6 +176,8 @@ b2_engine::~b2_engine() {
     cudaGetDevice(&cur);
     cudaSetDevice(device);
     if (graph) cudaGraphExecDestroy(graph);
+    cudaDeviceSynchronize();
+    for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
     if (comm) nccl().CommDestroy(comm);
     for (void* p : allocs) cudaFree(p);
     cudaSetDevice(cur);
@@ -333,25 +344,40 @@ namespace {
 // the step reads only constant weights before its griddep_wait().
 struct PdlScope {
     bool saved;
-#ifdef B2_EXP_NOPDL
-    PdlScope() : saved(pdl_enabled()) { pdl_enabled() = false; }
-#else
     PdlScope() : saved(pdl_enabled()) { pdl_enabled() = true; }
-#endif
     ~PdlScope() { pdl_enabled() = saved; }
 };
 
-#ifndef B2_EXP_SKIP
-#define B2_EXP_SKIP 0
-#endif
-#define B2_X(bit, call) ((B2_EXP_SKIP & (bit)) ? B2_OK : (call))
-int enqueue_step(b2_engine* e, cudaStream_t st) {
+// Optional per-launch timing of one eager step: an event is recorded on the step's stream
+// before every launch (and after the last), and the intervals are summed per label. The
+// events serialise the launches (no programmatic overlap), so the report is a breakdown of
+// where a step goes, not a faster or slower step.
+struct StepProfiler {
+    cudaStream_t st = nullptr;
+    std::vector<std::pair<const char*, cudaEvent_t>> marks;
+    bool ok = true;
+    void mark(const char* label) {
+        cudaEvent_t ev = nullptr;
+        if (cudaEventCreate(&ev) != cudaSuccess || cudaEventRecord(ev, st) != cudaSuccess) ok = false;
+        marks.push_back({label, ev});
+    }
+    ~StepProfiler() {
+        for (auto& m : marks)
+            if (m.second) cudaEventDestroy(m.second);
+    }
+};
+
+int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
     PdlScope pdl;
+    auto M = [&](const char* label) {
+        if (prof) prof->mark(label);
+    };
     const b2_gpt2_config& c = e->cfg;
     const int B = e->batch, d = c.d_model, ff = c.d_ff, H = c.n_heads, dh = c.d_head;
     const size_t kvb = e->kv_dtype == B2_KV_F32 ? 4 : 2;
     int r;
 #define B2_TRY(x) do { if ((r = (x)) != B2_OK) return r; } while (0)
+    M("embed");
     B2_TRY(launch_embed(B, d, e->tokens, e->pos, e->wte, e->wpe, e->x, e->ctx, e->keys, st));
     const bool tp = e->tp_size > 1;
     const int Hl = e->Hl, dl = e->dl, ffl = e->ffl;
@@ -361,15 +387,31 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
     };
     // row-parallel linear: global-scale quantisation of this rank's activation columns,
     // local int32 GEMM over them, int32 all-reduce (exact), then the dequant epilogue
-    auto row_parallel = [&](const float* act, int kl, const QLinear& W) {
+    auto row_parallel = [&](const float* act, int kl, const QLinear& W, const char* gemm_label) {
         int r2;
+        if (e->p2p) {
+            M("tp_quantize");
+            if ((r2 = launch_tp_quantize(B, kl, act, e->xq, e->xs, e->peers, st)) != B2_OK) return r2;
+            M(gemm_label);
+            if ((r2 = gemm_launch(B, d, kl, e->xq, W.w, nullptr, nullptr, nullptr, nullptr, e->acc32, B2_EPI_PLAIN,
+                                  true, st)) != B2_OK)
+                return r2;
+            M("tp_reduce");
+            return launch_tp_reduce(B, d, e->xs, W.s, W.bias, e->peers, st);
+        }
+        M("rowmax");
         if ((r2 = launch_rowmax(B, kl, act, e->amax, st)) != B2_OK) return r2;
+        M("allreduce_amax");
         if ((r2 = allreduce(e->amax, B, ncclFloat, ncclMax)) != B2_OK) return r2;
+        M("quantize_scaled");
         if ((r2 = launch_quantize_scaled(B, kl, act, e->amax, e->xq, e->xs, st)) != B2_OK) return r2;
+        M(gemm_label);
         if ((r2 = gemm_launch(B, d, kl, e->xq, W.w, nullptr, nullptr, nullptr, nullptr, e->acc32, B2_EPI_PLAIN, true,
                               st)) != B2_OK)
             return r2;
+        M("allreduce_partials");
         if ((r2 = allreduce(e->acc32, (size_t)B * d, ncclInt32, ncclSum)) != B2_OK) return r2;
+        M("dequant_residual");
         return launch_dequant_residual(B, d, e->acc32, e->xs, W.s, W.bias, e->x, e->x, st);
     };
     for (int l = 0; l < c.n_layers; ++l) {
@@ -377,11 +419,14 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         unsigned char* kc = static_cast<unsigned char*>(e->k_pool) + (size_t)l * e->layer_stride * kvb;
         unsigned char* vc = static_cast<unsigned char*>(e->v_pool) + (size_t)l * e->layer_stride * kvb;
         // attention sub-block (pre-norm; x stays the residual and is updated in place)
-        B2_TRY(B2_X(4, launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st)));
-        B2_TRY(B2_X(16, gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
-                           false, st)));
-        B2_TRY(B2_X(1, launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
-                                  vc, e->kv_dtype, st)));
+        M("ln_quant");
+        B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
+        M("gemm_qkv");
+        B2_TRY(gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS, false,
+                           st));
+        M("qkv_scatter");
+        B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc, vc,
+                                  e->kv_dtype, st));
         b2_decode_attn_args a{};
         a.B = B; a.H_q = Hl; a.H_kv = Hl; a.head_dim = dh;
         a.Q = e->q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;
@@ -389,34 +434,121 @@ int enqueue_step(b2_engine* e, cudaStream_t st) {
         a.max_context_len = c.max_seq_len; a.block_size = kBlock; a.num_blocks_per_seq = e->blocks_per_seq;
         a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = e->attn;
         a.workspace = e->attn_ws; a.workspace_bytes = e->attn_ws_bytes;
-        B2_TRY(B2_X(8, decode_attn_launch(&a, 64, true, st)));
+        M("attention");
+        B2_TRY(decode_attn_launch(&a, 64, true, st));
         if (tp) {
-            B2_TRY(row_parallel(e->attn, dl, L.out));
+            B2_TRY(row_parallel(e->attn, dl, L.out, "gemm_out"));
         } else {
-            B2_TRY(B2_X(2, quantize_launch(B, d, e->attn, e->xq, e->xs, st)));
-            B2_TRY(B2_X(16, gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
-                               false, st)));
+            M("quantize");
+            B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
+            M("gemm_out");
+            B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+                               false, st));
         }
         // MLP sub-block
-        B2_TRY(B2_X(4, launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st)));
-        B2_TRY(B2_X(16, gemm_launch(B, ffl, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU,
-                           false, st)));
+        M("ln_quant");
+        B2_TRY(launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st));
+        M("gemm_fc1");
+        B2_TRY(gemm_launch(B, ffl, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU, false,
+                           st));
         if (tp) {
-            B2_TRY(row_parallel(e->hbuf, ffl, L.down));
+            B2_TRY(row_parallel(e->hbuf, ffl, L.down, "gemm_fc2"));
         } else {
-            B2_TRY(B2_X(2, quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st)));
-            B2_TRY(B2_X(16, gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x,
-                               B2_EPI_BIAS_RESIDUAL, false, st)));
+            M("quantize");
+            B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
+            M("gemm_fc2");
+            B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+                               false, st));
         }
     }
+    M("ln_final");
     B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
                            e->xf_lo));
-    B2_TRY(B2_X(32, launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
+    M("vocab_argmax");
+    B2_TRY((launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
                                e->keep_logits ? e->logits : nullptr, e->keys, st, e->v0)));
-    if (tp) B2_TRY(allreduce(e->keys, B, ncclUint64, ncclMax));  // global argmax over the vocab shards
+    if (tp) {
+        M("allreduce_keys");
+        B2_TRY(allreduce(e->keys, B, ncclUint64, ncclMax));  // global argmax over the vocab shards
+    }
+    M("advance");
     B2_TRY(launch_advance(B, e->keys, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
                           e->out_stride, c.max_seq_len, st));
 #undef B2_TRY
+    return B2_OK;
+}
+
+// Maps every rank's x, acc32 and exchange region into this process for the peer-memory
+// collectives: CUDA IPC handles all-gathered over the engine's NCCL communicator. Every rank
+// runs the same collectives whatever happens locally, and all ranks agree (all-reduce min)
+// before switching p2p on, so a failure on one rank leaves every rank on NCCL all-reduces.
+// The closing all-reduce is also the barrier after which peers may write into this rank's
+// zeroed exchange region. B2_TP_COLLECTIVES=nccl keeps the NCCL path.
+// A rank whose allocations failed (local_ok false) still takes part, so no rank is left
+// waiting in a collective.
+int setup_peers(b2_engine* e, bool local_ok) {
+    const int world = e->tp_size, rank = e->tp_rank;
+    const char* env = getenv("B2_TP_COLLECTIVES");
+    if (!e->comm || world < 2 || world > TP_MAX_RANKS || (env && strcmp(env, "nccl") == 0)) return B2_OK;
+    const TpLayout L = TpLayout::make(e->max_batch);
+    e->xchg = local_ok ? e->alloc<unsigned char>(L.bytes) : nullptr;
+    struct Blob {
+        cudaIpcMemHandle_t h[3];
+        int ok;
+        int pad[15];
+    };
+    Blob mine{};
+    mine.ok = local_ok && e->xchg && (e->cfg.d_model % 4) == 0 && cudaMemset(e->xchg, 0, L.bytes) == cudaSuccess &&
+              cudaIpcGetMemHandle(&mine.h[0], e->x) == cudaSuccess &&
+              cudaIpcGetMemHandle(&mine.h[1], e->acc32) == cudaSuccess &&
+              cudaIpcGetMemHandle(&mine.h[2], e->xchg) == cudaSuccess;
+    unsigned char* dbuf = nullptr;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMalloc(&dbuf, (size_t)(world + 1) * sizeof(Blob) + 16) != cudaSuccess)
+        return B2_ERR_CUDA;
+    std::vector<Blob> all(world);
+    int agreed = 0;
+    bool nccl_ok = cudaMemcpy(dbuf, &mine, sizeof(Blob), cudaMemcpyHostToDevice) == cudaSuccess &&
+                   nccl().AllGather(dbuf, dbuf + sizeof(Blob), sizeof(Blob), ncclUint8, e->comm, 0) == ncclSuccess &&
+                   cudaMemcpy(all.data(), dbuf + sizeof(Blob), world * sizeof(Blob), cudaMemcpyDeviceToHost) ==
+                       cudaSuccess;
+    TpPeers P{};
+    int opened = nccl_ok ? 1 : 0;
+    for (int p = 0; p < world; ++p) opened = opened && all[p].ok;
+    for (int p = 0; opened && p < world; ++p) {
+        if (p == rank) {
+            P.x[p] = e->x;
+            P.acc[p] = e->acc32;
+            P.xchg[p] = e->xchg;
+            continue;
+        }
+        void* ptr[3] = {nullptr, nullptr, nullptr};
+        for (int k = 0; k < 3 && opened; ++k) {
+            if (cudaIpcOpenMemHandle(&ptr[k], all[p].h[k], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess)
+                e->ipc_opened.push_back(ptr[k]);
+            else
+                opened = 0;
+        }
+        P.x[p] = static_cast<float*>(ptr[0]);
+        P.acc[p] = static_cast<const int32_t*>(ptr[1]);
+        P.xchg[p] = static_cast<unsigned char*>(ptr[2]);
+    }
+    int* flag = reinterpret_cast<int*>(dbuf + (size_t)(world + 1) * sizeof(Blob));
+    nccl_ok = nccl_ok && cudaMemcpy(flag, &opened, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+              nccl().AllReduce(flag, flag, 1, ncclInt32, ncclMin, e->comm, 0) == ncclSuccess &&
+              cudaMemcpy(&agreed, flag, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(dbuf);
+    if (!nccl_ok) return B2_ERR_CUDA;
+    if (!agreed) {
+        for (void* p : e->ipc_opened) cudaIpcCloseMemHandle(p);
+        e->ipc_opened.clear();
+        return B2_OK;
+    }
+    P.L = L;
+    P.rank = rank;
+    P.world = world;
+    P.err = device_error_ptr();
+    e->peers = P;
+    e->p2p = true;
     return B2_OK;
 }
 
@@ -492,6 +624,10 @@ int create_random_impl(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, u
     }
     if (st == B2_OK) st = alloc_weights(e);
     if (st == B2_OK) st = alloc_runtime(e);
+    if (e->comm) {
+        const int sp = setup_peers(e, st == B2_OK);
+        if (st == B2_OK) st = sp;
+    }
     if (st != B2_OK) {
         delete e;
         return st;
@@ -711,6 +847,55 @@ int b2_engine_start(b2_engine* e, int batch, const int32_t* prompts_host, const 
 int b2_engine_step(b2_engine* e, b2_stream_t stream) {
     if (!e || e->batch <= 0) return B2_ERR_INVALID;
     return enqueue_step(e, static_cast<cudaStream_t>(stream));
+}
+
+int b2_engine_profile_step(b2_engine* e, char* report, size_t report_bytes) {
+    if (!e || e->batch <= 0 || !report || report_bytes == 0) return B2_ERR_INVALID;
+    cudaStream_t st;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return B2_ERR_CUDA;
+    int r = B2_OK;
+    {
+        StepProfiler prof;
+        prof.st = st;
+        r = enqueue_step(e, st, &prof);
+        prof.mark("end");
+        if (cudaStreamSynchronize(st) != cudaSuccess || !prof.ok) r = B2_ERR_CUDA;
+        if (r == B2_OK) {
+            struct Agg {
+                const char* label;
+                int n;
+                double us;
+            };
+            std::vector<Agg> agg;
+            for (size_t i = 0; i + 1 < prof.marks.size(); ++i) {
+                float ms = 0.f;
+                cudaEventElapsedTime(&ms, prof.marks[i].second, prof.marks[i + 1].second);
+                auto it = std::find_if(agg.begin(), agg.end(),
+                                       [&](const Agg& a) { return strcmp(a.label, prof.marks[i].first) == 0; });
+                if (it == agg.end()) {
+                    agg.push_back({prof.marks[i].first, 0, 0.0});
+                    it = agg.end() - 1;
+                }
+                it->n += 1;
+                it->us += ms * 1e3;
+            }
+            float total_ms = 0.f;
+            cudaEventElapsedTime(&total_ms, prof.marks.front().second, prof.marks.back().second);
+            std::sort(agg.begin(), agg.end(), [](const Agg& a, const Agg& b) { return a.us > b.us; });
+            std::string out;
+            char line[160];
+            snprintf(line, sizeof(line), "step_us %.1f launches %zu\n", total_ms * 1e3, prof.marks.size() - 1);
+            out += line;
+            for (const Agg& a : agg) {
+                snprintf(line, sizeof(line), "%-20s %5d %10.1f %6.1f%%\n", a.label, a.n, a.us,
+                         total_ms > 0.f ? 100.0 * a.us / (total_ms * 1e3) : 0.0);
+                out += line;
+            }
+            snprintf(report, report_bytes, "%s", out.c_str());
+        }
+    }
+    cudaStreamDestroy(st);
+    return r;
 }
 
 int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream) {

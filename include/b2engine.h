@@ -83,6 +83,13 @@ int b2_engine_step(b2_engine* e, b2_stream_t stream);
 /* `steps` decode steps, replayed from a CUDA graph of one step captured on first use. */
 int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream);
 
+/* Runs one decode step eagerly on a private stream with a CUDA event before every launch and
+ * writes a text breakdown into report[report_bytes]: a first line "step_us <total> launches
+ * <n>", then one line per kernel class "<label> <launches> <total µs> <share %>", largest
+ * first. The events serialise the launches, so the total is somewhat above a graph replay's.
+ * Under tensor parallelism every rank must call it for the same step. Synchronous. */
+int b2_engine_profile_step(b2_engine* e, char* report, size_t report_bytes);
+
 /* Copies the greedy token chosen at each position: out_host [batch, out_stride], entry
  * [b][p] = argmax after the step at position p-1 (-1 where no step has run). Synchronous. */
 int b2_engine_read_tokens(const b2_engine* e, int32_t* out_host, int out_stride);

@@ -1,7 +1,10 @@
 """Tensor-parallel decode (2 GPUs) equals the single-GPU engine.
 
-The sharded engine quantises row-parallel inputs with the global row scale and all-reduces
-exact int32 partials, so every int8 byte and int32 accumulator matches the unsharded run;
+The sharded engine quantises row-parallel inputs with the global row scale and sums exact
+int32 partials over the ranks, so every int8 byte and int32 accumulator matches the unsharded
+run, whether the exchange goes through the peer-memory kernels (default) or NCCL all-reduces
+(B2_TP_COLLECTIVES=nccl); after the eager steps each rank replays the step as a CUDA graph
+from a restart and must produce the same tokens;
 attention and the vocab logits are computed per head / per vocab row by the same kernels. The
 bar: identical greedy tokens and positions, and logits within 1e-5 relative (the split-K plan
 of the attention may merge a different number of splits per head shard)."""
@@ -26,14 +29,17 @@ def _need_gpus(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-@pytest.mark.parametrize("kv_dtype", [0, 1])
-def test_tp2_matches_single_gpu(b2, cuda, tmp_path, kv_dtype):
+@pytest.mark.parametrize("kv_dtype,collectives", [(0, "p2p"), (1, "p2p"), (0, "nccl")])
+def test_tp2_matches_single_gpu(b2, cuda, tmp_path, kv_dtype, collectives):
     _need_gpus(2)
     rng = np.random.default_rng(5)
     prompts = [list(map(int, rng.integers(0, CFG["vocab_size"], n))) for n in (4, 7, 2)]
     spec = dict(cfg=CFG, max_batch=3, kv_dtype=kv_dtype, seed=13, block_seed=2, prompts=prompts, new=5, steps=10)
     nid = b2.nccl_unique_id().hex()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env.pop("B2_TP_COLLECTIVES", None)
+    if collectives == "nccl":
+        env["B2_TP_COLLECTIVES"] = "nccl"
     procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "tp_worker.py"), str(r), "2", nid, json.dumps(spec),
                                str(tmp_path / f"r{r}.npz")], env=env) for r in range(2)]
     for p in procs:
@@ -50,5 +56,6 @@ def test_tp2_matches_single_gpu(b2, cuda, tmp_path, kv_dtype):
     for o in outs:
         assert np.array_equal(o["tokens"], e.tokens())
         assert np.array_equal(o["pos"], e.positions())
+        assert np.array_equal(o["graph_tokens"], e.tokens())
     tp_logits = np.concatenate([outs[0]["logits"], outs[1]["logits"]], axis=2)
     np.testing.assert_allclose(tp_logits, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())

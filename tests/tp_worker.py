@@ -3,7 +3,8 @@
     python tests/tp_worker.py RANK WORLD NCCL_ID_HEX SPEC_JSON OUT_NPZ
 
 Runs the seeded engine's steps on GPU RANK and saves the greedy tokens, the logits shard of
-every step and the final positions."""
+every step and the final positions; then restarts the same prompts and replays the step as a
+CUDA graph, saving those tokens too."""
 import importlib
 import json
 import os
@@ -32,7 +33,11 @@ def main():
         e.step()
         logits.append(e.logits())
     assert b2.device_error() == 0
-    np.savez(sys.argv[5], tokens=e.tokens(), logits=np.stack(logits), pos=e.positions())
+    tokens, pos = e.tokens(), e.positions()
+    e.start(spec["prompts"], spec["new"], seed=spec["block_seed"] + 1)
+    e.run_steps(spec["steps"])
+    assert b2.device_error() == 0
+    np.savez(sys.argv[5], tokens=tokens, logits=np.stack(logits), pos=pos, graph_tokens=e.tokens())
     e.close()
 
 
