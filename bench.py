@@ -428,7 +428,7 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
     eng = b2.Engine.random(cfg, max_batch=B, seed=SEED)
     rng = np.random.default_rng(SEED)
     prompts = [list(map(int, rng.integers(0, cfg["vocab_size"], prompt_len))) for _ in range(B)]
-    eng.start(prompts, steps_new, seed=SEED)
+    eng.start(prompts, steps_new, seed=block_seed())
     st = torch.cuda.current_stream()
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     e0.record(st)
@@ -452,11 +452,18 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
             "frac_of_hbm_bound": round(by / step_s / 1e9 / hbm_peak, 4),
             "hbm_bound_tok_s": round(B / (by / (hbm_peak * 1e9)), 1),
             "generated_tokens_valid": bool((toks[:, prompt_len:prompt_len + steps_new] >= 0).all()),
-            "timing": "CUDA graph replays of one decode step", "step_breakdown": breakdown}
+            "timing": "CUDA graph replays of one decode step", "kv_block_seed": block_seed(),
+            "step_breakdown": breakdown}
 
 
 WIDE = dict(n_layers=32, n_heads=32, d_model=4096, d_ff=16384, vocab_size=50257, max_seq_len=4096 + 64 + 1,
             d_head=128)
+
+
+def block_seed():
+    """KV block placement of the engine legs: 0 = in pool order, as the reference engine
+    allocates (src/gpt2_engine.cu:420-429); B2_BENCH_BLOCK_SEED=n scatters the blocks."""
+    return int(os.environ.get("B2_BENCH_BLOCK_SEED", "0"))
 
 
 def parse_profile(text):
@@ -483,7 +490,7 @@ def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B
     eng = b2.Engine.random_tp(cfg, B, bytes(nid.cpu().numpy().tobytes()), rank, world, kv_dtype=b2.B2_KV_BF16,
                               seed=SEED)
     rng = np.random.default_rng(SEED)
-    eng.start([[int(t)] for t in rng.integers(0, cfg["vocab_size"], B)], steps + 1, seed=SEED)
+    eng.start([[int(t)] for t in rng.integers(0, cfg["vocab_size"], B)], steps + 1, seed=block_seed())
     eng.fill_kv_random(ctx, seed=SEED)
     st = torch.cuda.current_stream()
     eng.run_steps(2, stream=st)  # warm-up (captures the graph); positions ctx, ctx+1
@@ -514,6 +521,7 @@ def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B
                            + ("NCCL all-reduces" if os.environ.get("B2_TP_COLLECTIVES") == "nccl"
                               else "peer-memory scale exchange and int32 reduce kernels over NVLink") + ")",
             "context": "seeded synthetic KV fill of 4096 tokens, then 2 warm-up + 64 timed steps",
+            "kv_block_seed": block_seed(),
             "step_breakdown_rank0": breakdown}
 
 
@@ -607,8 +615,11 @@ def run_only(args):
         # (batch 32 of the 128, so the case stays near 2 GB for profiling)
         import numpy as np
 
-        Bw, Hw, ctxw = 32, 32, 4096
-        nb = ctxw // BS
+        # B2_WIDE="B,H,ctx[,max_ctx]" overrides the shape (max_ctx: the bound passed to the launch)
+        wide = [int(v) for v in os.environ.get("B2_WIDE", "32,32,4096").split(",")]
+        Bw, Hw, ctxw = wide[:3]
+        mcw = wide[3] if len(wide) > 3 else ctxw
+        nb = (mcw + BS - 1) // BS
         P = Bw * nb
         g = torch.Generator(device=dev).manual_seed(SEED)
         kc = torch.randn(P, BS, Hw, D, generator=g, device=dev).to(torch.bfloat16)
@@ -617,8 +628,8 @@ def run_only(args):
         O = torch.empty_like(q)
         btd = torch.randperm(P, generator=g, device=dev).to(torch.int32).view(Bw, nb)
         lensd = torch.full((Bw,), ctxw, dtype=torch.int32, device=dev)
-        ws = b2.make_decode_workspace(Bw, Hw, Hw, D, ctxw, BS, device=dev)
-        fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, ctxw, O=O, workspace=ws)  # noqa: E731
+        ws = b2.make_decode_workspace(Bw, Hw, Hw, D, mcw, BS, device=dev)
+        fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, mcw, O=O, workspace=ws)  # noqa: E731
         by = attn_alg_bytes(np.full(Bw, ctxw), Hw, Hw, D, 2, nb)
     elif args.only.startswith("attn"):
         dt = torch.bfloat16 if args.only == "attn_bf16" else torch.float32

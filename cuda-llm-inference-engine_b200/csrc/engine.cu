@@ -803,12 +803,16 @@ int b2_engine_start(b2_engine* e, int batch, const int32_t* prompts_host, const 
                 return B2_ERR_INVALID;
         max_total = std::max(max_total, pl + max_new_tokens);
     }
-    // block allocator: return every block to the free list, shuffle it (seeded) so block
-    // tables are non-contiguous, then hand each sequence the blocks it can ever need
+    // block allocator: return every block to the free list and hand each sequence the blocks
+    // it can ever need. seed 0: in pool order, as the reference engine allocates
+    // (src/gpt2_engine.cu:420-429, physical block = logical block); any other seed shuffles
+    // the free list first, so block tables are scattered over the whole pool
     e->free_blocks.resize(e->num_blocks);
-    std::iota(e->free_blocks.begin(), e->free_blocks.end(), 0);
-    std::mt19937_64 rng(seed);
-    std::shuffle(e->free_blocks.begin(), e->free_blocks.end(), rng);
+    std::iota(e->free_blocks.rbegin(), e->free_blocks.rend(), 0);  // popped from the back: 0, 1, 2, ...
+    if (seed != 0) {
+        std::mt19937_64 rng(seed);
+        std::shuffle(e->free_blocks.begin(), e->free_blocks.end(), rng);
+    }
     std::vector<int> bt((size_t)batch * e->blocks_per_seq, 0);
     for (int b = 0; b < batch; ++b) {
         // every sequence owns blocks for the whole max_seq_len, so a step past the requested

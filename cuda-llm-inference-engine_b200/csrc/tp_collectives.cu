@@ -9,7 +9,7 @@
 // other rank (CUDA IPC), with epoch flags written by release stores and polled by acquire
 // loads at system scope:
 //
-//   tp_quantize_kernel : per CTA a few rows: local |x| max -> stored into every rank's slot
+//   tp_quantize_kernel : per CTA one row: local |x| max -> stored into every rank's slot
 //                        for this rank -> flag -> wait for every rank's flag -> global max ->
 //                        scale, int8 quantisation of the local columns (bytes identical to
 //                        the single-GPU quantiser's for those columns);
@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "tp_collectives.cuh"
+#include <algorithm>
 
 namespace b2 {
 
@@ -57,57 +58,77 @@ __device__ __forceinline__ unsigned int* tp_epoch(unsigned char* xchg, const TpL
 }
 
 constexpr int TPQ_THREADS = 256;
-constexpr int TPQ_MAX_ROWS = 64;
+constexpr int TPQ_CACHE = 8;  // float4 per thread kept in registers (rows up to 8192 columns)
 
+// One CTA per row: |x| max of this rank's columns of the row -> every rank's slot -> flag ->
+// wait for every rank -> global max -> scale and int8 quantisation of the local columns.
 __global__ void __launch_bounds__(TPQ_THREADS)
-tp_quantize_kernel(int B, int kl, int rows_per_cta, const float* __restrict__ x, int32_t* __restrict__ q_out,
-                   float* __restrict__ scale_out, const TpPeers P) {
-    __shared__ float am[TPQ_MAX_ROWS];
+tp_quantize_kernel(int kl, const float* __restrict__ x, int32_t* __restrict__ q_out, float* __restrict__ scale_out,
+                   const TpPeers P) {
+    __shared__ float red[TPQ_THREADS / 32];
     __shared__ unsigned int ep_s;
     griddep_wait();
     griddep_launch();
-    const int c = blockIdx.x;
-    const int r0 = c * rows_per_cta, nr = min(B - r0, rows_per_cta);
+    const int row = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     unsigned char* mine = P.xchg[P.rank];
-    for (int j = warp; j < nr; j += TPQ_THREADS / 32) {
-        const float* xr = x + (size_t)(r0 + j) * kl;
-        float m = 0.f;
-        for (int k = lane; k < kl; k += 32) m = fmaxf(m, fabsf(xr[k]));
-        m = warp_max(m);
-        if (lane == 0) am[j] = m;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * kl);
+    const int n4 = kl / 4;
+    float4 v[TPQ_CACHE];
+    float m = 0.f;
+#pragma unroll
+    for (int k = 0; k < TPQ_CACHE; ++k) {
+        const int i = threadIdx.x + k * TPQ_THREADS;
+        v[k] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
     }
-    if (threadIdx.x == 0) ep_s = *tp_epoch(mine, P.L, 0, c) + 1;
+    for (int i = threadIdx.x + TPQ_CACHE * TPQ_THREADS; i < n4; i += TPQ_THREADS) {
+        const float4 t = xr[i];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w))));
+    }
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    if (threadIdx.x == 0) ep_s = *tp_epoch(mine, P.L, 0, row) + 1;
     __syncthreads();
     const unsigned int ep = ep_s;
-    // this rank's row maxima into slot [rank] of every rank's exchange region
-    for (int i = threadIdx.x; i < P.world * nr; i += TPQ_THREADS) {
-        const int p = i / nr, j = i - p * nr;
-        reinterpret_cast<float*>(P.xchg[p] + P.L.amax)[(size_t)P.rank * P.L.bmax + r0 + j] = am[j];
+    if (threadIdx.x < P.world) {
+        float a = red[0];
+#pragma unroll
+        for (int w = 1; w < TPQ_THREADS / 32; ++w) a = fmaxf(a, red[w]);
+        // this rank's row maximum into slot [rank] of rank threadIdx.x, then its flag
+        reinterpret_cast<float*>(P.xchg[threadIdx.x] + P.L.amax)[(size_t)P.rank * P.L.bmax + row] = a;
+        __threadfence_system();
+        st_release_sys(tp_flag(P.xchg[threadIdx.x], P.L, 0, P.rank, row), ep);
+        wait_flag(tp_flag(mine, P.L, 0, threadIdx.x, row), ep, P.err);
     }
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < P.world) st_release_sys(tp_flag(P.xchg[threadIdx.x], P.L, 0, P.rank, c), ep);
-    if (threadIdx.x < P.world) wait_flag(tp_flag(mine, P.L, 0, threadIdx.x, c), ep, P.err);
-    __syncthreads();
-    if (threadIdx.x < nr) {
+    if (threadIdx.x == 0) {
         const volatile float* slots = reinterpret_cast<const volatile float*>(mine + P.L.amax);
         float g = 0.f;
-        for (int p = 0; p < P.world; ++p) g = fmaxf(g, slots[(size_t)p * P.L.bmax + r0 + threadIdx.x]);
-        am[threadIdx.x] = g;
+        for (int p = 0; p < P.world; ++p) g = fmaxf(g, slots[(size_t)p * P.L.bmax + row]);
+        red[0] = g;
+        *tp_epoch(mine, P.L, 0, row) = ep;
     }
     __syncthreads();
     // quantiser semantics of kernels/quantization/14_int8_gemm.cu:36-58 with the row's global absmax
-    for (int j = warp; j < nr; j += TPQ_THREADS / 32) {
-        const float a = am[j];
-        const float scale = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
-        const float inv = __fdiv_rn(1.0f, scale);
-        if (lane == 0) scale_out[r0 + j] = scale;
-        const float* xr = x + (size_t)(r0 + j) * kl;
-        int8_t* qr = reinterpret_cast<int8_t*>(q_out) + (size_t)(r0 + j) * kl;
-        for (int k = lane; k < kl; k += 32) qr[k] = (int8_t)(int)fminf(fmaxf(rintf(__fmul_rn(xr[k], inv)), -128.f), 127.f);
+    const float a = red[0];
+    const float scale = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (threadIdx.x == 0) scale_out[row] = scale;
+    auto q4 = [&](float4 t) {
+        const int b0 = (int)fminf(fmaxf(rintf(__fmul_rn(t.x, inv)), -128.f), 127.f);
+        const int b1 = (int)fminf(fmaxf(rintf(__fmul_rn(t.y, inv)), -128.f), 127.f);
+        const int b2 = (int)fminf(fmaxf(rintf(__fmul_rn(t.z, inv)), -128.f), 127.f);
+        const int b3 = (int)fminf(fmaxf(rintf(__fmul_rn(t.w, inv)), -128.f), 127.f);
+        return (int32_t)((b0 & 0xff) | ((b1 & 0xff) << 8) | ((b2 & 0xff) << 16) | ((uint32_t)(b3 & 0xff) << 24));
+    };
+    int32_t* qr = q_out + (size_t)row * n4;
+#pragma unroll
+    for (int k = 0; k < TPQ_CACHE; ++k) {
+        const int i = threadIdx.x + k * TPQ_THREADS;
+        if (i < n4) qr[i] = q4(v[k]);
     }
-    if (threadIdx.x == 0) *tp_epoch(mine, P.L, 0, c) = ep;
+    for (int i = threadIdx.x + TPQ_CACHE * TPQ_THREADS; i < n4; i += TPQ_THREADS) qr[i] = q4(xr[i]);
 }
 
 constexpr int TPR_THREADS = 256;
@@ -160,11 +181,8 @@ tp_reduce_kernel(int B, int d, int chunk, const float* __restrict__ sA, const fl
 
 int launch_tp_quantize(int B, int kl, const float* x, int32_t* q, float* scale, const TpPeers& P, cudaStream_t st) {
     if (B <= 0) return B2_OK;
-    const int rpc = std::max(1, (B + TP_MAX_CTAS - 1) / TP_MAX_CTAS);
-    if (rpc > TPQ_MAX_ROWS || B > P.L.bmax) return B2_ERR_UNSUPPORTED;
-    const int ctas = (B + rpc - 1) / rpc;
-    return launch_kernel(tp_quantize_kernel, dim3(ctas), dim3(TPQ_THREADS), 0, st, B, kl, rpc, x, q, scale, P) ==
-                   cudaSuccess
+    if (B > P.L.bmax || B > TP_MAX_CTAS || (kl & 3)) return B2_ERR_UNSUPPORTED;
+    return launch_kernel(tp_quantize_kernel, dim3(B), dim3(TPQ_THREADS), 0, st, kl, x, q, scale, P) == cudaSuccess
                ? B2_OK
                : B2_ERR_CUDA;
 }

@@ -7,7 +7,7 @@
 namespace b2 {
 
 constexpr int TP_MAX_RANKS = 8;
-constexpr int TP_MAX_CTAS = 64;
+constexpr int TP_MAX_CTAS = 256;
 
 // Byte offsets inside a rank's exchange region.
 struct TpLayout {

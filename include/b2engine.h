@@ -69,8 +69,9 @@ int b2_engine_config(const b2_engine* e, b2_gpt2_config* out);
 
 /* Starts `batch` sequences: prompts_host [batch, prompt_stride] token ids, prompt_lens_host
  * [batch] (>= 1). Frees the previous sequences' KV blocks, gives every sequence
- * ceil(max_seq_len / 16) blocks from the pool's free list (in a seeded random order, so block
- * tables are non-contiguous), and sets every position to 0. Positions stop at
+ * ceil(max_seq_len / 16) blocks from the pool's free list (seed 0: in pool order, like the
+ * reference engine; any other seed: a seeded random order, so block tables are scattered over
+ * the pool), and sets every position to 0. Positions stop at
  * max_seq_len - 1 (further steps rewrite that slot). Steps then
  * feed the prompt token by token through the decode path (the reference's continuation
  * mode, src/gpt2_engine.cu:683-696) and continue greedily. Synchronous. */
