@@ -633,14 +633,17 @@ def run_only(args):
         by = attn_alg_bytes(np.full(Bw, ctxw), Hw, Hw, D, 2, nb)
     elif args.only.startswith("attn"):
         dt = torch.bfloat16 if args.only == "attn_bf16" else torch.float32
+        # B2_ATTN_SHARD=n: the KV-head shard one rank of n holds (the per-rank launch of --gpus n)
+        nshard = int(os.environ.get("B2_ATTN_SHARD", "1"))
+        hkv, hq = H_KV // nshard, H_Q // nshard
         lens, bt, P = workload_meta()
-        kc, vc = make_kv_shard(torch, P, 0, H_KV, dt, dev)
-        q = torch.randn(B, H_Q, D, device=dev)
+        kc, vc = make_kv_shard(torch, P, 0, hkv, dt, dev)
+        q = torch.randn(B, hq, D, device=dev)
         O = torch.empty_like(q)
         btd, lensd = torch.from_numpy(bt).to(dev), torch.from_numpy(lens).to(dev)
-        ws = b2.make_decode_workspace(B, H_Q, H_KV, D, int(lens.max()), BS, device=dev)
+        ws = b2.make_decode_workspace(B, hq, hkv, D, int(lens.max()), BS, device=dev)
         fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, int(lens.max()), O=O, workspace=ws)  # noqa: E731
-        by = attn_alg_bytes(lens, H_KV, H_Q, D, 2 if dt == torch.bfloat16 else 4, bt.shape[1])
+        by = attn_alg_bytes(lens, hkv, hq, D, 2 if dt == torch.bfloat16 else 4, bt.shape[1])
     else:
         M, N, K = {"gemm2048": (2048,) * 3, "gemm8192": (8192,) * 3, "gemm_rect": (64, 3072, 768)}[args.only]
         A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev).view(torch.int32)

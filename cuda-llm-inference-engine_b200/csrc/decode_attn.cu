@@ -143,172 +143,106 @@ __device__ __forceinline__ void load_row(const unsigned char* p, float (&f)[N]) 
     }
 }
 
-template <int G, int D, typename KV>
-__global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
-decode_attn_kernel(const DecodeAttnParams p) {
-    using C = DACfg<G, D, KV>;
-    extern __shared__ __align__(1024) unsigned char smem[];
+// ------------------------------------------------------------------ pieces shared by both kernels
 
-    const int split = blockIdx.x;
-    const int kvh = blockIdx.y;
-    const int b = blockIdx.z;
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int lane = tid & 31;
-
-    griddep_wait();
-    griddep_launch();
-    // ---- this CTA's token range (whole blocks, as the reference splits, 13_decode_attn.cu:63-65)
+// Context length of sequence b, clamped to its block-table row (an overlong length is
+// reported once per launch by the caller's choice of `report`).
+__device__ __forceinline__ int da_context(const DecodeAttnParams& p, int b, bool report) {
     int ctx = p.context_lens[b];
     const int cap = p.num_blocks_per_seq * p.block_size;
     if (ctx > cap) {
-        if (tid == 0 && split == 0 && kvh == 0) raise_error(p.err, B2_DEVERR_CTX_RANGE);
+        if (report) raise_error(p.err, B2_DEVERR_CTX_RANGE);
         ctx = cap;
     }
-    if (ctx < 0) ctx = 0;
-    const int nblk = (ctx + p.block_size - 1) / p.block_size;
-    const int nsplit = (nblk + p.blocks_per_split - 1) / p.blocks_per_split;  // non-empty splits
-    const int hq0 = kvh * G;
-    float* O = p.O + ((size_t)b * p.H_q + hq0) * D;
+    return ctx < 0 ? 0 : ctx;
+}
 
-    if (nblk == 0) {  // empty context: O = 0 (reference reduce writes o * 0, 13_decode_attn.cu:48-52)
-        if (split == 0)
-            for (int i = tid; i < G * D; i += DA_NT) O[i] = 0.f;
-        return;
-    }
-    if (split >= nsplit) return;  // empty split: contributes nothing
-
-    const int tok_begin = split * p.blocks_per_split * p.block_size;
-    const int tok_end = min(ctx, (split + 1) * p.blocks_per_split * p.block_size);
-    const int ntiles = (tok_end - tok_begin + C::T - 1) / C::T;
-
-    volatile unsigned int* misc = reinterpret_cast<volatile unsigned int*>(smem + C::OFF_MISC);
-    const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
-    auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
-    const uint32_t ring = smem_u32(smem);
-
-    if (tid == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(full_bar(s), 32);  // one cp.async arrival per producer lane
-            mbar_init(empty_bar(s), DA_NW);
+// Producer warp: gathers tile `i` of the token range [tok_begin, tok_end) of (b, kvh) into
+// the stage at sK (K rows) / sV (V rows). Lane r resolves the cache offset of row r of each
+// 32-row chunk; the warp then moves rows with coalesced 16-byte cp.async, CPR lanes per row.
+// bt_s holds the range's block-table slice when `staged` (else the row is read from global).
+template <typename C>
+__device__ __forceinline__ void da_issue_tile(const DecodeAttnParams& p, int b, int kvh, int tok_begin, int tok_end,
+                                              int i, uint32_t sK, uint32_t sV, const int* bt_s, bool staged,
+                                              int lane, uint64_t pol) {
+    constexpr int CPR = C::ROW / 16;  // 16-byte chunks per row
+    constexpr int RPI = 32 / CPR;     // rows per warp instruction
+    constexpr int RC = C::T / 32;     // 32-row chunks per tile
+    const int* bt = p.block_table + (size_t)b * p.num_blocks_per_seq;
+    const int blk0 = tok_begin / p.block_size;
+    auto row_off = [&](int c) -> long long {
+        const int t0 = tok_begin + i * C::T + c * 32;
+        if (lane >= tok_end - t0) return 0;
+        const int pos = t0 + lane;
+        const int blk = pos / p.block_size;
+        const int slot = pos - blk * p.block_size;
+        int phys = staged ? bt_s[blk - blk0] : bt[blk];
+        if (p.num_phys_blocks > 0 && (unsigned)phys >= (unsigned)p.num_phys_blocks) {
+            raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
+            phys = 0;
         }
-        misc[0] = 0;  // abort flag
-        misc[1] = 0;  // merge ticket
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    if (warp == DA_NW) {
-        // ------------------------------------------------------------ producer warp
-        // The split's slice of the block table is staged in shared memory once, so no tile
-        // waits on a dependent global load (long splits fall back to global reads). Lane r
-        // resolves the cache offset of row r of each 32-row chunk; the warp then moves rows
-        // with coalesced 16-byte cp.async, CPR lanes per row, and every lane arrives on the
-        // stage's full barrier once its copies have landed.
-        constexpr int CPR = C::ROW / 16;  // 16-byte chunks per row
-        constexpr int RPI = 32 / CPR;     // rows per warp instruction
-        constexpr int RC = C::T / 32;     // 32-row chunks per tile
-        const int* bt = p.block_table + (size_t)b * p.num_blocks_per_seq;
-        const int blk0 = tok_begin / p.block_size;
-        const int nbt = (tok_end - 1) / p.block_size - blk0 + 1;
-        int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT);
-        const bool staged = nbt <= C::BT_CAP;
-        if (staged) {
-            for (int j = lane; j < nbt; j += 32) bt_s[j] = bt[blk0 + j];
-            __syncwarp();
-        }
-        const uint64_t pol = policy_evict_first();
-        auto row_off = [&](int i, int c) -> long long {
-            const int t0 = tok_begin + i * C::T + c * 32;
-            if (lane >= tok_end - t0) return 0;
-            const int pos = t0 + lane;
-            const int blk = pos / p.block_size;
-            const int slot = pos - blk * p.block_size;
-            int phys = staged ? bt_s[blk - blk0] : bt[blk];
-            if (p.num_phys_blocks > 0 && (unsigned)phys >= (unsigned)p.num_phys_blocks) {
-                raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
-                phys = 0;
-            }
-            return ((((long long)phys * p.block_size + slot) * p.H_kv + kvh) * (long long)C::ROW);
-        };
-        const int sub = lane / CPR;
-        const int chunk = (lane % CPR) * 16;
-        for (int i = 0; i < ntiles; ++i) {
-            const int st = i % C::STAGES;
-            if (i >= C::STAGES) {
-                const uint32_t par = ((i / C::STAGES) - 1) & 1;
-                bool ok = misc[0] == 0 && mbar_wait(empty_bar(st), par, p.err);
-                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-                if (!ok) { if (lane == 0) misc[0] = 1; break; }
-            }
-            const int n = min(C::T, tok_end - (tok_begin + i * C::T));
-            const uint32_t sK = ring + st * C::STAGE;
-            const uint32_t sV = sK + C::T * C::ROW;
+        return ((((long long)phys * p.block_size + slot) * p.H_kv + kvh) * (long long)C::ROW);
+    };
+    const int sub = lane / CPR;
+    const int chunk = (lane % CPR) * 16;
+    const int n = min(C::T, tok_end - (tok_begin + i * C::T));
 #pragma unroll
-            for (int c = 0; c < RC; ++c) {
-                if (c * 32 >= n) break;
-                const long long cur = row_off(i, c);
+    for (int c = 0; c < RC; ++c) {
+        if (c * 32 >= n) break;
+        const long long cur = row_off(c);
 #pragma unroll 4
-                for (int r0 = c * 32; r0 < min(n, c * 32 + 32); r0 += RPI) {
-                    const int r = r0 + sub;
-                    const long long off = __shfl_sync(0xffffffffu, cur, r & 31);
-                    if (r < n) {
-                        cp_async16(sK + r * C::ROW + chunk, p.k_cache + off + chunk, pol);
-                        cp_async16(sV + r * C::ROW + chunk, p.v_cache + off + chunk, pol);
-                    }
-                }
+        for (int r0 = c * 32; r0 < min(n, c * 32 + 32); r0 += RPI) {
+            const int r = r0 + sub;
+            const long long off = __shfl_sync(0xffffffffu, cur, r & 31);
+            if (r < n) {
+                cp_async16(sK + r * C::ROW + chunk, p.k_cache + off + chunk, pol);
+                cp_async16(sV + r * C::ROW + chunk, p.v_cache + off + chunk, pol);
             }
-            cp_async_mbar_arrive_noinc(full_bar(st));
         }
-        cp_async_wait_all();  // nothing may still be landing in the ring when the warp exits
-        return;
     }
+}
 
-    // ---------------------------------------------------------------- consumer warps
-    // Warp w owns tokens [TW w, TW (w+1)) of every tile and keeps its own online softmax
-    // state; lanes span head_dim (VPL columns each), so K/V rows are read as contiguous,
-    // conflict-free shared loads. The TPW x G dot products of a token group are reduced
-    // across the warp with a transposed butterfly (about one shuffle per dot product), p
-    // and alpha are exchanged through warp-private shared memory, and no CTA-wide barrier
-    // is taken inside the tile loop.
-    constexpr int NC = DA_NW * 32;
-    constexpr int TPW = C::TPW;            // tokens per group
-    constexpr int NV = TPW * G;            // dot products per group (<= 16)
-    constexpr int SHIFT = 5 - ilog2(NV);   // lane -> (token, head) index: idx = lane >> SHIFT
-    constexpr int LG = ilog2(G);
-    const int idx = lane >> SHIFT;
-    const int my_t = idx / G, my_g = idx % G;
-    const bool owner = (lane & ((1 << SHIFT) - 1)) == 0;
-    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
-
-    // q and the output accumulator are held as fp32 pairs for the packed f32x2 FMA
-    constexpr int VP = C::VPL / 2;
+// One consumer warp's online-softmax state for one (sequence, KV head) work unit. Warp w
+// owns tokens [TW w, TW (w+1)) of every tile; lanes span head_dim (VPL columns each), so
+// K/V rows are read as contiguous, conflict-free shared loads. The TPW x G dot products of
+// a token group are reduced across the warp with a transposed butterfly (about one shuffle
+// per dot product), p and alpha are exchanged through warp-private shared memory, and no
+// CTA-wide barrier is taken inside the tile loop.
+template <int G, int D, typename KV>
+struct DAWarp {
+    using C = DACfg<G, D, KV>;
+    static constexpr int VP = C::VPL / 2;  // q and the accumulator as fp32 pairs (packed f32x2 FMA)
+    static constexpr int TPW = C::TPW;     // tokens per group
+    static constexpr int NV = TPW * G;     // dot products per group (<= 16)
+    static constexpr int SHIFT = 5 - ilog2(NV);
+    static constexpr int LG = ilog2(G);
     float2 q[G][VP];
-    {
+    float2 acc[G][VP];
+    float m_run, l_run;  // head my_g; l over this lane's token subset
+    int idx, my_t, my_g;
+    bool owner;
+
+    __device__ __forceinline__ void begin(const DecodeAttnParams& p, int b, int hq0, int lane) {
+        idx = lane >> SHIFT;
+        my_t = idx / G;
+        my_g = idx % G;
+        owner = (lane & ((1 << SHIFT) - 1)) == 0;
         const float* Qb = p.Q + ((size_t)b * p.H_q + hq0) * D;
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int j = 0; j < VP; ++j)
+            for (int j = 0; j < VP; ++j) {
                 q[g][j] = make_float2(Qb[g * D + lane * C::VPL + 2 * j] * p.scale_log2,
                                       Qb[g * D + lane * C::VPL + 2 * j + 1] * p.scale_log2);
+                acc[g][j] = make_float2(0.f, 0.f);
+            }
+        m_run = -INFINITY;
+        l_run = 0.f;
     }
-    float2 acc[G][VP];
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int j = 0; j < VP; ++j) acc[g][j] = make_float2(0.f, 0.f);
-    float m_run = -INFINITY, l_run = 0.f;  // head my_g; l over this lane's token subset
 
-    for (int i = 0; i < ntiles; ++i) {
-        const int st = i % C::STAGES;
-        const int n = min(C::T, tok_end - (tok_begin + i * C::T));
-        if (misc[0] == 0) {
-            if (!mbar_wait(full_bar(st), (i / C::STAGES) & 1, p.err)) misc[0] = 1;
-        }
-        const unsigned char* Kt = smem + st * C::STAGE;
-        const unsigned char* Vt = Kt + C::T * C::ROW;
+    // This warp's token slice of a tile of n tokens (K rows at Kt, V rows at Vt).
+    __device__ __forceinline__ void tile(const unsigned char* Kt, const unsigned char* Vt, int n, int warp, int lane,
+                                         float* xw) {
 #pragma unroll
         for (int grp = 0; grp < C::TW / TPW; ++grp) {
             const int tok0 = warp * C::TW + grp * TPW;
@@ -372,65 +306,40 @@ decode_attn_kernel(const DecodeAttnParams p) {
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(st));
     }
 
-    // ---- per-warp totals: l summed over the lanes holding this head's tokens
-    float l_tot = owner ? l_run : 0.f;
+    // l summed over the lanes holding this head's tokens (valid in owner lanes).
+    __device__ __forceinline__ float l_total() const {
+        float l = owner ? l_run : 0.f;
 #pragma unroll
-    for (int k = 0; k < ilog2(TPW); ++k) l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 1 << (SHIFT + LG + k));
-    named_barrier(1, NC);  // every warp is done reading the ring
-    float* red = reinterpret_cast<float*>(smem);  // [NW][G][D], reuses the ring
-    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);  // [NW][G][2]
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int j = 0; j < VP; ++j) {
-            red[(warp * G + g) * D + lane * C::VPL + 2 * j] = acc[g][j].x;
-            red[(warp * G + g) * D + lane * C::VPL + 2 * j + 1] = acc[g][j].y;
-        }
-    if (owner && my_t == 0) {
-        ml_s[(warp * G + my_g) * 2] = m_run;
-        ml_s[(warp * G + my_g) * 2 + 1] = l_tot;
+        for (int k = 0; k < ilog2(TPW); ++k) l += __shfl_xor_sync(0xffffffffu, l, 1 << (SHIFT + LG + k));
+        return l;
     }
-    named_barrier(1, NC);
-    if (misc[0] != 0) return;  // a wait gave up: the error bit is set, O is left untouched
+};
 
-    // Log-sum-exp merge of the 8 warps for element i = g*D + d -> (o, M, L).
-    auto merge_warps = [&](int i, float& o, float& M, float& L) {
-        const int g = i / D;
-        M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < DA_NW; ++w) M = fmaxf(M, ml_s[(w * G + g) * 2]);
-        o = 0.f;
-        L = 0.f;
-        if (M == -INFINITY) return;
-#pragma unroll
-        for (int w = 0; w < DA_NW; ++w) {
-            const float mw = ml_s[(w * G + g) * 2];
-            if (mw == -INFINITY) continue;
-            const float sc = fast_exp2(mw - M);
-            o = fmaf(red[w * G * D + i], sc, o);
-            L = fmaf(ml_s[(w * G + g) * 2 + 1], sc, L);
-        }
-    };
-
+// Final stage of a (sequence, KV head) split, by the NC consumer threads: `get(i, o, M, L)`
+// gives the split's merged unnormalised output o, max M and sum L for element i = g*D + d.
+// One split: O = o / L. Otherwise the split's partial goes to the workspace and the last of
+// the nsplit CTAs (or work items) to arrive (atomic ticket) merges all partials into O and
+// leaves the counter at zero.
+template <int G, int D, int NC, typename Get>
+__device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int kvh, int split, int nsplit, int tid,
+                                          volatile unsigned int* ticket, Get get) {
+    const int hq0 = kvh * G;
+    float* O = p.O + ((size_t)b * p.H_q + hq0) * D;
     if (nsplit == 1) {
         for (int i = tid; i < G * D; i += NC) {
             float o, M, L;
-            merge_warps(i, o, M, L);
+            get(i, o, M, L);
             O[i] = L > 0.f ? o / L : 0.f;
         }
         return;
     }
-
-    // ---- write this split's partial, then the last CTA of the (b, kv_head) merges
     const size_t rowlen = D + 2;
     for (int i = tid; i < G * D; i += NC) {
         const int g = i / D, d = i - g * D;
         float o, M, L;
-        merge_warps(i, o, M, L);
+        get(i, o, M, L);
         float* ws = p.ws_partial + (((size_t)b * p.H_q + hq0 + g) * p.num_splits + split) * rowlen;
         ws[d] = o;
         if (d == 0) { ws[D] = M; ws[D + 1] = L; }
@@ -438,9 +347,9 @@ decode_attn_kernel(const DecodeAttnParams p) {
     __threadfence();
     named_barrier(1, NC);
     unsigned int* counter = p.ws_counter + (size_t)b * p.H_kv + kvh;
-    if (tid == 0) misc[1] = atomicAdd(counter, 1u);
+    if (tid == 0) *ticket = atomicAdd(counter, 1u);
     named_barrier(1, NC);
-    if (misc[1] != (unsigned)(nsplit - 1)) return;
+    if (*ticket != (unsigned)(nsplit - 1)) return;
     __threadfence();
     for (int i = tid; i < G * D; i += NC) {
         const int g = i / D, d = i - g * D;
@@ -456,6 +365,146 @@ decode_attn_kernel(const DecodeAttnParams p) {
         O[i] = L > 0.f ? o / L : 0.f;
     }
     if (tid == 0) *counter = 0u;  // every sibling has arrived: leave the counter reusable
+}
+
+// ------------------------------------------------------------------ the kernel
+// Grid (KV head, split, sequence): the CTA's warps merge through the ring's memory once the
+// producer is done.
+template <int G, int D, typename KV>
+__global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
+decode_attn_kernel(const DecodeAttnParams p) {
+    using C = DACfg<G, D, KV>;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    // KV head fastest in the grid: the CTAs of one token range run side by side
+    const int kvh = blockIdx.x;
+    const int split = blockIdx.y;
+    const int b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    griddep_wait();
+    griddep_launch();
+    // ---- this CTA's token range (whole blocks, as the reference splits, 13_decode_attn.cu:63-65)
+    const int ctx = da_context(p, b, tid == 0 && split == 0 && kvh == 0);
+    const int nblk = (ctx + p.block_size - 1) / p.block_size;
+    const int nsplit = (nblk + p.blocks_per_split - 1) / p.blocks_per_split;  // non-empty splits
+    const int hq0 = kvh * G;
+
+    if (nblk == 0) {  // empty context: O = 0 (reference reduce writes o * 0, 13_decode_attn.cu:48-52)
+        float* O = p.O + ((size_t)b * p.H_q + hq0) * D;
+        if (split == 0)
+            for (int i = tid; i < G * D; i += DA_NT) O[i] = 0.f;
+        return;
+    }
+    if (split >= nsplit) return;  // empty split: contributes nothing
+
+    const int tok_begin = split * p.blocks_per_split * p.block_size;
+    const int tok_end = min(ctx, (split + 1) * p.blocks_per_split * p.block_size);
+    const int ntiles = (tok_end - tok_begin + C::T - 1) / C::T;
+
+    volatile unsigned int* misc = reinterpret_cast<volatile unsigned int*>(smem + C::OFF_MISC);
+    const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+    const uint32_t ring = smem_u32(smem);
+
+    if (tid == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full_bar(s), 32);  // one cp.async arrival per producer lane
+            mbar_init(empty_bar(s), DA_NW);
+        }
+        misc[0] = 0;  // abort flag
+        misc[1] = 0;  // merge ticket
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == DA_NW) {
+        // ------------------------------------------------------------ producer warp
+        // The split's slice of the block table is staged in shared memory once, so no tile
+        // waits on a dependent global load (long splits fall back to global reads); every lane
+        // arrives on the stage's full barrier once its copies have landed.
+        const int* bt = p.block_table + (size_t)b * p.num_blocks_per_seq;
+        const int blk0 = tok_begin / p.block_size;
+        const int nbt = (tok_end - 1) / p.block_size - blk0 + 1;
+        int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT);
+        const bool staged = nbt <= C::BT_CAP;
+        if (staged) {
+            for (int j = lane; j < nbt; j += 32) bt_s[j] = bt[blk0 + j];
+            __syncwarp();
+        }
+        const uint64_t pol = policy_evict_first();
+        for (int i = 0; i < ntiles; ++i) {
+            const int st = i % C::STAGES;
+            if (i >= C::STAGES) {
+                const uint32_t par = ((i / C::STAGES) - 1) & 1;
+                bool ok = misc[0] == 0 && mbar_wait(empty_bar(st), par, p.err);
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) { if (lane == 0) misc[0] = 1; break; }
+            }
+            const uint32_t sK = ring + st * C::STAGE;
+            da_issue_tile<C>(p, b, kvh, tok_begin, tok_end, i, sK, sK + C::T * C::ROW, bt_s, staged, lane, pol);
+            cp_async_mbar_arrive_noinc(full_bar(st));
+        }
+        cp_async_wait_all();  // nothing may still be landing in the ring when the warp exits
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumer warps
+    constexpr int NC = DA_NW * 32;
+    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
+    DAWarp<G, D, KV> w;
+    w.begin(p, b, hq0, lane);
+    for (int i = 0; i < ntiles; ++i) {
+        const int st = i % C::STAGES;
+        const int n = min(C::T, tok_end - (tok_begin + i * C::T));
+        if (misc[0] == 0) {
+            if (!mbar_wait(full_bar(st), (i / C::STAGES) & 1, p.err)) misc[0] = 1;
+        }
+        const unsigned char* Kt = smem + st * C::STAGE;
+        w.tile(Kt, Kt + C::T * C::ROW, n, warp, lane, xw);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(st));
+    }
+
+    // ---- merge the 8 warps through the ring's memory (the producer is done with it)
+    const float l_tot = w.l_total();
+    named_barrier(1, NC);  // every warp is done reading the ring
+    float* red = reinterpret_cast<float*>(smem);               // [NW][G][D]
+    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);  // [NW][G][2]
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DAWarp<G, D, KV>::VP; ++j) {
+            red[(warp * G + g) * D + lane * C::VPL + 2 * j] = w.acc[g][j].x;
+            red[(warp * G + g) * D + lane * C::VPL + 2 * j + 1] = w.acc[g][j].y;
+        }
+    if (w.owner && w.my_t == 0) {
+        ml_s[(warp * G + w.my_g) * 2] = w.m_run;
+        ml_s[(warp * G + w.my_g) * 2 + 1] = l_tot;
+    }
+    named_barrier(1, NC);
+    if (misc[0] != 0) return;  // a wait gave up: the error bit is set, O is left untouched
+    // log-sum-exp merge of the 8 warps for element i = g*D + d -> (o, M, L)
+    auto merge_warps = [&](int i, float& o, float& M, float& L) {
+        const int g = i / D;
+        M = -INFINITY;
+#pragma unroll
+        for (int v = 0; v < DA_NW; ++v) M = fmaxf(M, ml_s[(v * G + g) * 2]);
+        o = 0.f;
+        L = 0.f;
+        if (M == -INFINITY) return;
+#pragma unroll
+        for (int v = 0; v < DA_NW; ++v) {
+            const float mw = ml_s[(v * G + g) * 2];
+            if (mw == -INFINITY) continue;
+            const float sc = fast_exp2(mw - M);
+            o = fmaf(red[v * G * D + i], sc, o);
+            L = fmaf(ml_s[(v * G + g) * 2 + 1], sc, L);
+        }
+    };
+    da_finish<G, D, NC>(p, b, kvh, split, nsplit, tid, misc + 1, merge_warps);
 }
 
 // ------------------------------------------------------------------ host side
@@ -493,12 +542,13 @@ static SplitPlan plan_splits(int B, int H_kv, int head_dim, int kv_bytes, int ma
 
 bool set_smem_attr_once(const void* func, int bytes, int slot);
 
+int num_sms_current_device();
+
 template <int G, int D, typename KV>
 static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int B, cudaStream_t st) {
     using C = DACfg<G, D, KV>;
-    constexpr int slot = 32 + (G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3) + (D == 64 ? 0 : 4) + (sizeof(KV) == 4 ? 0 : 8);
-    if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV>, C::SMEM, slot)) return cudaErrorInvalidValue;
-    dim3 grid(prm.num_splits, prm.H_kv, B);
+    if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV>, C::SMEM, 0)) return cudaErrorInvalidValue;
+    dim3 grid(prm.H_kv, prm.num_splits, B);
     return launch_kernel(decode_attn_kernel<G, D, KV>, grid, dim3(DA_NT), (size_t)C::SMEM, st, prm);
 }
 
@@ -512,8 +562,6 @@ static cudaError_t dispatch_group(int G, const DecodeAttnParams& prm, int B, cud
         default: return cudaErrorInvalidValue;
     }
 }
-
-int num_sms_current_device();
 
 // Workspace layout: [B, H_q, num_splits, D+2] f32 partials, then [B, H_kv] u32 counters
 // (256-byte aligned).
