@@ -156,6 +156,8 @@ struct b2_engine {
     cudaGraphExec_t graph = nullptr;
     bool graph_dirty = true;
     bool failed = false;  // a device allocation failed
+    // fused QKV split in the GEMM epilogue (B2_ENGINE_FUSE_QKV=0 runs GEMM + scatter kernel)
+    bool fuse_qkv = !(getenv("B2_ENGINE_FUSE_QKV") && strcmp(getenv("B2_ENGINE_FUSE_QKV"), "0") == 0);
 
     ~b2_engine();
     template <typename T>
@@ -421,12 +423,30 @@ int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
         // attention sub-block (pre-norm; x stays the residual and is updated in place)
         M("ln_quant");
         B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
+        // QKV linear with the split into q and the paged K/V write in its epilogue; shapes the
+        // fused path does not take run as GEMM + scatter kernel
         M("gemm_qkv");
-        B2_TRY(gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS, false,
-                           st));
-        M("qkv_scatter");
-        B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc, vc,
-                                  e->kv_dtype, st));
+        QkvScatterArgs qa;
+        qa.q = e->q;
+        qa.k = kc;
+        qa.v = vc;
+        qa.pos = e->pos;
+        qa.block_table = e->block_table;
+        qa.d = dl;
+        qa.block_size = kBlock;
+        qa.nbps = e->blocks_per_seq;
+        qa.bf16 = e->kv_dtype == B2_KV_BF16;
+        r = e->fuse_qkv ? gemm_launch_qkv(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, qa, st)
+                        : B2_ERR_UNSUPPORTED;
+        if (r == B2_ERR_UNSUPPORTED) {
+            B2_TRY(gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
+                               false, st));
+            M("qkv_scatter");
+            B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
+                                      vc, e->kv_dtype, st));
+        } else if (r != B2_OK) {
+            return r;
+        }
         b2_decode_attn_args a{};
         a.B = B; a.H_q = Hl; a.H_kv = Hl; a.head_dim = dh;
         a.Q = e->q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;

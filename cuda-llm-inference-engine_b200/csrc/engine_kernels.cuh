@@ -4,6 +4,19 @@
 #include <cstdint>
 
 namespace b2 {
+// Fused QKV split of the decode step (int8_gemm.cu gemm_launch_qkv): q [B, d]; K/V caches
+// [P, block_size, H, d_head] (fp32, or bf16 when bf16 != 0) written at each sequence's pos.
+struct QkvScatterArgs {
+    float* q = nullptr;
+    void* k = nullptr;
+    void* v = nullptr;
+    const int* pos = nullptr;
+    const int* block_table = nullptr;
+    int d = 0, block_size = 0, nbps = 0, bf16 = 0;
+};
+int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
+                    const float* bias, const QkvScatterArgs& sc, cudaStream_t st);
+
 int launch_embed(int B, int d, const int* tokens, const int* pos, const float* wte, const float* wpe, float* x,
                  int* ctx_lens, unsigned long long* keys, cudaStream_t st);
 int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,

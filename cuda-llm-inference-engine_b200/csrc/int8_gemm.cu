@@ -22,6 +22,8 @@
 //   share A and B tiles in L2.
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "engine_kernels.cuh"
+#include <cuda_bf16.h>
 #include <algorithm>
 #include <cmath>
 #include <mutex>
@@ -94,6 +96,19 @@ constexpr int GM_BM = 128;
 constexpr int GM_BK = 128;  // bytes of K per stage (one 128-byte swizzle atom row)
 constexpr int GM_THREADS = 192;
 
+// Destination of a fused QKV epilogue (decode engine): output column n of row b belongs to
+// q (n < d), K (d <= n < 2d) or V; q goes to q[b, n], K/V to the paged cache row of token
+// pos[b] of sequence b: cache[((phys * bs + pos % bs) * d + n % d)] with
+// phys = block_table[b * nbps + pos / bs] (layout [P, bs, H, d_head], d = H * d_head).
+struct QkvScatter {
+    float* q = nullptr;
+    void* k = nullptr;
+    void* v = nullptr;
+    const int* pos = nullptr;
+    const int* block_table = nullptr;
+    int d = 0, bs = 0, nbps = 0, bf16 = 0;
+};
+
 struct GemmParams {
     int M, N, K;
     const float* scale_A;
@@ -111,6 +126,7 @@ struct GemmParams {
     // when the output has a single 128-row tile (rows past it hold stale data whose
     // accumulator rows the epilogue never stores)
     int a_rows;
+    QkvScatter sc;  // sc.q != nullptr: the engine's fused QKV split + paged KV write
 };
 
 template <int BN>
@@ -146,7 +162,8 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 // relative to n); rs holds the residual values when EPI needs them.
 template <int EPI, bool S32>
 __device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n, float sa, const float* sBs,
-                                        const float* bis, const float (&rs)[16], const GemmParams& p) {
+                                        const float* bis, const float (&rs)[16], const GemmParams& p,
+                                        long long sc_row = -1) {
     if constexpr (S32) {
         int32_t* Crow = static_cast<int32_t*>(p.C) + (size_t)row * p.N;
         if (n + 16 <= p.N && (p.N & 3) == 0) {
@@ -164,6 +181,33 @@ __device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n,
 #pragma unroll
         for (int j = 0; j < 16; ++j)
             v[j] = epilogue<EPI>((int32_t)r[j], sa, sBs[j], EPI != B2_EPI_PLAIN ? bis[j] : 0.f, rs[j]);
+        if (p.sc.q) {  // fused QKV split: 16 columns never straddle q/K/V (d % 16 == 0)
+            const int part = n / p.sc.d, i = n - part * p.sc.d;
+            if (part == 0) {
+                float* dst = p.sc.q + (size_t)row * p.sc.d + i;
+#pragma unroll
+                for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+                const size_t off = (size_t)sc_row + i;
+                void* cache = part == 1 ? p.sc.k : p.sc.v;
+                if (p.sc.bf16) {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        w[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * j])) |
+                               ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * j + 1])) << 16);
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(cache) + off);
+                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+                    float* dst = static_cast<float*>(cache) + off;
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4)
+                        *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                }
+            }
+            return;
+        }
         if (n + 16 <= p.N && (p.N & 3) == 0) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
@@ -350,6 +394,16 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     if (EPI != B2_EPI_PLAIN) bias_s[c] = n < p.N ? __ldg(p.bias + n) : 0.f;
                 }
             }
+            // fused QKV split: this row's paged-cache row offset, looked up while the MMAs run
+            long long sc_row = 0;
+            if (p.sc.q) {
+                const int r = mt * GM_BM + quad * 32 + lane;
+                if (r < p.M) {
+                    const int pos = p.sc.pos[r];
+                    const int phys = p.sc.block_table[(size_t)r * p.sc.nbps + pos / p.sc.bs];
+                    sc_row = ((long long)phys * p.sc.bs + pos % p.sc.bs) * p.sc.d;
+                }
+            }
             named_barrier(2, 128);
             // after a timed-out wait the warps keep taking the named barriers but do no work
             const bool ok = !*abort_flag && mbar_wait(accf_bar(a), u & 1, p.err);
@@ -369,9 +423,9 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     if (row_ok && n < p.N) load_res16(p, row, n, rs0);
                     if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
                 }
-                if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
+                if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p, sc_row);
                 if (row_ok && n + 16 < p.N)
-                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
+                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p, sc_row);
             };
             if (p.k_splits == 1) {
 #pragma unroll 1
@@ -934,6 +988,38 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
         case B2_EPI_BIAS_GELU: return gemm_dispatch<B2_EPI_BIAS_GELU, false>(p, A, BT, ws, ws_bytes, st);
         default: return gemm_dispatch<B2_EPI_BIAS_RESIDUAL, false>(p, A, BT, ws, ws_bytes, st);
     }
+}
+
+// The engine's QKV linear with the split into q and the paged K/V write fused into the
+// epilogue (bias epilogue, then the 16-column stores go to q or the cache row of pos[b]).
+// Only the one-CTA tcgen05 kernel implements it; shapes that would take another kernel (or
+// N != 3 d, d % 16 != 0) return B2_ERR_UNSUPPORTED and the caller runs the two steps apart.
+int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
+                    const float* bias, const QkvScatterArgs& sc, cudaStream_t st) {
+    if (M <= 0 || N <= 0 || (K & 15) || K == 0 || ((uintptr_t)A & 15) || ((uintptr_t)BT & 15)) return B2_ERR_UNSUPPORTED;
+    if (!A || !BT || !sA || !sB || !bias || !sc.q || !sc.k || !sc.v || !sc.pos || !sc.block_table)
+        return B2_ERR_INVALID;
+    if (sc.d <= 0 || sc.d % 16 || N != 3 * sc.d || M > GM_BM) return B2_ERR_UNSUPPORTED;
+    GemmParams p{M, N, K, sA, sB, bias, nullptr, sc.q, device_error_ptr(), 1, 0, nullptr, nullptr, (M + 7) & ~7};
+    p.sc.q = sc.q;
+    p.sc.k = sc.k;
+    p.sc.v = sc.v;
+    p.sc.pos = sc.pos;
+    p.sc.block_table = sc.block_table;
+    p.sc.d = sc.d;
+    p.sc.bs = sc.block_size;
+    p.sc.nbps = sc.nbps;
+    p.sc.bf16 = sc.bf16;
+    // the tile choice of gemm_dispatch for M <= 128 outside the CTA-pair range
+    const int sms = num_sms_current_device();
+    const int pair_tiles = (N + 255) / 256;
+    if (g_gemm_pairs && pair_tiles * 2 >= (sms * 3) / 4) return B2_ERR_UNSUPPORTED;
+    const int t256 = (N + 255) / 256, t128 = (N + 127) / 128, t64 = (N + 63) / 64, t32 = (N + 31) / 32;
+    plan_split(p, 1, nullptr, 0, sms);  // one k range per tile (sets kb_per_split)
+    if (t256 >= sms) return launch_tc<256, B2_EPI_BIAS, false>(p, A, BT, st, 0);
+    if (t128 >= sms) return launch_tc<128, B2_EPI_BIAS, false>(p, A, BT, st, 0);
+    if (t64 * 2 <= sms && t32 <= sms) return launch_tc<32, B2_EPI_BIAS, false>(p, A, BT, st, 0);
+    return launch_tc<64, B2_EPI_BIAS, false>(p, A, BT, st, 0);
 }
 
 }  // namespace b2

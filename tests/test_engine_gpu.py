@@ -108,3 +108,26 @@ def test_engine_rejects_bad_inputs(b2, cuda, tmp_path):
         e.start([[SMALL["vocab_size"]]], 4)                  # token id out of range
     with pytest.raises(b2.B2Error):
         e.start([[1] * 60], 10)                              # beyond max_seq_len
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_fused_qkv_split_equals_separate_kernel(b2, cuda, kv_dtype, monkeypatch):
+    """The QKV GEMM's epilogue writes q and the paged K/V itself; with the fusion switched
+    off (B2_ENGINE_FUSE_QKV=0) the same step runs GEMM + scatter kernel. Same arithmetic, so
+    tokens and logits are identical."""
+    rng = np.random.default_rng(4)
+    prompts = _prompts(rng, 3, SMALL["vocab_size"], [5, 2, 8])
+    out = []
+    for fuse in ("1", "0"):
+        monkeypatch.setenv("B2_ENGINE_FUSE_QKV", fuse)
+        e = b2.Engine.random(SMALL, max_batch=3, kv_dtype=kv_dtype, seed=17)
+        e.start(prompts, 6, seed=7)
+        e.keep_logits(True)
+        logits = []
+        for _ in range(10):
+            e.step()
+            logits.append(e.logits())
+        out.append((e.tokens(), np.stack(logits)))
+        e.close()
+    assert np.array_equal(out[0][0], out[1][0])
+    assert np.array_equal(out[0][1], out[1][1])
