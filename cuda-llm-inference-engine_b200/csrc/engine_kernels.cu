@@ -127,6 +127,89 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
     }
 }
 
+// One warp per row (32-thread CTA), the row in registers (cols <= 32 x 4 x NV4, 16-byte
+// aligned): the same LayerNorm and quantiser arithmetic as ln_quant_kernel with shuffle
+// reductions instead of CTA-wide ones (decode rows are short).
+template <int NV4>
+__global__ void __launch_bounds__(32)
+ln_quant_warp_kernel(int cols, const float* __restrict__ x, const float* __restrict__ gamma,
+                     const float* __restrict__ beta, float eps, int32_t* __restrict__ q_out,
+                     float* __restrict__ scale_out, float* __restrict__ y_out, __nv_bfloat16* __restrict__ y_hi,
+                     __nv_bfloat16* __restrict__ y_lo) {
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.x, lane = threadIdx.x;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * cols);
+    const int c4 = cols >> 2;
+    float4 v[NV4];
+    float s = 0.f, ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < c4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        ss = fmaf(v[k].x, v[k].x, ss);
+        ss = fmaf(v[k].y, v[k].y, ss);
+        ss = fmaf(v[k].z, v[k].z, ss);
+        ss = fmaf(v[k].w, v[k].w, ss);
+    }
+    const float mean = warp_sum(s) / cols;
+    const float var = warp_sum(ss) / cols - mean * mean;
+    const float inv = rsqrtf(var + eps);
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = lane + 32 * k;
+        if (i < c4) {
+            const float4 g = reinterpret_cast<const float4*>(gamma)[i];
+            const float4 bb = reinterpret_cast<const float4*>(beta)[i];
+            v[k].x = fmaf(g.x * (v[k].x - mean), inv, bb.x);
+            v[k].y = fmaf(g.y * (v[k].y - mean), inv, bb.y);
+            v[k].z = fmaf(g.z * (v[k].z - mean), inv, bb.z);
+            v[k].w = fmaf(g.w * (v[k].w - mean), inv, bb.w);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+        }
+    }
+    if (!q_out) {  // plain LayerNorm (final ln_f feeding the vocab projection), fp32 and/or bf16 hi/lo
+#pragma unroll
+        for (int k = 0; k < NV4; ++k) {
+            const int i = lane + 32 * k;
+            if (i >= c4) continue;
+            const float t[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+            if (y_out) reinterpret_cast<float4*>(y_out + (size_t)row * cols)[i] = v[k];
+            if (y_hi) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(t[j]);
+                    y_hi[(size_t)row * cols + 4 * i + j] = h;
+                    y_lo[(size_t)row * cols + 4 * i + j] = __float2bfloat16_rn(t[j] - __bfloat162float(h));
+                }
+            }
+        }
+        return;
+    }
+    amax = warp_max(amax);
+    // quantiser semantics of kernels/quantization/14_int8_gemm.cu:36-58
+    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float invs = __fdiv_rn(1.0f, scale);
+    if (lane == 0) scale_out[row] = scale;
+    int32_t* qr = q_out + (size_t)row * c4;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = lane + 32 * k;
+        if (i >= c4) continue;
+        const float t[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        uint32_t packed = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float qf = fminf(fmaxf(rintf(__fmul_rn(t[j], invs)), -128.f), 127.f);
+            packed |= (uint32_t)(uint8_t)(int8_t)(int)qf << (8 * j);
+        }
+        qr[i] = (int32_t)packed;
+        if (y_out) reinterpret_cast<float4*>(y_out + (size_t)row * cols)[i] = v[k];
+    }
+}
+
 // ------------------------------------------------------------------ QKV split + paged KV write
 template <typename KV>
 __device__ __forceinline__ KV to_kv(float v);
@@ -248,6 +331,19 @@ int launch_embed(int B, int d, const int* tokens, const int* pos, const float* w
 int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
                     int32_t* q, float* scale, float* y, cudaStream_t st, void* y_hi, void* y_lo) {
     if (cols > LNQ_THREADS * LNQ_MAX_PER_THREAD || (cols & 3)) return B2_ERR_UNSUPPORTED;
+    if (cols <= 4096 && ((uintptr_t)x & 15) == 0) {
+        const int c4 = cols / 4;
+        auto* hi = static_cast<__nv_bfloat16*>(y_hi);
+        auto* lo = static_cast<__nv_bfloat16*>(y_lo);
+        cudaError_t e;
+        if (c4 <= 64)
+            e = launch_kernel(ln_quant_warp_kernel<2>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+        else if (c4 <= 256)
+            e = launch_kernel(ln_quant_warp_kernel<8>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+        else
+            e = launch_kernel(ln_quant_warp_kernel<32>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+        return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    }
     return launch_kernel(ln_quant_kernel, dim3(rows), dim3(LNQ_THREADS), 0, st, cols, x, gamma, beta, eps, q, scale,
                          y, static_cast<__nv_bfloat16*>(y_hi), static_cast<__nv_bfloat16*>(y_lo)) == cudaSuccess
                ? B2_OK

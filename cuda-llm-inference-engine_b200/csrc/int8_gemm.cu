@@ -81,14 +81,64 @@ quantize_rows_kernel(int cols, const float* __restrict__ in, int32_t* __restrict
     }
 }
 
+// Rows of at most 32 x 4 x NV4 columns (16-byte aligned): one warp per row in a 32-thread
+// CTA, the row held in registers, shuffle reductions only (decode rows are short: a CTA-wide
+// reduction costs more than the row's bytes).
+template <int NV4>
+__global__ void __launch_bounds__(32)
+quantize_rows_warp_kernel(int cols, const float* __restrict__ in, int32_t* __restrict__ out,
+                          float* __restrict__ scales) {
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.x, lane = threadIdx.x;
+    const float4* x4 = reinterpret_cast<const float4*>(in + (size_t)row * cols);
+    const int c4 = cols >> 2;
+    float4 v[NV4];
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < c4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+    }
+    amax = warp_max(amax);
+    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (lane == 0) scales[row] = scale;
+    int32_t* o = out + (size_t)row * c4;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = lane + 32 * k;
+        if (i < c4) {
+            const float t[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+            uint32_t packed = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float q = fminf(fmaxf(rintf(__fmul_rn(t[j], inv)), -128.f), 127.f);
+                packed |= (uint32_t)(uint8_t)(int8_t)(int)q << (8 * j);
+            }
+            o[i] = (int32_t)packed;
+        }
+    }
+}
+
 int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st) {
     if (rows < 0 || cols < 0 || (cols & 3)) return B2_ERR_INVALID;
     if (rows == 0) return B2_OK;
     if (!in || !out || !scales) return B2_ERR_INVALID;
-    return launch_kernel(quantize_rows_kernel, dim3(rows), dim3(QZ_THREADS), 0, st, cols, in, out, scales) ==
-                   cudaSuccess
-               ? B2_OK
-               : B2_ERR_CUDA;
+    cudaError_t e;
+    if (((uintptr_t)in & 15) == 0 && cols <= 4096) {
+        const int c4 = (cols + 3) / 4;
+        if (c4 <= 64)
+            e = launch_kernel(quantize_rows_warp_kernel<2>, dim3(rows), dim3(32), 0, st, cols, in, out, scales);
+        else if (c4 <= 256)
+            e = launch_kernel(quantize_rows_warp_kernel<8>, dim3(rows), dim3(32), 0, st, cols, in, out, scales);
+        else
+            e = launch_kernel(quantize_rows_warp_kernel<32>, dim3(rows), dim3(32), 0, st, cols, in, out, scales);
+    } else {
+        e = launch_kernel(quantize_rows_kernel, dim3(rows), dim3(QZ_THREADS), 0, st, cols, in, out, scales);
+    }
+    return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
 // ------------------------------------------------------------------ tcgen05 GEMM
