@@ -440,16 +440,20 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
     prompts = [list(map(int, rng.integers(0, cfg["vocab_size"], prompt_len))) for _ in range(B)]
     eng.start(prompts, steps_new, seed=block_seed())
     st = torch.cuda.current_stream()
-    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-    e0.record(st)
-    eng.run_steps(prompt_len - 1, stream=st)      # positions 0..126: the prompt
+    e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+    eng.prefill(stream=st)                         # warm-up (allocates the prefill buffers) ...
+    eng.start(prompts, steps_new, seed=block_seed())  # ... then the same prompts from scratch
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    eng.prefill(stream=st)                         # positions 0..126 of every prompt in one pass
+    torch.cuda.synchronize()
+    pre_ms = (time.perf_counter() - t0) * 1e3      # synchronous call: host clock, end to end
     e1.record(st)
     eng.run_steps(steps_new, stream=st)           # positions 127..254: 128 generated tokens
     e2.record(st)
     torch.cuda.synchronize()
     assert b2.device_error() == 0
     gen_ms = e1.elapsed_time(e2)
-    pre_ms = e0.elapsed_time(e1)
     ctx_mean = prompt_len + (steps_new - 1) / 2.0 + 0.5
     by = gpt2_step_bytes(cfg, B, ctx_mean)
     step_s = gen_ms / steps_new * 1e-3
@@ -458,6 +462,7 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
     eng.close()
     return {"tok_s": round(B * steps_new / (gen_ms * 1e-3), 1), "ms_per_step": round(gen_ms / steps_new, 4),
             "prefill_tok_s": round(B * (prompt_len - 1) / (pre_ms * 1e-3), 1),
+            "prefill": "b2_engine_prefill: the 127 x 64 prompt tokens in one batched pass (host clock)",
             "step_bytes": int(by), "gbs": round(by / step_s / 1e9, 1),
             "frac_of_hbm_bound": round(by / step_s / 1e9 / hbm_peak, 4),
             "hbm_bound_tok_s": round(B / (by / (hbm_peak * 1e9)), 1),

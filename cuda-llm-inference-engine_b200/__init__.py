@@ -334,7 +334,7 @@ ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_nccl_unique_id", "b2_engine_cre
                   "b2_engine_fill_kv_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
                   "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps",
                   "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions",
-                  "b2_engine_profile_step"]
+                  "b2_engine_profile_step", "b2_engine_prefill"]
 
 
 def _engine_lib():
@@ -356,6 +356,7 @@ def _engine_lib():
     lib.b2_engine_step.argtypes = [vp, vp]
     lib.b2_engine_run_steps.argtypes = [vp, i, vp]
     lib.b2_engine_profile_step.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
+    lib.b2_engine_prefill.argtypes = [vp, vp]
     lib.b2_engine_read_tokens.argtypes = [vp, vp, i]
     lib.b2_engine_keep_logits.argtypes = [vp, i, ctypes.POINTER(vp)]
     lib.b2_engine_read_logits.argtypes = [vp, vp]
@@ -434,6 +435,11 @@ class Engine:
 
     def step(self, stream=None):
         _check(self._lib.b2_engine_step(self._h, _stream(stream)), "b2_engine_step")
+
+    def prefill(self, stream=None):
+        """Right after start(): all prompt tokens but the last of each sequence in one batched
+        pass (b2_engine_prefill); the next step predicts the first new token."""
+        _check(self._lib.b2_engine_prefill(self._h, _stream(stream)), "b2_engine_prefill")
 
     def run_steps(self, steps: int, stream=None):
         _check(self._lib.b2_engine_run_steps(self._h, steps, _stream(stream)), "b2_engine_run_steps")

@@ -60,6 +60,7 @@ const NcclApi& nccl() {
 }
 
 constexpr int kBlock = 16;        // KV block size (reference engine: block_size_ = 16)
+constexpr int kPrefillRows = 8192;  // prompt tokens per prefill pass (longer prompts run in chunks)
 constexpr float kLnEps = 1e-5f;   // reference LayerNorm eps (15_layernorm_residual.cuh default)
 
 // Device linear layer in the reference's QuantWeight format + bias.
@@ -156,6 +157,20 @@ struct b2_engine {
     cudaGraphExec_t graph = nullptr;
     bool graph_dirty = true;
     bool failed = false;  // a device allocation failed
+    // host copies of the current sequences' prompts and block tables (prefill builds its rows
+    // from them); at_start: no step has run since b2_engine_start (every position is 0)
+    std::vector<int> host_prompts, host_prompt_lens, host_bt;
+    int host_prompt_stride = 0;
+    bool at_start = false;
+    // batched prefill: one row per prompt token, buffers allocated on first use for pf_cap rows
+    int pf_cap = 0;
+    int *pf_tokens = nullptr, *pf_pos = nullptr, *pf_ctx = nullptr, *pf_bt = nullptr;
+    unsigned long long* pf_keys = nullptr;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_hbuf = nullptr, *pf_xs = nullptr,
+          *pf_amax = nullptr;
+    int32_t *pf_xq = nullptr, *pf_acc32 = nullptr;
+    void* pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
     // fused QKV split in the GEMM epilogue (B2_ENGINE_FUSE_QKV=0 runs GEMM + scatter kernel)
     bool fuse_qkv = !(getenv("B2_ENGINE_FUSE_QKV") && strcmp(getenv("B2_ENGINE_FUSE_QKV"), "0") == 0);
 
@@ -369,18 +384,37 @@ struct StepProfiler {
     }
 };
 
-int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
-    PdlScope pdl;
+// The rows one pass of the layer stack runs over: the decode step's batch (one row per
+// sequence, at its current position) or a prefill chunk (one row per prompt token). Every
+// row carries its token, position, context length (position + 1, written by the embedding)
+// and block-table row; activations and workspaces are sized for n rows.
+struct RowSet {
+    int n = 0;
+    const int* tokens = nullptr;
+    const int* pos = nullptr;
+    int* ctx = nullptr;
+    const int* block_table = nullptr;  // [n, blocks_per_seq]
+    unsigned long long* keys = nullptr;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *hbuf = nullptr, *xs = nullptr, *amax = nullptr;
+    int32_t *xq = nullptr, *acc32 = nullptr;
+    void* attn_ws = nullptr;
+    size_t attn_ws_bytes = 0;
+    int max_ctx = 0;
+    bool p2p = false;  // the peer-memory exchange (its buffers are the decode step's)
+};
+
+// Embedding and every transformer layer for the rows of R (no final LayerNorm / vocab).
+int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler* prof) {
     auto M = [&](const char* label) {
         if (prof) prof->mark(label);
     };
     const b2_gpt2_config& c = e->cfg;
-    const int B = e->batch, d = c.d_model, ff = c.d_ff, H = c.n_heads, dh = c.d_head;
+    const int B = R.n, d = c.d_model, ff = c.d_ff, dh = c.d_head;
     const size_t kvb = e->kv_dtype == B2_KV_F32 ? 4 : 2;
     int r;
 #define B2_TRY(x) do { if ((r = (x)) != B2_OK) return r; } while (0)
     M("embed");
-    B2_TRY(launch_embed(B, d, e->tokens, e->pos, e->wte, e->wpe, e->x, e->ctx, e->keys, st));
+    B2_TRY(launch_embed(B, d, R.tokens, R.pos, e->wte, e->wpe, R.x, R.ctx, R.keys, st));
     const bool tp = e->tp_size > 1;
     const int Hl = e->Hl, dl = e->dl, ffl = e->ffl;
     // all-reduces of the tensor-parallel step (NCCL on the step's stream; captured in the graph)
@@ -391,30 +425,30 @@ int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
     // local int32 GEMM over them, int32 all-reduce (exact), then the dequant epilogue
     auto row_parallel = [&](const float* act, int kl, const QLinear& W, const char* gemm_label) {
         int r2;
-        if (e->p2p) {
+        if (R.p2p) {
             M("tp_quantize");
-            if ((r2 = launch_tp_quantize(B, kl, act, e->xq, e->xs, e->peers, st)) != B2_OK) return r2;
+            if ((r2 = launch_tp_quantize(B, kl, act, R.xq, R.xs, e->peers, st)) != B2_OK) return r2;
             M(gemm_label);
-            if ((r2 = gemm_launch(B, d, kl, e->xq, W.w, nullptr, nullptr, nullptr, nullptr, e->acc32, B2_EPI_PLAIN,
+            if ((r2 = gemm_launch(B, d, kl, R.xq, W.w, nullptr, nullptr, nullptr, nullptr, R.acc32, B2_EPI_PLAIN,
                                   true, st)) != B2_OK)
                 return r2;
             M("tp_reduce");
-            return launch_tp_reduce(B, d, e->xs, W.s, W.bias, e->peers, st);
+            return launch_tp_reduce(B, d, R.xs, W.s, W.bias, e->peers, st);
         }
         M("rowmax");
-        if ((r2 = launch_rowmax(B, kl, act, e->amax, st)) != B2_OK) return r2;
+        if ((r2 = launch_rowmax(B, kl, act, R.amax, st)) != B2_OK) return r2;
         M("allreduce_amax");
-        if ((r2 = allreduce(e->amax, B, ncclFloat, ncclMax)) != B2_OK) return r2;
+        if ((r2 = allreduce(R.amax, B, ncclFloat, ncclMax)) != B2_OK) return r2;
         M("quantize_scaled");
-        if ((r2 = launch_quantize_scaled(B, kl, act, e->amax, e->xq, e->xs, st)) != B2_OK) return r2;
+        if ((r2 = launch_quantize_scaled(B, kl, act, R.amax, R.xq, R.xs, st)) != B2_OK) return r2;
         M(gemm_label);
-        if ((r2 = gemm_launch(B, d, kl, e->xq, W.w, nullptr, nullptr, nullptr, nullptr, e->acc32, B2_EPI_PLAIN, true,
+        if ((r2 = gemm_launch(B, d, kl, R.xq, W.w, nullptr, nullptr, nullptr, nullptr, R.acc32, B2_EPI_PLAIN, true,
                               st)) != B2_OK)
             return r2;
         M("allreduce_partials");
-        if ((r2 = allreduce(e->acc32, (size_t)B * d, ncclInt32, ncclSum)) != B2_OK) return r2;
+        if ((r2 = allreduce(R.acc32, (size_t)B * d, ncclInt32, ncclSum)) != B2_OK) return r2;
         M("dequant_residual");
-        return launch_dequant_residual(B, d, e->acc32, e->xs, W.s, W.bias, e->x, e->x, st);
+        return launch_dequant_residual(B, d, R.acc32, R.xs, W.s, W.bias, R.x, R.x, st);
     };
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer& L = e->layers[l];
@@ -422,65 +456,96 @@ int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
         unsigned char* vc = static_cast<unsigned char*>(e->v_pool) + (size_t)l * e->layer_stride * kvb;
         // attention sub-block (pre-norm; x stays the residual and is updated in place)
         M("ln_quant");
-        B2_TRY(launch_ln_quant(B, d, e->x, L.ln1_g, L.ln1_b, kLnEps, e->xq, e->xs, nullptr, st));
+        B2_TRY(launch_ln_quant(B, d, R.x, L.ln1_g, L.ln1_b, kLnEps, R.xq, R.xs, nullptr, st));
         // QKV linear with the split into q and the paged K/V write in its epilogue; shapes the
         // fused path does not take run as GEMM + scatter kernel
         M("gemm_qkv");
         QkvScatterArgs qa;
-        qa.q = e->q;
+        qa.q = R.q;
         qa.k = kc;
         qa.v = vc;
-        qa.pos = e->pos;
-        qa.block_table = e->block_table;
+        qa.pos = R.pos;
+        qa.block_table = R.block_table;
         qa.d = dl;
         qa.block_size = kBlock;
         qa.nbps = e->blocks_per_seq;
         qa.bf16 = e->kv_dtype == B2_KV_BF16;
-        r = e->fuse_qkv ? gemm_launch_qkv(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, qa, st)
+        r = e->fuse_qkv ? gemm_launch_qkv(B, 3 * dl, d, R.xq, L.qkv.w, R.xs, L.qkv.s, L.qkv.bias, qa, st)
                         : B2_ERR_UNSUPPORTED;
         if (r == B2_ERR_UNSUPPORTED) {
-            B2_TRY(gemm_launch(B, 3 * dl, d, e->xq, L.qkv.w, e->xs, L.qkv.s, L.qkv.bias, nullptr, e->qkv, B2_EPI_BIAS,
+            B2_TRY(gemm_launch(B, 3 * dl, d, R.xq, L.qkv.w, R.xs, L.qkv.s, L.qkv.bias, nullptr, R.qkv, B2_EPI_BIAS,
                                false, st));
             M("qkv_scatter");
-            B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, e->qkv, e->pos, e->block_table, e->q, kc,
+            B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, R.qkv, R.pos, R.block_table, R.q, kc,
                                       vc, e->kv_dtype, st));
         } else if (r != B2_OK) {
             return r;
         }
         b2_decode_attn_args a{};
         a.B = B; a.H_q = Hl; a.H_kv = Hl; a.head_dim = dh;
-        a.Q = e->q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;
-        a.block_table = e->block_table; a.context_lens = e->ctx;
-        a.max_context_len = c.max_seq_len; a.block_size = kBlock; a.num_blocks_per_seq = e->blocks_per_seq;
-        a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = e->attn;
-        a.workspace = e->attn_ws; a.workspace_bytes = e->attn_ws_bytes;
+        a.Q = R.q; a.k_cache = kc; a.v_cache = vc; a.kv_dtype = e->kv_dtype;
+        a.block_table = R.block_table; a.context_lens = R.ctx;
+        a.max_context_len = R.max_ctx; a.block_size = kBlock; a.num_blocks_per_seq = e->blocks_per_seq;
+        a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = R.attn;
+        a.workspace = R.attn_ws; a.workspace_bytes = R.attn_ws_bytes;
         M("attention");
         B2_TRY(decode_attn_launch(&a, 64, true, st));
         if (tp) {
-            B2_TRY(row_parallel(e->attn, dl, L.out, "gemm_out"));
+            B2_TRY(row_parallel(R.attn, dl, L.out, "gemm_out"));
         } else {
             M("quantize");
-            B2_TRY(quantize_launch(B, d, e->attn, e->xq, e->xs, st));
+            B2_TRY(quantize_launch(B, d, R.attn, R.xq, R.xs, st));
             M("gemm_out");
-            B2_TRY(gemm_launch(B, d, d, e->xq, L.out.w, e->xs, L.out.s, L.out.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+            B2_TRY(gemm_launch(B, d, d, R.xq, L.out.w, R.xs, L.out.s, L.out.bias, R.x, R.x, B2_EPI_BIAS_RESIDUAL,
                                false, st));
         }
         // MLP sub-block
         M("ln_quant");
-        B2_TRY(launch_ln_quant(B, d, e->x, L.ln2_g, L.ln2_b, kLnEps, e->xq, e->xs, nullptr, st));
+        B2_TRY(launch_ln_quant(B, d, R.x, L.ln2_g, L.ln2_b, kLnEps, R.xq, R.xs, nullptr, st));
         M("gemm_fc1");
-        B2_TRY(gemm_launch(B, ffl, d, e->xq, L.up.w, e->xs, L.up.s, L.up.bias, nullptr, e->hbuf, B2_EPI_BIAS_GELU, false,
+        B2_TRY(gemm_launch(B, ffl, d, R.xq, L.up.w, R.xs, L.up.s, L.up.bias, nullptr, R.hbuf, B2_EPI_BIAS_GELU, false,
                            st));
         if (tp) {
-            B2_TRY(row_parallel(e->hbuf, ffl, L.down, "gemm_fc2"));
+            B2_TRY(row_parallel(R.hbuf, ffl, L.down, "gemm_fc2"));
         } else {
             M("quantize");
-            B2_TRY(quantize_launch(B, ff, e->hbuf, e->xq, e->xs, st));
+            B2_TRY(quantize_launch(B, ff, R.hbuf, R.xq, R.xs, st));
             M("gemm_fc2");
-            B2_TRY(gemm_launch(B, d, ff, e->xq, L.down.w, e->xs, L.down.s, L.down.bias, e->x, e->x, B2_EPI_BIAS_RESIDUAL,
+            B2_TRY(gemm_launch(B, d, ff, R.xq, L.down.w, R.xs, L.down.s, L.down.bias, R.x, R.x, B2_EPI_BIAS_RESIDUAL,
                                false, st));
         }
     }
+#undef B2_TRY
+    return B2_OK;
+}
+
+int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
+    PdlScope pdl;
+    auto M = [&](const char* label) {
+        if (prof) prof->mark(label);
+    };
+    const b2_gpt2_config& c = e->cfg;
+    const int B = e->batch, d = c.d_model;
+    const bool tp = e->tp_size > 1;
+    RowSet R;
+    R.n = B;
+    R.tokens = e->tokens;
+    R.pos = e->pos;
+    R.ctx = e->ctx;
+    R.block_table = e->block_table;
+    R.keys = e->keys;
+    R.x = e->x; R.qkv = e->qkv; R.q = e->q; R.attn = e->attn; R.hbuf = e->hbuf; R.xs = e->xs; R.amax = e->amax;
+    R.xq = e->xq; R.acc32 = e->acc32;
+    R.attn_ws = e->attn_ws;
+    R.attn_ws_bytes = e->attn_ws_bytes;
+    R.max_ctx = c.max_seq_len;
+    R.p2p = e->p2p;
+    int r;
+#define B2_TRY(x) do { if ((r = (x)) != B2_OK) return r; } while (0)
+    B2_TRY(enqueue_layers(e, R, st, prof));
+    auto allreduce = [&](void* buf, size_t n, ncclDataType_t t, ncclRedOp_t op) {
+        return nccl().AllReduce(buf, buf, n, t, op, e->comm, st) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
+    };
     M("ln_final");
     B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
                            e->xf_lo));
@@ -865,16 +930,112 @@ int b2_engine_start(b2_engine* e, int batch, const int32_t* prompts_host, const 
               cudaMemcpy(e->pos, zero.data(), (size_t)batch * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
               cudaMemset(e->out_tokens, 0xff, (size_t)batch * ostride * 4) == cudaSuccess;
     e->graph_dirty = true;  // the batch size or buffers may have changed
+    e->host_prompts.assign(prompts_host, prompts_host + (size_t)batch * stride);
+    e->host_prompt_lens.assign(prompt_lens_host, prompt_lens_host + batch);
+    e->host_prompt_stride = stride;
+    e->host_bt = bt;
+    e->at_start = ok;
     return ok ? B2_OK : B2_ERR_CUDA;
 }
 
 int b2_engine_step(b2_engine* e, b2_stream_t stream) {
     if (!e || e->batch <= 0) return B2_ERR_INVALID;
+    e->at_start = false;
     return enqueue_step(e, static_cast<cudaStream_t>(stream));
+}
+
+int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
+    if (!e || e->batch <= 0 || !e->at_start) return B2_ERR_INVALID;
+    const b2_gpt2_config& c = e->cfg;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int nbps = e->blocks_per_seq;
+    // rows: every prompt token but each sequence's last, in (sequence, position) order
+    std::vector<int> rb, rp;
+    for (int b = 0; b < e->batch; ++b)
+        for (int p = 0; p + 1 < e->host_prompt_lens[b]; ++p) {
+            rb.push_back(b);
+            rp.push_back(p);
+        }
+    const int total = (int)rb.size();
+    if (total > 0 && e->pf_cap == 0) {
+        const int cap = std::min(total, kPrefillRows);
+        const int d = c.d_model;
+        e->pf_tokens = e->alloc<int>(cap);
+        e->pf_pos = e->alloc<int>(cap);
+        e->pf_ctx = e->alloc<int>(cap);
+        e->pf_bt = e->alloc<int>((size_t)cap * nbps);
+        e->pf_keys = e->alloc<unsigned long long>(cap);
+        e->pf_x = e->alloc<float>((size_t)cap * d);
+        e->pf_qkv = e->alloc<float>((size_t)cap * 3 * e->dl);
+        e->pf_q = e->alloc<float>((size_t)cap * d);
+        e->pf_attn = e->alloc<float>((size_t)cap * d);
+        e->pf_hbuf = e->alloc<float>((size_t)cap * e->ffl);
+        e->pf_xs = e->alloc<float>(cap);
+        e->pf_amax = e->alloc<float>(cap);
+        e->pf_xq = e->alloc<int32_t>((size_t)cap * std::max(d, c.d_ff) / 4);
+        e->pf_acc32 = e->alloc<int32_t>((size_t)cap * d);
+        e->pf_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(cap, e->Hl, e->Hl, c.d_head, c.max_seq_len,
+                                                                          kBlock, 64, 4));
+        e->pf_ws = e->alloc<unsigned char>(e->pf_ws_bytes);
+        if (e->failed || cudaMemset(e->pf_ws, 0, e->pf_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
+        e->pf_cap = cap;
+    }
+    std::vector<int> tok, pos, bt;
+    for (int r0 = 0; r0 < total; r0 += e->pf_cap) {
+        const int n = std::min(e->pf_cap, total - r0);
+        tok.resize(n);
+        pos.resize(n);
+        bt.resize((size_t)n * nbps);
+        int max_ctx = 1;
+        for (int i = 0; i < n; ++i) {
+            const int b = rb[r0 + i], p = rp[r0 + i];
+            tok[i] = e->host_prompts[(size_t)b * e->host_prompt_stride + p];
+            pos[i] = p;
+            max_ctx = std::max(max_ctx, p + 1);
+            std::copy(e->host_bt.begin() + (size_t)b * nbps, e->host_bt.begin() + (size_t)(b + 1) * nbps,
+                      bt.begin() + (size_t)i * nbps);
+        }
+        // the previous chunk has finished with the row arrays before they are overwritten
+        if (cudaStreamSynchronize(st) != cudaSuccess ||
+            cudaMemcpy(e->pf_tokens, tok.data(), (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(e->pf_pos, pos.data(), (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(e->pf_bt, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return B2_ERR_CUDA;
+        RowSet R;
+        R.n = n;
+        R.tokens = e->pf_tokens;
+        R.pos = e->pf_pos;
+        R.ctx = e->pf_ctx;
+        R.block_table = e->pf_bt;
+        R.keys = e->pf_keys;
+        R.x = e->pf_x; R.qkv = e->pf_qkv; R.q = e->pf_q; R.attn = e->pf_attn; R.hbuf = e->pf_hbuf; R.xs = e->pf_xs;
+        R.amax = e->pf_amax; R.xq = e->pf_xq; R.acc32 = e->pf_acc32;
+        R.attn_ws = e->pf_ws;
+        R.attn_ws_bytes = e->pf_ws_bytes;
+        R.max_ctx = max_ctx;
+        R.p2p = false;  // the peer-mapped buffers are the decode step's: NCCL all-reduces here
+        PdlScope pdl;
+        const int r = enqueue_layers(e, R, st, nullptr);
+        if (r != B2_OK) return r;
+    }
+    // continue at each sequence's last prompt token: the next step feeds it and predicts the
+    // first new token, exactly as after prompt_len - 1 steps
+    std::vector<int> tok_last(e->batch), pos_last(e->batch);
+    for (int b = 0; b < e->batch; ++b) {
+        pos_last[b] = e->host_prompt_lens[b] - 1;
+        tok_last[b] = e->host_prompts[(size_t)b * e->host_prompt_stride + pos_last[b]];
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess ||
+        cudaMemcpy(e->tokens, tok_last.data(), (size_t)e->batch * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(e->pos, pos_last.data(), (size_t)e->batch * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return B2_ERR_CUDA;
+    e->at_start = false;
+    return B2_OK;
 }
 
 int b2_engine_profile_step(b2_engine* e, char* report, size_t report_bytes) {
     if (!e || e->batch <= 0 || !report || report_bytes == 0) return B2_ERR_INVALID;
+    e->at_start = false;
     cudaStream_t st;
     if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return B2_ERR_CUDA;
     int r = B2_OK;
@@ -924,6 +1085,7 @@ int b2_engine_profile_step(b2_engine* e, char* report, size_t report_bytes) {
 
 int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream) {
     if (!e || e->batch <= 0 || steps < 0) return B2_ERR_INVALID;
+    if (steps > 0) e->at_start = false;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (e->graph_dirty || !e->graph) {
         if (e->graph) {
@@ -976,6 +1138,7 @@ int b2_engine_read_logits(const b2_engine* e, float* out_host) {
 }
 
 int b2_engine_fill_kv_random(b2_engine* e, int ctx_len, uint64_t seed) {
+    if (e) e->at_start = false;
     if (!e || e->batch <= 0 || ctx_len < 0 || ctx_len >= e->cfg.max_seq_len) return B2_ERR_INVALID;
     const size_t n = (size_t)e->cfg.n_layers * e->layer_stride;
     for (int which = 0; which < 2; ++which) {

@@ -78,6 +78,16 @@ int b2_engine_config(const b2_engine* e, b2_gpt2_config* out);
 int b2_engine_start(b2_engine* e, int batch, const int32_t* prompts_host, const int32_t* prompt_lens_host,
                     int prompt_stride, int max_new_tokens, uint64_t seed);
 
+/* Batched prefill, right after b2_engine_start: every prompt token but each sequence's last
+ * runs through the layer stack in one pass (8192 tokens per pass; longer prompts in several),
+ * one row per token: LayerNorm+quantise, one QKV GEMM over all rows with the K/V written to
+ * each token's cache slot, attention of each row over its own prefix, and the MLP; then every
+ * sequence waits at its last prompt token, so the next step predicts the first new token.
+ * Same K/V and states as prompt_len - 1 decode steps (attention splits may merge in another
+ * order: logits agree to ~1e-6 relative), except that the per-position predictions of those
+ * steps are not recorded. Under tensor parallelism every rank calls it. Synchronous. */
+int b2_engine_prefill(b2_engine* e, b2_stream_t stream);
+
 /* One decode step for every active sequence (asynchronous on `stream`). */
 int b2_engine_step(b2_engine* e, b2_stream_t stream);
 

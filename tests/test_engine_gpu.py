@@ -131,3 +131,65 @@ def test_fused_qkv_split_equals_separate_kernel(b2, cuda, kv_dtype, monkeypatch)
         e.close()
     assert np.array_equal(out[0][0], out[1][0])
     assert np.array_equal(out[0][1], out[1][1])
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_prefill_matches_token_by_token(b2, cuda, kv_dtype):
+    """Batched prefill of equal-length prompts, then decode steps, against the same prompts fed
+    one token per step: the steps after the prompt see the same K/V and hidden states (the
+    prefill rows' attention may merge splits in another order), so logits agree to 1e-4 of
+    their range and the greedy tokens match wherever the top-2 gap is clear."""
+    rng = np.random.default_rng(8)
+    L, new = 9, 5
+    prompts = _prompts(rng, 3, SMALL["vocab_size"], [L, L, L])
+    runs = []
+    for use_prefill in (True, False):
+        e = b2.Engine.random(SMALL, max_batch=3, kv_dtype=kv_dtype, seed=29)
+        e.start(prompts, new, seed=3)
+        e.keep_logits(True)
+        if use_prefill:
+            e.prefill()
+            assert np.array_equal(e.positions(), np.full(3, L - 1))
+        else:
+            for _ in range(L - 1):
+                e.step()
+        logits = []
+        for _ in range(new):
+            e.step()
+            logits.append(e.logits())
+        runs.append((np.stack(logits), e.tokens(), e.positions()))
+        assert b2.device_error() == 0
+        e.close()
+    (lp, tp, pp), (ld, td, pd) = runs
+    assert np.array_equal(pp, pd)
+    bound = 1e-4 * np.abs(ld).max()
+    assert np.abs(lp - ld).max() <= bound
+    top2 = np.sort(ld, axis=2)[..., -2:]
+    clear = (top2[..., 1] - top2[..., 0]) > 2 * bound  # [steps, batch]
+    for s in range(new):
+        for b in range(3):
+            if clear[s, b]:
+                assert tp[b, L + s] == td[b, L + s]
+
+
+def test_prefill_ragged_prompts_and_graph_replay(b2, cuda):
+    """Ragged prompts (one of a single token, which has nothing to prefill), prefill, then
+    CUDA-graph replays: the generated tokens equal those of pure token-by-token decoding."""
+    rng = np.random.default_rng(9)
+    lens, new = [6, 1, 11], 4
+    prompts = _prompts(rng, 3, SMALL["vocab_size"], lens)
+    e1 = b2.Engine.random(SMALL, max_batch=3, seed=31)
+    e1.start(prompts, new, seed=5)
+    e1.prefill()
+    assert np.array_equal(e1.positions(), np.array(lens) - 1)
+    e1.run_steps(new)
+    t1 = e1.tokens()
+    e2 = b2.Engine.random(SMALL, max_batch=3, seed=31)
+    e2.start(prompts, new, seed=5)
+    for _ in range(max(lens) - 1 + new):
+        e2.step()
+    t2 = e2.tokens()
+    for b, n in enumerate(lens):
+        assert np.array_equal(t1[b, n:n + new], t2[b, n:n + new]), b
+    with pytest.raises(b2.B2Error):
+        e1.prefill()  # only right after start()
