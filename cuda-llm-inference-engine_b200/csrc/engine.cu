@@ -61,6 +61,7 @@ const NcclApi& nccl() {
 
 constexpr int kBlock = 16;        // KV block size (reference engine: block_size_ = 16)
 constexpr int kPrefillRows = 8192;  // prompt tokens per prefill pass (longer prompts run in chunks)
+constexpr int kPrefillItemRows = 16;  // rows of one sequence per prefill-attention CTA (PA_PQ)
 constexpr float kLnEps = 1e-5f;   // reference LayerNorm eps (15_layernorm_residual.cuh default)
 
 // Device linear layer in the reference's QuantWeight format + bias.
@@ -165,6 +166,7 @@ struct b2_engine {
     // batched prefill: one row per prompt token, buffers allocated on first use for pf_cap rows
     int pf_cap = 0;
     int *pf_tokens = nullptr, *pf_pos = nullptr, *pf_ctx = nullptr, *pf_bt = nullptr;
+    int2* pf_items = nullptr;
     unsigned long long* pf_keys = nullptr;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_hbuf = nullptr, *pf_xs = nullptr,
           *pf_amax = nullptr;
@@ -401,6 +403,9 @@ struct RowSet {
     size_t attn_ws_bytes = 0;
     int max_ctx = 0;
     bool p2p = false;  // the peer-memory exchange (its buffers are the decode step's)
+    // prefill: causal attention over work items (first row, rows) of one sequence each
+    const int2* items = nullptr;
+    int n_items = 0;
 };
 
 // Embedding and every transformer layer for the rows of R (no final LayerNorm / vocab).
@@ -489,7 +494,11 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
         a.num_phys_blocks = e->num_blocks; a.scale = 0.f; a.O = R.attn;
         a.workspace = R.attn_ws; a.workspace_bytes = R.attn_ws_bytes;
         M("attention");
-        B2_TRY(decode_attn_launch(&a, 64, true, st));
+        if (R.items)
+            B2_TRY(launch_prefill_attention(R.items, R.n_items, Hl, dh, e->kv_dtype, R.q, kc, vc, R.block_table,
+                                            e->blocks_per_seq, kBlock, R.pos, R.attn, st));
+        else
+            B2_TRY(decode_attn_launch(&a, 64, true, st));
         if (tp) {
             B2_TRY(row_parallel(R.attn, dl, L.out, "gemm_out"));
         } else {
@@ -964,6 +973,7 @@ int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
         e->pf_pos = e->alloc<int>(cap);
         e->pf_ctx = e->alloc<int>(cap);
         e->pf_bt = e->alloc<int>((size_t)cap * nbps);
+        e->pf_items = e->alloc<int2>(cap);
         e->pf_keys = e->alloc<unsigned long long>(cap);
         e->pf_x = e->alloc<float>((size_t)cap * d);
         e->pf_qkv = e->alloc<float>((size_t)cap * 3 * e->dl);
@@ -981,11 +991,13 @@ int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
         e->pf_cap = cap;
     }
     std::vector<int> tok, pos, bt;
+    std::vector<int2> items;
     for (int r0 = 0; r0 < total; r0 += e->pf_cap) {
         const int n = std::min(e->pf_cap, total - r0);
         tok.resize(n);
         pos.resize(n);
         bt.resize((size_t)n * nbps);
+        items.clear();
         int max_ctx = 1;
         for (int i = 0; i < n; ++i) {
             const int b = rb[r0 + i], p = rp[r0 + i];
@@ -994,12 +1006,18 @@ int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
             max_ctx = std::max(max_ctx, p + 1);
             std::copy(e->host_bt.begin() + (size_t)b * nbps, e->host_bt.begin() + (size_t)(b + 1) * nbps,
                       bt.begin() + (size_t)i * nbps);
+            // attention work items: runs of up to kPrefillItemRows rows of one sequence
+            if (items.empty() || rb[r0 + items.back().x] != b || items.back().y == kPrefillItemRows)
+                items.push_back(make_int2(i, 1));
+            else
+                ++items.back().y;
         }
         // the previous chunk has finished with the row arrays before they are overwritten
         if (cudaStreamSynchronize(st) != cudaSuccess ||
             cudaMemcpy(e->pf_tokens, tok.data(), (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemcpy(e->pf_pos, pos.data(), (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-            cudaMemcpy(e->pf_bt, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            cudaMemcpy(e->pf_bt, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(e->pf_items, items.data(), items.size() * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess)
             return B2_ERR_CUDA;
         RowSet R;
         R.n = n;
@@ -1014,6 +1032,8 @@ int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
         R.attn_ws_bytes = e->pf_ws_bytes;
         R.max_ctx = max_ctx;
         R.p2p = false;  // the peer-mapped buffers are the decode step's: NCCL all-reduces here
+        R.items = e->pf_items;
+        R.n_items = (int)items.size();
         PdlScope pdl;
         const int r = enqueue_layers(e, R, st, nullptr);
         if (r != B2_OK) return r;

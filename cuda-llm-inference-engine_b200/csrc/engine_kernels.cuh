@@ -14,6 +14,9 @@ struct QkvScatterArgs {
     const int* block_table = nullptr;
     int d = 0, block_size = 0, nbps = 0, bf16 = 0;
 };
+int launch_prefill_attention(const int2* items, int n_items, int H, int D, int kv_dtype, const float* q,
+                             const void* k_cache, const void* v_cache, const int* block_table, int nbps,
+                             int block_size, const int* pos, float* O, cudaStream_t st);
 int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
                     const float* bias, const QkvScatterArgs& sc, cudaStream_t st);
 
