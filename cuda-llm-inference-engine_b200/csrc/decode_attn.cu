@@ -28,6 +28,8 @@
 #include <cuda_bf16.h>
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace b2 {
@@ -370,9 +372,15 @@ __device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int 
 // ------------------------------------------------------------------ the kernel
 // Grid (KV head, split, sequence): the CTA's warps merge through the ring's memory once the
 // producer is done.
-template <int G, int D, typename KV>
+// TMA = true: the producer's lane 0 moves each cache block of the tile with two 3-D TMA loads
+// (box head_dim x 1 head x block_size tokens of a tensor map over [P * block_size, H_kv,
+// head_dim]) into the same dense rows, completion counted in bytes on the stage's barrier;
+// used when tiles hold whole blocks and the pool size is known. Otherwise the warp gathers
+// rows with cp.async.
+template <int G, int D, typename KV, bool TMA>
 __global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
-decode_attn_kernel(const DecodeAttnParams p) {
+decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   const DecodeAttnParams p) {
     using C = DACfg<G, D, KV>;
     extern __shared__ __align__(1024) unsigned char smem[];
     // KV head fastest in the grid: the CTAs of one token range run side by side
@@ -411,7 +419,7 @@ decode_attn_kernel(const DecodeAttnParams p) {
 
     if (tid == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(full_bar(s), 32);  // one cp.async arrival per producer lane
+            mbar_init(full_bar(s), TMA ? 1 : 32);  // TMA: lane 0's expect_tx; else one cp.async arrival per lane
             mbar_init(empty_bar(s), DA_NW);
         }
         misc[0] = 0;  // abort flag
@@ -420,6 +428,51 @@ decode_attn_kernel(const DecodeAttnParams p) {
     }
     __syncthreads();
 
+    if constexpr (TMA) {
+        if (warp == DA_NW) {
+            // the split's slice of the block table in shared memory (all lanes), then lane 0
+            // issues the copies
+            const int* btg = p.block_table + (size_t)b * p.num_blocks_per_seq;
+            const int blk0 = tok_begin / p.block_size;
+            const int nbt = (tok_end - 1) / p.block_size - blk0 + 1;
+            int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT);
+            const bool staged = nbt <= C::BT_CAP;
+            if (staged) {
+                for (int j = lane; j < nbt; j += 32) bt_s[j] = btg[blk0 + j];
+                __syncwarp();
+            }
+            if (lane == 0) {
+                prefetch_tensormap(&kmap);
+                prefetch_tensormap(&vmap);
+                const uint64_t pol = policy_evict_first();
+                const int bs = p.block_size;
+                const uint32_t block_bytes = (uint32_t)(bs * C::ROW);
+                for (int i = 0; i < ntiles; ++i) {
+                    const int st = i % C::STAGES;
+                    if (i >= C::STAGES &&
+                        (misc[0] != 0 || !mbar_wait(empty_bar(st), ((i / C::STAGES) - 1) & 1, p.err))) {
+                        misc[0] = 1;
+                        break;
+                    }
+                    const int t0 = tok_begin + i * C::T;
+                    const int n = min(C::T, tok_end - t0);
+                    const int nb = (n + bs - 1) / bs;  // whole blocks (the last may run past the context)
+                    const uint32_t sK = ring + st * C::STAGE;
+                    mbar_arrive_expect_tx(full_bar(st), 2u * nb * block_bytes);
+                    for (int j = 0; j < nb; ++j) {
+                        int phys = staged ? bt_s[t0 / bs + j - blk0] : btg[t0 / bs + j];
+                        if ((unsigned)phys >= (unsigned)p.num_phys_blocks) {
+                            raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
+                            phys = 0;
+                        }
+                        tma_load_3d(sK + j * block_bytes, &kmap, 0, kvh, phys * bs, full_bar(st), pol);
+                        tma_load_3d(sK + C::T * C::ROW + j * block_bytes, &vmap, 0, kvh, phys * bs, full_bar(st), pol);
+                    }
+                }
+            }
+            return;
+        }
+    }
     if (warp == DA_NW) {
         // ------------------------------------------------------------ producer warp
         // The split's slice of the block table is staged in shared memory once, so no tile
@@ -544,12 +597,73 @@ bool set_smem_attr_once(const void* func, int bytes, int slot);
 
 int num_sms_current_device();
 
+typedef CUresult (*DaEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Tensor map over a K or V cache [P, block_size, H_kv, D] as [P * block_size][H_kv][D] with a
+// box of D x 1 x block_size (one head of one block); cached per (device, pointer, shape).
+template <typename KV>
+static bool kv_map(CUtensorMap* map, const void* cache, long long tokens, int H_kv, int D, int block_size) {
+    struct Entry { int dev; const void* base; long long tokens; int H, D, bs; CUtensorMap map; };
+    constexpr int kEntries = 64;
+    static Entry cache_[kEntries];
+    static int fill = 0, next = 0;
+    static std::mutex mu;
+    static DaEncodeFn enc = nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < fill; ++i) {
+        const Entry& e = cache_[i];
+        if (e.dev == dev && e.base == cache && e.tokens == tokens && e.H == H_kv && e.D == D && e.bs == block_size) {
+            *map = e.map;
+            return true;
+        }
+    }
+    if (!enc) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return false;
+        enc = reinterpret_cast<DaEncodeFn>(ptr);
+    }
+    const cuuint64_t es = sizeof(KV);
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H_kv, (cuuint64_t)tokens};
+    cuuint64_t strides[2] = {(cuuint64_t)D * es, (cuuint64_t)H_kv * D * es};
+    cuuint32_t box[3] = {(cuuint32_t)D, 1, (cuuint32_t)block_size};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(map, sizeof(KV) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+            const_cast<void*>(cache), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return false;
+    Entry& e = cache_[next];
+    e = Entry{dev, cache, tokens, H_kv, D, block_size, *map};
+    next = (next + 1) % kEntries;
+    if (fill < kEntries) ++fill;
+    return true;
+}
+
 template <int G, int D, typename KV>
 static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int B, cudaStream_t st) {
     using C = DACfg<G, D, KV>;
-    if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV>, C::SMEM, 0)) return cudaErrorInvalidValue;
     dim3 grid(prm.H_kv, prm.num_splits, B);
-    return launch_kernel(decode_attn_kernel<G, D, KV>, grid, dim3(DA_NT), (size_t)C::SMEM, st, prm);
+    CUtensorMap km, vm;
+    static const bool tma_off = getenv("B2_ATTN_TMA") && strcmp(getenv("B2_ATTN_TMA"), "0") == 0;
+    const bool tma = !tma_off && prm.num_phys_blocks > 0 && prm.block_size <= 256 && C::T % prm.block_size == 0 &&
+                     kv_map<KV>(&km, prm.k_cache, (long long)prm.num_phys_blocks * prm.block_size, prm.H_kv, D,
+                                prm.block_size) &&
+                     kv_map<KV>(&vm, prm.v_cache, (long long)prm.num_phys_blocks * prm.block_size, prm.H_kv, D,
+                                prm.block_size);
+    if (tma) {
+        if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV, true>, C::SMEM, 0)) return cudaErrorInvalidValue;
+        return launch_kernel(decode_attn_kernel<G, D, KV, true>, grid, dim3(DA_NT), (size_t)C::SMEM, st, km, vm, prm);
+    }
+    memset(&km, 0, sizeof(km));
+    if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV, false>, C::SMEM, 0)) return cudaErrorInvalidValue;
+    return launch_kernel(decode_attn_kernel<G, D, KV, false>, grid, dim3(DA_NT), (size_t)C::SMEM, st, km, km, prm);
 }
 
 template <int D, typename KV>
