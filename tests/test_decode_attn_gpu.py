@@ -173,6 +173,20 @@ def test_block_size_not_16(b2, oracle, cuda):
         np.testing.assert_allclose(got, want, **F32_TOL, err_msg=f"block_size={bs}")
 
 
+def test_block_size_not_16_bf16(b2, oracle, cuda):
+    """bf16 caches at block sizes other than 16: those whose blocks divide the tiles (1, 8,
+    32) take the TMA producer, 48 the cp.async gather; G 4, head_dim 128 and 64."""
+    import torch
+
+    rng = np.random.default_rng(13)
+    for d in (128, 64):
+        for bs in (1, 8, 32, 48):
+            q, kc, vc, bt, lens = random_paged(rng, 3, 16, 4, d, [5, 77, 1000], block_size=bs, dtype="bf16")
+            want = oracle.decode_attn(q, kc, vc, bt, lens)
+            got = run_b2(b2, torch, cuda, q, kc, vc, bt, lens)
+            np.testing.assert_allclose(got, want, **BF16_TOL, err_msg=f"d={d} block_size={bs}")
+
+
 def test_config3_scaled_ragged(b2, oracle, cuda):
     """BASELINE config 3 shape (B32, H32/8, d128) at lengths the oracle finishes quickly."""
     import torch
