@@ -22,6 +22,7 @@ same workload, on rank 0 only.
 from __future__ import annotations
 
 import argparse
+import datetime
 import importlib
 import json
 import os
@@ -39,6 +40,7 @@ B, H_Q, H_KV, D, BS = 32, 32, 8, 128, 16
 CTX_LO, CTX_HI = 512, 8192
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+PG_TIMEOUT_S = 300  # process-group timeout of multi-GPU runs
 
 
 def measured_peaks():
@@ -68,6 +70,27 @@ def workload_meta():
         bt[b, : nb[b]] = perm[off: off + nb[b]]
         off += int(nb[b])
     return lens, bt, P
+
+
+def head_shard(rank, world, h_kv=H_KV, h_q=H_Q):
+    """The heads rank `rank` of `world` holds in the sharded config-3 run: KV heads
+    [h0, h0 + hkv) and, with them, the query heads [hq0, hq0 + hq) that read them
+    (query head h reads KV head h // (h_q // h_kv), as in the reference's GQA mapping)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of {world}")
+    if h_kv % world:
+        raise ValueError(f"{h_kv} KV heads do not shard over {world} ranks")
+    hkv, hq = h_kv // world, h_q // world
+    return rank * hkv, hkv, rank * hq, hq
+
+
+def max_over_ranks(dist, value, device):
+    """The maximum of a per-rank float over all ranks (the slowest rank's time)."""
+    import torch
+
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def attn_alg_bytes(lens, h_kv, h_q, d, kv_bytes, nbps):
@@ -155,9 +178,7 @@ def time_steps(torch, fn, steps, warmup, dist=None):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     if dist is not None:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = max_over_ranks(dist, ms, "cuda")
         dist.barrier()
     return ms
 
@@ -261,23 +282,25 @@ def run_gpu(args):
     if world > 1:
         import torch.distributed as tdist
 
-        tdist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # a rank that dies or never joins ends the others' next collective with an error
+        # after PG_TIMEOUT_S instead of holding every GPU of the run
+        tdist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                 timeout=datetime.timedelta(seconds=PG_TIMEOUT_S))
         dist = tdist
-    if H_KV % world:
-        raise SystemExit(f"{H_KV} KV heads do not shard over {world} ranks")
+    try:
+        h0, hkv, hq0, hq = head_shard(rank, world)
+    except ValueError as e:
+        raise SystemExit(str(e))
     b2.load_library()
     dev = torch.device("cuda", local)
     hbm_peak, bf16_peak, peak_kind = measured_peaks()
 
     lens, bt, P = workload_meta()
     nbps = bt.shape[1]
-    hkv = H_KV // world
-    hq = H_Q // world
-    h0 = rank * hkv
     kc, vc = make_kv_shard(torch, P, h0, h0 + hkv, torch.float32, dev)
     gq = torch.Generator(device=dev).manual_seed(SEED + 1)
     q_full = torch.randn(B, H_Q, D, generator=gq, device=dev)
-    q = q_full[:, rank * hq:(rank + 1) * hq].contiguous()
+    q = q_full[:, hq0:hq0 + hq].contiguous()
     O = torch.empty_like(q)
     btd = torch.from_numpy(bt).to(dev)
     lensd = torch.from_numpy(lens).to(dev)
@@ -520,9 +543,7 @@ def tp_config5(torch, b2, np, dist, rank, world, hbm_peak, steps=64, ctx=4096, B
     eng.run_steps(steps, stream=st)
     e1.record(st)
     torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
     assert b2.device_error() == 0
     breakdown = parse_profile(eng.profile_step())  # every rank takes part (collectives inside)
     d, L = cfg["d_model"], cfg["n_layers"]
