@@ -334,7 +334,8 @@ ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_nccl_unique_id", "b2_engine_cre
                   "b2_engine_fill_kv_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
                   "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps",
                   "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions",
-                  "b2_engine_profile_step", "b2_engine_prefill"]
+                  "b2_engine_profile_step", "b2_engine_prefill", "b2_tp_exchange_bytes",
+                  "b2_tp_quantize_absent_peer"]
 
 
 def _engine_lib():
@@ -361,9 +362,12 @@ def _engine_lib():
     lib.b2_engine_keep_logits.argtypes = [vp, i, ctypes.POINTER(vp)]
     lib.b2_engine_read_logits.argtypes = [vp, vp]
     lib.b2_engine_positions.argtypes = [vp, vp]
+    lib.b2_tp_exchange_bytes.argtypes = [i]
+    lib.b2_tp_quantize_absent_peer.argtypes = [i, i, vp, vp, vp, vp, vp, vp]
     for n in ENGINE_SYMBOLS:
         if n != "b2_engine_destroy":
             getattr(lib, n).restype = i
+    lib.b2_tp_exchange_bytes.restype = ctypes.c_size_t
     lib._engine_ready = True
     return lib
 
@@ -497,3 +501,20 @@ def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     _check(_engine_lib().b2_nccl_unique_id(buf, 128), "b2_nccl_unique_id")
     return buf.raw
+
+
+def tp_quantize_absent_peer(x, stream=None):
+    """Failure path of the tensor-parallel scale exchange (``b2_tp_quantize_absent_peer``):
+    quantises x [rows, cols] as rank 0 of a 2-rank group whose other rank never arrives.
+    Every row's bounded wait gives up and sets B2_DEVERR_TIMEOUT; returns (q_packed, scales)."""
+    import torch
+
+    lib = _engine_lib()
+    rows, cols = x.shape
+    nbytes = int(lib.b2_tp_exchange_bytes(rows))
+    xchg = torch.zeros(2, (nbytes + 255) // 256 * 256, dtype=torch.uint8, device=x.device)
+    q = torch.empty(rows, cols // 4, dtype=torch.int32, device=x.device)
+    s = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _check(lib.b2_tp_quantize_absent_peer(rows, cols, _ptr(x), _ptr(q), _ptr(s), xchg[0].data_ptr(),
+                                          xchg[1].data_ptr(), _stream(stream)), "b2_tp_quantize_absent_peer")
+    return q, s

@@ -78,6 +78,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// After a timed-out wait a kernel drains before it exits: every copy and MMA it issued
+// must have landed before its shared memory and tensor memory are released. These waits
+// are bounded too (B2_DRAIN_NS each) and report nothing more: the timeout is already in
+// the device error word.
+#define B2_DRAIN_NS 50000000ull  // 50 ms
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() - t0 > B2_DRAIN_NS) return false;
+    return true;
+}
+
 // ---------------------------------------------------------------- bulk copies
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (bytes % 16 == 0,
 // both addresses 16-byte aligned).

@@ -447,6 +447,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                 const uint64_t pol = policy_evict_first();
                 const int bs = p.block_size;
                 const uint32_t block_bytes = (uint32_t)(bs * C::ROW);
+                int issued = 0;  // tiles whose copies were all requested
                 for (int i = 0; i < ntiles; ++i) {
                     const int st = i % C::STAGES;
                     if (i >= C::STAGES &&
@@ -468,7 +469,12 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                         tma_load_3d(sK + j * block_bytes, &kmap, 0, kvh, phys * bs, full_bar(st), pol);
                         tma_load_3d(sK + C::T * C::ROW + j * block_bytes, &vmap, 0, kvh, phys * bs, full_bar(st), pol);
                     }
+                    issued = i + 1;
                 }
+                // drain: the last fill of every stage this thread requested has landed before
+                // the CTA can exit, also when a consumer gave up waiting on one
+                for (int j = max(0, issued - C::STAGES); j < issued; ++j)
+                    mbar_wait_drain(full_bar(j % C::STAGES), (j / C::STAGES) & 1);
             }
             return;
         }

@@ -186,8 +186,8 @@ struct GemmCfg {
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int STAGES = std::min(8, (196 * 1024) / STAGE);
     static constexpr int OFF_BAR = STAGES * STAGE;
-    // full[S], empty[S], acc_full[2], acc_empty[2]
-    static constexpr int NBAR = 2 * STAGES + 4;
+    // full[S], empty[S], acc_full[2], acc_empty[2], drain
+    static constexpr int NBAR = 2 * STAGES + 5;
     static constexpr int OFF_COL = OFF_BAR + NBAR * 8 + 16;      // f32 [2][BN]: scale_B, bias of the tile
     static constexpr int SMEM = OFF_COL + 2 * BN * 4 + 1024;     // + 1 KB for alignment
     static constexpr uint32_t ACC_COLS = BN < 32 ? 32 : BN;      // one accumulator
@@ -303,6 +303,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * C::STAGES + 4);  // the MMA issuer's drain after an abort
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_BAR + C::NBAR * 8);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -325,6 +326,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             mbar_init(accf_bar(a), 1);   // tcgen05.commit of the tile's last MMA
             mbar_init(acce_bar(a), 4);   // one arrival per epilogue warp
         }
+        mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -386,6 +388,11 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     tma_load_2d(b_s, &mapB, kb * GM_BK, nt * BN, full_bar(s), pol);
                 }
             }
+            // drain: the last fill of every stage this thread requested has landed before the
+            // CTA can exit, also when a consumer gave up waiting (a prefetched fill whose A
+            // tile was never requested cannot complete; its bounded wait covers the B tile)
+            for (int j = max(0, it - C::STAGES); j < max(it, npre); ++j)
+                mbar_wait_drain(full_bar(j % C::STAGES), (j / C::STAGES) & 1);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -419,6 +426,10 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     mma_commit(empty_bar(s));  // ring slot free once these MMAs have read it
                 }
                 mma_commit(accf_bar(a));  // accumulator a complete
+            }
+            if (*abort_flag) {  // drain: every MMA issued has finished before TMEM is freed
+                mma_commit(drain_bar);
+                mbar_wait_drain(drain_bar, 0);
             }
         }
         __syncwarp();
@@ -604,7 +615,7 @@ constexpr int P2_STAGE = 2 * P2_ROWS * GM_BK;      // 32 KB
 constexpr int P2_STAGES = 5;
 constexpr int P2_BN = 256;                         // accumulator columns per CTA
 constexpr int P2_OFF_BAR = P2_STAGES * P2_STAGE;
-constexpr int P2_NBAR = 2 * P2_STAGES + 4;
+constexpr int P2_NBAR = 2 * P2_STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], drain
 constexpr int P2_OFF_COL = P2_OFF_BAR + P2_NBAR * 8 + 16;
 // epilogue staging: per epilogue warp 2 buffers of 32 rows x 32 fp32 (128-byte swizzled)
 constexpr int P2_OFF_EPI = (P2_OFF_COL + 2 * P2_BN * 4 + 1023) & ~1023;
@@ -625,6 +636,7 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
     auto empty_bar = [&](int s) { return bar0 + 8u * (P2_STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * P2_STAGES + a); };
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * P2_STAGES + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * P2_STAGES + 4);  // the MMA issuer's drain after an abort
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + P2_OFF_BAR + P2_NBAR * 8);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -647,6 +659,7 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
             mbar_init(accf_bar(a), 1);
             mbar_init(acce_bar(a), 8);  // 4 epilogue warps x 2 CTAs
         }
+        mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -684,6 +697,13 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
                     tma_load_2d_pair(b_s, &mapB, kb * GM_BK, nt * P2_BN + (int)rank * P2_ROWS, lead_full, pol);
                 }
             }
+            if (rank == 0) {
+                // drain: the even CTA's full barriers count both CTAs' bytes, so its last
+                // fill of every stage landing covers the pair (the closing cluster barrier
+                // keeps the odd CTA resident until then)
+                for (int j = max(0, it - P2_STAGES); j < it; ++j)
+                    mbar_wait_drain(full_bar(j % P2_STAGES), (j / P2_STAGES) & 1);
+            }
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -713,6 +733,10 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
                 }
                 mma_commit_pair(mapa_shared(accf_bar(a), 0));
                 mma_commit_pair(mapa_shared(accf_bar(a), 1));
+            }
+            if (*abort_flag) {  // drain: every MMA issued has finished before TMEM is freed
+                mma_commit_pair(mapa_shared(drain_bar, 0));
+                mbar_wait_drain(drain_bar, 0);
             }
         }
         __syncwarp();

@@ -202,3 +202,31 @@ int launch_tp_reduce(int B, int d, const float* sA, const float* sB, const float
 }
 
 }  // namespace b2
+
+// ------------------------------------------------------------------ failure-path diagnostic
+extern "C" size_t b2_tp_exchange_bytes(int rows) {
+    return rows > 0 ? b2::TpLayout::make(rows).bytes : 0;
+}
+
+extern "C" int b2_tp_quantize_absent_peer(int rows, int cols, const float* x, int32_t* q_packed, float* scales,
+                                          void* xchg_self, void* xchg_absent, b2_stream_t stream) {
+    if (rows <= 0 || rows > b2::TP_MAX_CTAS || cols <= 0 || (cols & 3) || !x || !q_packed || !scales ||
+        !xchg_self || !xchg_absent)
+        return B2_ERR_INVALID;
+    if (((uintptr_t)x | (uintptr_t)xchg_self | (uintptr_t)xchg_absent) & 15) return B2_ERR_INVALID;
+    b2::TpPeers P;
+    for (int r = 0; r < b2::TP_MAX_RANKS; ++r) {
+        P.x[r] = nullptr;
+        P.acc[r] = nullptr;
+        P.xchg[r] = nullptr;
+    }
+    P.xchg[0] = static_cast<unsigned char*>(xchg_self);
+    P.xchg[1] = static_cast<unsigned char*>(xchg_absent);
+    P.L = b2::TpLayout::make(rows);
+    P.rank = 0;
+    P.world = 2;
+    P.err = b2::device_error_ptr();
+    if (!P.err) return B2_ERR_CUDA;
+    return b2::launch_tp_quantize(rows, cols, x, q_packed, scales, P, static_cast<cudaStream_t>(stream));
+}
+

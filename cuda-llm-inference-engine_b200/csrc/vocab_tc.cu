@@ -31,7 +31,7 @@ constexpr int VT_A = VT_BM * VT_BKB, VT_B = VT_BN * VT_BKB;
 constexpr int VT_STAGE = 2 * VT_A + 2 * VT_B;  // A_hi, A_lo, W_hi, W_lo
 constexpr int VT_STAGES = 3;
 constexpr int VT_OFF_BAR = VT_STAGES * VT_STAGE;
-constexpr int VT_NBAR = 2 * VT_STAGES + 4;
+constexpr int VT_NBAR = 2 * VT_STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], drain
 constexpr int VT_SMEM = VT_OFF_BAR + VT_NBAR * 8 + 16 + 1024;
 constexpr uint32_t VT_ACC_COLS = VT_BN, VT_TMEM_COLS = 2 * VT_BN;
 
@@ -78,6 +78,7 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
     auto empty_bar = [&](int s) { return bar0 + 8u * (VT_STAGES + s); };
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * VT_STAGES + a); };
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * VT_STAGES + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * VT_STAGES + 4);  // the MMA issuer's drain after an abort
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + VT_OFF_BAR + VT_NBAR * 8);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -98,6 +99,7 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
             mbar_init(accf_bar(a), 1);
             mbar_init(acce_bar(a), 4);
         }
+        mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -150,6 +152,12 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
                     tma_load_2d(a_s + VT_A, &mAl, kb * 64, mt * VT_BM, full_bar(s), pol_a);
                 }
             }
+            // drain: the last fill of every stage this thread requested has landed before the
+            // CTA can exit, also when a consumer gave up waiting (a prefetched fill whose
+            // activation tiles were never requested cannot complete; its bounded wait covers
+            // the embedding tiles in flight)
+            for (int j = max(0, it - VT_STAGES); j < max(it, npre); ++j)
+                mbar_wait_drain(full_bar(j % VT_STAGES), (j / VT_STAGES) & 1);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -181,6 +189,10 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
                     mma_commit(empty_bar(s));
                 }
                 mma_commit(accf_bar(a));
+            }
+            if (*abort_flag) {  // drain: every MMA issued has finished before TMEM is freed
+                mma_commit(drain_bar);
+                mbar_wait_drain(drain_bar, 0);
             }
         }
         __syncwarp();

@@ -112,6 +112,20 @@ int b2_engine_keep_logits(b2_engine* e, int enable, const float** logits);
 /* Copies the last step's logits [batch, vocab] to host memory (needs keep_logits). Synchronous. */
 int b2_engine_read_logits(const b2_engine* e, float* out_host);
 
+/* Failure path of the tensor-parallel scale exchange, for diagnostics and tests (no
+ * counterpart in the reference, which has no multi-GPU path). Runs the row-parallel
+ * quantiser that the out-projection and FC2 use under tensor parallelism (one CTA per row:
+ * row maximum published to every rank, then a bounded wait for every rank's) as rank 0 of a
+ * 2-rank group whose rank 1 never arrives. xchg_self and xchg_absent are zeroed device
+ * regions of b2_tp_exchange_bytes(rows) bytes; the second stands in for the absent rank's.
+ * Each row's wait gives up after its bound (2 s), sets B2_DEVERR_TIMEOUT in the device error
+ * word and the kernel finishes with this rank's own row maxima, so the context stays usable.
+ * x [rows, cols] fp32 (cols % 4 == 0, rows <= 256); q_packed [rows, cols/4]; scales [rows].
+ * Asynchronous on `stream`. */
+size_t b2_tp_exchange_bytes(int rows);
+int b2_tp_quantize_absent_peer(int rows, int cols, const float* x, int32_t* q_packed, float* scales,
+                               void* xchg_self, void* xchg_absent, b2_stream_t stream);
+
 /* Synthetic context: fills the whole KV pool with seeded N(0,1) values and moves every
  * sequence to position ctx_len (< max_seq_len), as if ctx_len tokens had been decoded. For
  * benchmarks of long contexts without a prefill. Synchronous. */
