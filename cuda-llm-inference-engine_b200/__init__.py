@@ -27,7 +27,7 @@ import os
 _PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG_DIR, "libb2decode.so")
 
-B2_OK, B2_ERR_INVALID, B2_ERR_UNSUPPORTED, B2_ERR_WORKSPACE, B2_ERR_CUDA = 0, 1, 2, 3, 4
+B2_OK, B2_ERR_INVALID, B2_ERR_UNSUPPORTED, B2_ERR_WORKSPACE, B2_ERR_CUDA, B2_ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
 B2_DEVERR_TIMEOUT, B2_DEVERR_CTX_RANGE, B2_DEVERR_BLOCK_RANGE = 1, 2, 4
 B2_KV_F32, B2_KV_BF16 = 0, 1
 EPI_PLAIN, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL = 0, 1, 2, 3

@@ -148,6 +148,7 @@ const char* b2_status_string(int status) {
         case B2_ERR_UNSUPPORTED: return "unsupported shape";
         case B2_ERR_WORKSPACE: return "workspace missing or too small";
         case B2_ERR_CUDA: return "CUDA runtime error";
+        case B2_ERR_TIMEOUT: return "peer timeout";
         default: return "unknown status";
     }
 }

@@ -6,6 +6,7 @@
 #include "b2engine.h"
 #include <cuda_bf16.h>
 #include <nccl.h>
+#include "nccl_bounded.h"
 #include <dlfcn.h>
 #include <algorithm>
 #include <cstdio>
@@ -34,11 +35,13 @@ size_t gemm_workspace_size(int M, int N, int K);
 // forces a second NCCL version into a process.
 struct NcclApi {
     ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
-    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*GetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     bool ok = false;
 };
 
@@ -50,11 +53,15 @@ const NcclApi& nccl() {
         if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (!h) return;
         api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
-        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
         api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
         api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
-        api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy && api.AllGather;
+        api.CommInitRankConfig =
+            reinterpret_cast<decltype(api.CommInitRankConfig)>(dlsym(h, "ncclCommInitRankConfig"));
+        api.GetAsyncError = reinterpret_cast<decltype(api.GetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+        api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
+        api.ok = api.GetUniqueId && api.AllReduce && api.CommDestroy && api.AllGather &&
+                 api.CommInitRankConfig && api.GetAsyncError && api.CommAbort;
     });
     return api;
 }
@@ -424,7 +431,8 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
     const int Hl = e->Hl, dl = e->dl, ffl = e->ffl;
     // all-reduces of the tensor-parallel step (NCCL on the step's stream; captured in the graph)
     auto allreduce = [&](void* buf, size_t n, ncclDataType_t t, ncclRedOp_t op) {
-        return nccl().AllReduce(buf, buf, n, t, op, e->comm, st) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
+        return nccl_call_bounded(nccl(), e->comm, [&] { return nccl().AllReduce(buf, buf, n, t, op, e->comm, st); },
+                                 nccl_timeout_s());
     };
     // row-parallel linear: global-scale quantisation of this rank's activation columns,
     // local int32 GEMM over them, int32 all-reduce (exact), then the dequant epilogue
@@ -553,7 +561,8 @@ int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
 #define B2_TRY(x) do { if ((r = (x)) != B2_OK) return r; } while (0)
     B2_TRY(enqueue_layers(e, R, st, prof));
     auto allreduce = [&](void* buf, size_t n, ncclDataType_t t, ncclRedOp_t op) {
-        return nccl().AllReduce(buf, buf, n, t, op, e->comm, st) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
+        return nccl_call_bounded(nccl(), e->comm, [&] { return nccl().AllReduce(buf, buf, n, t, op, e->comm, st); },
+                                 nccl_timeout_s());
     };
     M("ln_final");
     B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
@@ -602,7 +611,9 @@ int setup_peers(b2_engine* e, bool local_ok) {
     std::vector<Blob> all(world);
     int agreed = 0;
     bool nccl_ok = cudaMemcpy(dbuf, &mine, sizeof(Blob), cudaMemcpyHostToDevice) == cudaSuccess &&
-                   nccl().AllGather(dbuf, dbuf + sizeof(Blob), sizeof(Blob), ncclUint8, e->comm, 0) == ncclSuccess &&
+                   nccl_call_bounded(nccl(), e->comm, [&] {
+                       return nccl().AllGather(dbuf, dbuf + sizeof(Blob), sizeof(Blob), ncclUint8, e->comm, 0);
+                   }, nccl_timeout_s()) == B2_OK &&
                    cudaMemcpy(all.data(), dbuf + sizeof(Blob), world * sizeof(Blob), cudaMemcpyDeviceToHost) ==
                        cudaSuccess;
     TpPeers P{};
@@ -628,7 +639,9 @@ int setup_peers(b2_engine* e, bool local_ok) {
     }
     int* flag = reinterpret_cast<int*>(dbuf + (size_t)(world + 1) * sizeof(Blob));
     nccl_ok = nccl_ok && cudaMemcpy(flag, &opened, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
-              nccl().AllReduce(flag, flag, 1, ncclInt32, ncclMin, e->comm, 0) == ncclSuccess &&
+              nccl_call_bounded(nccl(), e->comm, [&] {
+                  return nccl().AllReduce(flag, flag, 1, ncclInt32, ncclMin, e->comm, 0);
+              }, nccl_timeout_s()) == B2_OK &&
               cudaMemcpy(&agreed, flag, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
     cudaFree(dbuf);
     if (!nccl_ok) return B2_ERR_CUDA;
@@ -714,7 +727,8 @@ int create_random_impl(const b2_gpt2_config* cfg, int max_batch, int kv_dtype, u
     if (st == B2_OK && world > 1) {
         ncclUniqueId id;
         memcpy(&id, nccl_id, sizeof(id));
-        if (!nccl().ok || nccl().CommInitRank(&e->comm, world, id, rank) != ncclSuccess) st = B2_ERR_CUDA;
+        // non-blocking creation with a bound: a rank that never joins is a timeout, not a hang
+        st = nccl().ok ? comm_init_bounded(nccl(), &e->comm, world, id, rank, nccl_timeout_s()) : B2_ERR_CUDA;
     }
     if (st == B2_OK) st = alloc_weights(e);
     if (st == B2_OK) st = alloc_runtime(e);

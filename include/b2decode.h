@@ -44,7 +44,8 @@ enum {
     B2_ERR_INVALID = 1,      /* bad argument: null pointer, negative size, misaligned buffer */
     B2_ERR_UNSUPPORTED = 2,  /* shape the kernels do not implement (e.g. GQA group 3) */
     B2_ERR_WORKSPACE = 3,    /* workspace missing or smaller than the size query returned */
-    B2_ERR_CUDA = 4          /* a CUDA runtime call failed (launch error, bad device) */
+    B2_ERR_CUDA = 4,         /* a CUDA runtime call failed (launch error, bad device) */
+    B2_ERR_TIMEOUT = 5       /* a tensor-parallel peer did not answer within its bound */
 };
 
 /* Device error bits (b2_get_device_error). */
