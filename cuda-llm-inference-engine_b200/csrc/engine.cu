@@ -42,6 +42,7 @@ struct NcclApi {
     ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
     ncclResult_t (*GetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
     bool ok = false;
 };
 
@@ -60,8 +61,9 @@ const NcclApi& nccl() {
             reinterpret_cast<decltype(api.CommInitRankConfig)>(dlsym(h, "ncclCommInitRankConfig"));
         api.GetAsyncError = reinterpret_cast<decltype(api.GetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
         api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
+        api.CommFinalize = reinterpret_cast<decltype(api.CommFinalize)>(dlsym(h, "ncclCommFinalize"));
         api.ok = api.GetUniqueId && api.AllReduce && api.CommDestroy && api.AllGather &&
-                 api.CommInitRankConfig && api.GetAsyncError && api.CommAbort;
+                 api.CommInitRankConfig && api.GetAsyncError && api.CommAbort && api.CommFinalize;
     });
     return api;
 }
@@ -204,7 +206,7 @@ b2_engine::~b2_engine() {
     if (graph) cudaGraphExecDestroy(graph);
     cudaDeviceSynchronize();
     for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
-    if (comm) nccl().CommDestroy(comm);
+    if (comm) comm_destroy_bounded(nccl(), comm, nccl_timeout_s());
     for (void* p : allocs) cudaFree(p);
     cudaSetDevice(cur);
 }

@@ -73,4 +73,18 @@ int nccl_call_bounded(const Api& api, ncclComm_t comm, Call&& call, double timeo
     return r == ncclInProgress ? B2_ERR_TIMEOUT : B2_ERR_CUDA;
 }
 
+// Tears a non-blocking communicator down: ncclCommFinalize flushes its operations, the
+// state is polled until the communicator is quiescent, then ncclCommDestroy frees it; if
+// that does not happen within the bound (a peer is gone), ncclCommAbort frees it instead.
+// Returns B2_OK, or B2_ERR_TIMEOUT / B2_ERR_CUDA after an abort.
+template <class Api>
+int comm_destroy_bounded(const Api& api, ncclComm_t comm, double timeout_s) {
+    if (!comm) return B2_OK;
+    ncclResult_t r = api.CommFinalize(comm);
+    if (r == ncclSuccess || r == ncclInProgress) r = nccl_wait_ready(api, comm, timeout_s);
+    if (r == ncclSuccess) return api.CommDestroy(comm) == ncclSuccess ? B2_OK : B2_ERR_CUDA;
+    api.CommAbort(comm);
+    return r == ncclInProgress ? B2_ERR_TIMEOUT : B2_ERR_CUDA;
+}
+
 }  // namespace b2

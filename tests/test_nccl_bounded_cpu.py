@@ -1,7 +1,8 @@
 """Bounded NCCL communicator creation and enqueue (csrc/nccl_bounded.h), on the host with fake
 NCCL functions: a peer that joins late is waited for; one that never joins ends in
 B2_ERR_TIMEOUT within the bound with the communicator aborted; NCCL errors become
-B2_ERR_CUDA (aborted too); an enqueue that reports ncclInProgress is waited out or times out.
+B2_ERR_CUDA (aborted too); an enqueue that reports ncclInProgress is waited out or times out;
+teardown finalizes and destroys a quiescent communicator and aborts one whose peer is gone.
 The communicator is always requested in non-blocking mode."""
 import os
 import shutil
@@ -42,6 +43,13 @@ def test_enqueue_in_progress_is_bounded(b2, fakes_output):
     assert int(fakes_output["enqueue_in_progress"][0]) == b2.B2_OK
     assert int(fakes_output["enqueue_stuck"][0]) == b2.B2_ERR_TIMEOUT
     assert int(fakes_output["enqueue_error"][0]) == b2.B2_ERR_CUDA
+
+
+def test_teardown_is_bounded(b2, fakes_output):
+    st, destroyed, aborted = map(int, fakes_output["destroy_quiescent"])
+    assert (st, destroyed, aborted) == (b2.B2_OK, 1, 0)
+    st, destroyed, aborted = map(int, fakes_output["destroy_peer_gone"])
+    assert (st, destroyed, aborted) == (b2.B2_ERR_TIMEOUT, 0, 1)
 
 
 def test_timeout_status_string(b2):
