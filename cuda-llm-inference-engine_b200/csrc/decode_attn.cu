@@ -13,11 +13,13 @@
 // B200 design (one CTA per (split, kv_head, sequence)):
 //   - the CTA serves all G = H_q/H_kv query heads of its KV head, so every K/V byte is
 //     read from HBM once (the reference re-reads it once per query head);
-//   - warp 8 is a producer: it gathers each tile's K and V rows (tiles of ~32 KB: 32-128
-//     tokens) through the block table with coalesced 16-byte cp.async (one warp
-//     instruction per 512-byte row) into a 64 KB shared-memory ring, completion counted
-//     on a per-stage mbarrier (cp.async.mbarrier.arrive). 1-D bulk copies of single rows
-//     were measured to be request-rate bound here (fp32 and bf16 took equal time);
+//   - warp 8 is a producer: it fills a 64 KB shared-memory ring with tiles of ~32 KB (32-128
+//     tokens of K and V) found through the block table. When a tile holds whole cache blocks,
+//     its lane 0 issues one 3-D TMA load per block for K and one for V (a tensor map over the
+//     cache as [P * block_size][H_kv][D]) and the stage barrier counts the bytes; otherwise
+//     the warp gathers rows with coalesced 16-byte cp.async and counts completion with
+//     cp.async.mbarrier.arrive. 1-D bulk copies of single rows were measured to be
+//     request-rate bound here (fp32 and bf16 took equal time);
 //   - warps 0..7 consume: each owns a slice of every tile's tokens and runs its own
 //     exp2-domain online softmax with no CTA barrier inside the loop; the warps' partial
 //     (o, m, l) are merged by log-sum-exp at the end of the split;
