@@ -2,7 +2,7 @@
 # Builds the oracle libraries (test infrastructure only):
 #   oracle/liboracle.so    the C restatement (oracle.c), gcc, OpenMP;
 #   oracle/_ref/libref.so  the reference's own sources, compiled unchanged from where they
-#                          lie (REF, default /root/reference): its CPU attention harness and
+#                          lie (REF: the reference checkout's root): its CPU attention harness and
 #                          its K10-K14 CUDA kernels for sm_100a. Skipped when REF is absent
 #                          (the GPU box uses the prebuilt file).
 set -euo pipefail
