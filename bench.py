@@ -580,16 +580,86 @@ def cpu_baseline(torch, q, kc, vc, bt, lens):
                       f"{sec * 1e3:.0f} ms per pass"}
 
 
+def reference_line(args, value, ms_step, kind, cores, sample):
+    return {
+        "impl": "reference", "metric": "decode-attn HBM GB/s (GQA paged decode, BASELINE config 3, fp32 KV)",
+        "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), ragged lengths U[512,8192])",
+        "config": {"workload": "gqa_decode_attn_config3", "batch": B, "h_q": H_Q, "h_kv": H_KV, "head_dim": D,
+                   "block_size": BS, "kv_dtype": "fp32", "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference_harness(args):
+    """The reference's own CPU attention, gqa_cpu_reference (tests/test_paged_attention.cu:
+    138-179, compiled unchanged from its sources into oracle/_ref/libref.so), in its own
+    form: N query rows of one sequence against its N keys, all 32 query / 8 KV heads, d 128,
+    fp32. Each row is the work of one decode call at context N (every K/V byte of the
+    sequence read once, the same arithmetic per key), so a call counts N decode calls'
+    algorithmic bytes. Each step runs one call per host thread in parallel (the harness is
+    single-threaded; ctypes releases the GIL), N sized so the run stays within ~2 minutes."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle
+
+    threads = max(1, min(os.cpu_count() or 1, 64))
+    rng = np.random.default_rng(SEED)
+
+    def sample(n):
+        return (rng.standard_normal((1, H_Q, n, D)).astype(np.float32),
+                rng.standard_normal((1, H_KV, n, D)).astype(np.float32),
+                rng.standard_normal((1, H_KV, n, D)).astype(np.float32))
+
+    n0 = 128
+    probe = sample(n0)
+    oracle.ref_gqa_cpu(*probe)
+    t0 = time.perf_counter()
+    oracle.ref_gqa_cpu(*probe)
+    t_probe = time.perf_counter() - t0
+    # a call costs ~N^2: aim at ~100 s for the whole run (B2_REF_BUDGET_S overrides)
+    target = float(os.environ.get("B2_REF_BUDGET_S", "100")) / max(1, args.steps + args.warmup)
+    n = int(n0 * (target / max(t_probe, 1e-6)) ** 0.5) // 16 * 16
+    n = max(32, min(n, 1024))
+    sets = [sample(n) for _ in range(threads)]
+    pool = ThreadPoolExecutor(max_workers=threads)
+
+    def step():
+        list(pool.map(lambda qkv: oracle.ref_gqa_cpu(*qkv), sets))
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    sec = time.perf_counter() - t0
+    pool.shutdown()
+    row_bytes = attn_alg_bytes(np.array([n]), H_KV, H_Q, D, 4, (n + BS - 1) // BS)
+    by = threads * n * row_bytes  # per step
+    v = by * args.steps / sec / 1e9
+    smp = (f"reference gqa_cpu_reference (oracle/_ref, its own compiled code): per step {threads} calls in "
+           f"parallel, each {n} query rows x {n} keys, H 32/8, d 128, fp32; a row = one decode call at context {n}")
+    print(json.dumps(reference_line(args, v, sec / args.steps * 1e3, "reference", threads, smp)), flush=True)
+
+
 def run_reference(args):
-    """The reference's CPU implementation of the path (the oracle's restatement of its
-    CPU attention harness, tests/test_paged_attention.cu:138-179, on all host threads),
-    timed on a bounded sample of the headline workload per step. Rank 0 only."""
+    """The reference's CPU implementation of the path on all host threads, timed on a
+    bounded sample of the headline workload per step, rank 0 only: its own compiled CPU
+    attention harness when oracle/_ref was built (run_reference_harness), else the oracle's
+    restatement of that harness (tests/test_paged_attention.cu:138-179) over the workload's
+    paged sequences."""
     import numpy as np
 
     if int(os.environ.get("RANK", "0")) != 0:
         return
     from oracle import oracle
 
+    if oracle.ref_available() and os.environ.get("B2_REF_ARM") != "port":
+        return run_reference_harness(args)
     lens, bt, P = workload_meta()
     threads = oracle.max_threads()
     rng = np.random.default_rng(SEED)
@@ -624,17 +694,7 @@ def run_reference(args):
     by = attn_alg_bytes(sl, H_KV, H_Q, D, 4, sbt.shape[1])
     v = by * args.steps / sec / 1e9
     sample = f"sequences 0-{nseq - 1} of the workload per step (sum ctx {int(sl.sum())}), all heads, fp32 KV"
-    print(json.dumps({
-        "impl": "reference", "metric": "decode-attn HBM GB/s (GQA paged decode, BASELINE config 3, fp32 KV)",
-        "value": round(v, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1), ragged lengths U[512,8192])",
-        "config": {"workload": "gqa_decode_attn_config3", "batch": B, "h_q": H_Q, "h_kv": H_KV, "head_dim": D,
-                   "block_size": BS, "kv_dtype": "fp32", "parallelism": "host threads"},
-        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    print(json.dumps(reference_line(args, v, sec / args.steps * 1e3, "port", threads, sample)), flush=True)
 
 
 def run_only(args):

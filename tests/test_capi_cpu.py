@@ -86,3 +86,21 @@ def test_library_before_torch_keeps_torch_importable():
             "import torch; print('ok')" % ROOT)
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+def test_bench_reference_arm_runs_the_reference_harness():
+    """bench.py --impl reference prints its JSON line from the reference's own compiled CPU
+    attention when oracle/_ref is built (a short budget keeps this quick)."""
+    import json
+
+    from oracle import oracle
+
+    if not oracle.ref_available():
+        pytest.skip("oracle/_ref not built")
+    env = dict(os.environ, B2_REF_BUDGET_S="2", CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "1"], capture_output=True, text=True, timeout=300, env=env)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "reference" and line["e2e"]["h2d_bytes_per_step"] == 0
