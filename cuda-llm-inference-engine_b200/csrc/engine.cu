@@ -206,7 +206,8 @@ b2_engine::~b2_engine() {
     if (graph) cudaGraphExecDestroy(graph);
     cudaDeviceSynchronize();
     for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
-    if (comm) comm_destroy_bounded(nccl(), comm, nccl_timeout_s());
+    // peers tear down within moments of each other; a gone peer costs at most a minute here
+    if (comm) comm_destroy_bounded(nccl(), comm, std::min(nccl_timeout_s(), 60.0));
     for (void* p : allocs) cudaFree(p);
     cudaSetDevice(cur);
 }
