@@ -212,15 +212,18 @@ def make_decode_workspace(B, H_q, H_kv, head_dim, max_context_len, block_size=16
     return torch.zeros(n, dtype=torch.uint8, device=device or "cuda")
 
 
-def decode_attn(Q, k_cache, v_cache, block_table, context_lens, max_context_len, O=None, workspace=None,
-                block_size=None, num_phys_blocks=None, scale=0.0, stream=None):
-    """Paged decode attention through ``b2_decode_attn``.
-
-    Q [B, H_q, d] (or [B, H_q, 1, d]) fp32; k/v_cache [P, block_size, H_kv, d] fp32 or bf16;
-    block_table [B, nbps] int32; context_lens [B] int32. Returns O (same shape as Q)."""
+def _decode_shapes(Q, k_cache, v_cache, block_size=None):
+    """Validates the decode-attention operands before anything is launched and returns
+    (B, H_q, d, P, block_size, H_kv, kv_dtype). The KV cache must be fp32 or bf16, k and v
+    must agree in shape and dtype, and head_dim must equal Q's last dimension: a wrong
+    element size would make the kernels address past the caches' allocations."""
     import torch
 
     B, H_q, d = Q.shape[0], Q.shape[1], Q.shape[-1]
+    if Q.dtype != torch.float32:
+        raise B2Error(f"Q must be float32, got {Q.dtype}")
+    if k_cache.dim() != 4:
+        raise B2Error("k_cache must be [P, block_size, H_kv, head_dim]")
     P, bs, H_kv, d2 = k_cache.shape
     if d2 != d or v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
         raise B2Error("k_cache / v_cache / Q shapes disagree")
@@ -232,6 +235,18 @@ def decode_attn(Q, k_cache, v_cache, block_table, context_lens, max_context_len,
         kvd = B2_KV_BF16
     else:
         raise B2Error(f"unsupported KV dtype {k_cache.dtype}")
+    return B, H_q, d, P, bs, H_kv, kvd
+
+
+def decode_attn(Q, k_cache, v_cache, block_table, context_lens, max_context_len, O=None, workspace=None,
+                block_size=None, num_phys_blocks=None, scale=0.0, stream=None):
+    """Paged decode attention through ``b2_decode_attn``.
+
+    Q [B, H_q, d] (or [B, H_q, 1, d]) fp32; k/v_cache [P, block_size, H_kv, d] fp32 or bf16;
+    block_table [B, nbps] int32; context_lens [B] int32. Returns O (same shape as Q)."""
+    import torch
+
+    B, H_q, d, P, bs, H_kv, kvd = _decode_shapes(Q, k_cache, v_cache, block_size)
     if O is None:
         O = torch.empty_like(Q)
     if workspace is None:
@@ -253,11 +268,9 @@ def decode_attn_noalloc(Q, k_cache, v_cache, block_table, context_lens, max_cont
     uses its fixed per-GPU scratch array instead of a workspace. For callers that cannot
     allocate device memory; O must be provided. Overlapping calls on one GPU race on the
     shared scratch, so issue them on one stream (or otherwise serialise them)."""
-    import torch
-
-    B, H_q, d = Q.shape[0], Q.shape[1], Q.shape[-1]
-    P, bs, H_kv, _ = k_cache.shape
-    kvd = B2_KV_BF16 if k_cache.dtype == torch.bfloat16 else B2_KV_F32
+    B, H_q, d, P, bs, H_kv, kvd = _decode_shapes(Q, k_cache, v_cache)
+    if O is None or O.shape != Q.shape or O.dtype != Q.dtype:
+        raise B2Error("O must be provided with Q's shape and dtype")
     a = DecodeAttnArgs(B, H_q, H_kv, d, _ptr(Q), _ptr(k_cache), _ptr(v_cache), kvd, _ptr(block_table),
                        _ptr(context_lens), int(max_context_len), bs, block_table.shape[1],
                        int(P if num_phys_blocks is None else num_phys_blocks), float(scale), _ptr(O), None, 0)

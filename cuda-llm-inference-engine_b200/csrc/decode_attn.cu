@@ -697,6 +697,16 @@ static size_t partial_bytes(int B, int H_q, int D, int S) {
 }
 
 
+// Largest split count whose workspace fits the allocation-free entry point's fixed array
+// (1 when not even two splits fit: a single split needs no workspace).
+int noalloc_max_splits(int B, int H_q, int H_kv, int D) {
+    if (B <= 0 || H_q <= 0 || H_kv <= 0 || D <= 0) return 1;
+    const size_t counters = (size_t)B * H_kv * sizeof(unsigned int);
+    int s = 64;
+    while (s > 1 && partial_bytes(B, H_q, D, s) + counters > (size_t)B2_DECODE_NOALLOC_SCRATCH_BYTES) --s;
+    return s;
+}
+
 size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size,
                                   int max_splits, int kv_bytes) {
     SplitPlan sp = plan_splits(B, H_kv, D, kv_bytes, max_ctx, block_size, max_splits, num_sms_current_device());
@@ -802,9 +812,12 @@ extern "C" int b2_decode_attn_noalloc(const b2_decode_attn_args* args, b2_stream
     b2_decode_attn_args a = *args;
     a.workspace = scratch;
     a.workspace_bytes = B2_DECODE_NOALLOC_SCRATCH_BYTES;
-    // Same split plan as b2_decode_attn. A plan whose workspace exceeds the fixed array is
-    // rejected with B2_ERR_WORKSPACE by the launcher's size check. The arrival counters are
-    // cleared with a stream-ordered memset on every call, since the array keeps whatever
-    // the previous call left in it.
-    return b2::decode_attn_launch(&a, 64, false, static_cast<cudaStream_t>(stream));
+    // The split count is capped by what the fixed array holds: the largest S whose partials
+    // [B, H_q, S, d+2] plus the [B, H_kv] counters fit, at most b2_decode_attn's cap of 64.
+    // A plan with one split uses no scratch, so no shape is refused for its size; large
+    // batches simply run with fewer splits. The arrival counters are cleared with a
+    // stream-ordered memset on every call, since the array keeps whatever the previous
+    // call left in it.
+    return b2::decode_attn_launch(&a, b2::noalloc_max_splits(a.B, a.H_q, a.H_kv, a.head_dim),
+                                  false, static_cast<cudaStream_t>(stream));
 }

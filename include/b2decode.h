@@ -83,6 +83,9 @@ typedef struct {
 /* Bytes of workspace b2_decode_attn needs for these shapes. The workspace holds per-split
  * partial results and one arrival counter per (sequence, KV head). The counters must be
  * zero before the first call (cudaMemset once); every call leaves them zero again.
+ * The size is that of the split plan for an fp32 cache; a bf16 cache plans at most as many
+ * splits, so this size serves both element types. A shape that plans a single split needs
+ * no workspace at all (workspace may then be NULL).
  * Replaces the caller-side sizing `B*H_q*DA_MAX_SPLITS*(d+2)` floats
  * (reference src/gpt2_engine.cu:156, tests/test_decode_attention.cu:91). */
 size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim,
@@ -103,10 +106,16 @@ int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream);
  *   - The caller still passes Q, the caches, the block table, context_lens and O;
  *     args->workspace and args->workspace_bytes are ignored.
  *   - The split workspace is a file-scope device array of B2_DECODE_NOALLOC_SCRATCH_BYTES
- *     held by every GPU that loads the library until the process exits. Shapes whose
- *     workspace (b2_decode_attn_workspace_size) exceeds it return B2_ERR_WORKSPACE.
+ *     held by every GPU that loads the library until the process exits. The split count is
+ *     the one b2_decode_attn would plan, capped at the largest S whose partials
+ *     (B * H_q * S * (head_dim + 2) floats, rounded up to 256 bytes) plus B * H_kv 4-byte
+ *     counters fit the array. One split needs no workspace, so no shape is refused for its
+ *     size: a batch too large for the default plan runs with fewer splits (slower on long
+ *     contexts, same results within fp32 rounding).
  *   - The first call on each device looks up the array's device address; make that first
- *     call before any stream capture that should contain this entry point.
+ *     call before any stream capture that should contain this entry point. Each kernel
+ *     variant (GQA group, head_dim, KV dtype) also sets its shared-memory limit on its own
+ *     first call.
  *   - Every call uses the same array: calls that may overlap on the GPU (different streams,
  *     or different host threads on one device) race on it and must be serialised by the
  *     caller. Each call clears the array's arrival counters itself (a stream-ordered memset).

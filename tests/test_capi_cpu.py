@@ -104,3 +104,30 @@ def test_bench_reference_arm_runs_the_reference_harness():
     line = json.loads(out.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference" and line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_decode_operand_validation_before_launch(b2):
+    """The host mirror refuses caches the kernels cannot address (fp16/int8 elements, k and v
+    that disagree in shape or dtype, a head_dim other than Q's) before it loads or launches
+    anything, for both the workspace and the allocation-free entry points."""
+    import torch
+
+    q = torch.zeros(2, 4, 64)
+    kc = torch.zeros(3, 16, 2, 64)
+    bt = torch.zeros(2, 3, dtype=torch.int32)
+    lens = torch.zeros(2, dtype=torch.int32)
+    O = torch.zeros_like(q)
+    for fn in (lambda k, v: b2.decode_attn(q, k, v, bt, lens, 48),
+               lambda k, v: b2.decode_attn_noalloc(q, k, v, bt, lens, 48, O)):
+        with pytest.raises(b2.B2Error, match="KV dtype"):
+            fn(kc.half(), kc.half())
+        with pytest.raises(b2.B2Error, match="KV dtype"):
+            fn(kc.to(torch.int8), kc.to(torch.int8))
+        with pytest.raises(b2.B2Error, match="disagree"):
+            fn(kc, kc.bfloat16())
+        with pytest.raises(b2.B2Error, match="disagree"):
+            fn(kc, torch.zeros(4, 16, 2, 64))
+        with pytest.raises(b2.B2Error, match="disagree"):
+            fn(torch.zeros(3, 16, 2, 128), torch.zeros(3, 16, 2, 128))
+    with pytest.raises(b2.B2Error, match="O must"):
+        b2.decode_attn_noalloc(q, kc, kc, bt, lens, 48, None)

@@ -291,3 +291,40 @@ def test_device_bounds_checks_flag_errors(b2, cuda):
     b2.decode_attn(tq, tk, tv, tbt, tl, 40 + 16 * 8)
     assert b2.device_error() & b2.B2_DEVERR_CTX_RANGE
     assert b2.device_error() == 0  # cleared
+
+
+@pytest.mark.parametrize("kv", ["f32", "bf16"])
+def test_bench_workload_full_size_against_oracle(b2, oracle, cuda, kv):
+    """The exact inputs the bench's headline line times (config 3: seed 42, B32, H 32/8,
+    d128, Σctx 147,397, 16-token blocks behind the seeded shuffled table), every sequence
+    and head, against the oracle run on all host threads; then the same through the
+    allocation-free entry point. fp32 within rtol 1e-4 / atol 1e-5, bf16 within 2e-2."""
+    import torch
+
+    import bench
+
+    lens, bt, P = bench.workload_meta()
+    kc, vc = bench.make_kv_shard(torch, P, 0, bench.H_KV, torch.float32, cuda)
+    gq = torch.Generator(device=cuda).manual_seed(bench.SEED + 1)
+    q = torch.randn(bench.B, bench.H_Q, bench.D, generator=gq, device=cuda)
+    if kv == "bf16":
+        kc, vc = kc.to(torch.bfloat16), vc.to(torch.bfloat16)
+    btd, lensd = torch.from_numpy(bt).to(cuda), torch.from_numpy(lens).to(cuda)
+    max_ctx = int(lens.max())
+    got = b2.decode_attn(q, kc, vc, btd, lensd, max_ctx).cpu().numpy()
+    O = torch.empty_like(q)
+    b2.decode_attn_noalloc(q, kc, vc, btd, lensd, max_ctx, O)
+    got_na = O.cpu().numpy()
+    assert b2.device_error() == 0
+
+    def host(t):
+        if t.dtype == torch.bfloat16:
+            return t.view(torch.int16).cpu().numpy().view(np.uint16)
+        return t.cpu().numpy()
+
+    kh, vh = host(kc), host(vc)
+    del kc, vc
+    want = oracle.decode_attn(q.cpu().numpy(), kh, vh, bt, lens, nthreads=0)
+    tol = F32_TOL if kv == "f32" else BF16_TOL
+    np.testing.assert_allclose(got, want, **tol)
+    np.testing.assert_allclose(got_na, want, **tol)
