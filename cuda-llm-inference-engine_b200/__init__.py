@@ -46,7 +46,7 @@ _CXX = {
 # Every symbol include/*.h declares (checked by the CPU tests).
 C_ABI_SYMBOLS = [
     "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_decode_attn_noalloc", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
-    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
+    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_layernorm", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
 ]
 
 
@@ -97,6 +97,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     lib.b2_int8_gemm_ws.restype = i
     lib.b2_int8_gemm_s32.argtypes = [i, i, i, vp, vp, vp, vp]
     lib.b2_int8_gemm_s32.restype = i
+    lib.b2_layernorm.argtypes = [i, i, vp, vp, vp, ctypes.c_float, vp, vp, vp, vp]
+    lib.b2_layernorm.restype = i
     lib.b2_get_device_error.argtypes = [i]
     lib.b2_get_device_error.restype = ctypes.c_uint
     lib.b2_last_status.argtypes = []
@@ -278,6 +280,23 @@ def decode_attn_noalloc(Q, k_cache, v_cache, block_table, context_lens, max_cont
     return O
 
 
+def layernorm(x, gamma, beta, eps=1e-5, out=None, quantize=False, stream=None):
+    """LayerNorm of x [rows, cols] fp32 (b2_layernorm), in the reference kernel's summation
+    order. quantize=True also returns the per-row int8 quantisation: (out, q_packed, scales)."""
+    import torch
+
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    q = s = None
+    if quantize:
+        q = torch.empty(rows, cols // 4, dtype=torch.int32, device=x.device)
+        s = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _check(load_library().b2_layernorm(rows, cols, _ptr(x), _ptr(gamma), _ptr(beta), float(eps), _ptr(out), _ptr(q),
+                                       _ptr(s), _stream(stream)), "b2_layernorm")
+    return (out, q, s) if quantize else out
+
+
 def quantize_fp32_to_int8(x, out=None, scales=None, stream=None):
     """Returns (packed int32 [rows, cols/4], scales fp32 [rows])."""
     import torch
@@ -345,7 +364,7 @@ class GPT2Config(ctypes.Structure):
 
 ENGINE_SYMBOLS = ["b2_engine_create_random", "b2_nccl_unique_id", "b2_engine_create_random_tp",
                   "b2_engine_fill_kv_random", "b2_engine_load", "b2_engine_export", "b2_engine_destroy",
-                  "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps",
+                  "b2_engine_config", "b2_engine_start", "b2_engine_step", "b2_engine_run_steps", "b2_engine_decode_step",
                   "b2_engine_read_tokens", "b2_engine_keep_logits", "b2_engine_read_logits", "b2_engine_positions",
                   "b2_engine_profile_step", "b2_engine_prefill", "b2_tp_exchange_bytes",
                   "b2_tp_quantize_absent_peer"]
@@ -369,6 +388,7 @@ def _engine_lib():
     lib.b2_engine_start.argtypes = [vp, i, vp, vp, i, i, u64]
     lib.b2_engine_step.argtypes = [vp, vp]
     lib.b2_engine_run_steps.argtypes = [vp, i, vp]
+    lib.b2_engine_decode_step.argtypes = [vp, vp, vp, vp]
     lib.b2_engine_profile_step.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
     lib.b2_engine_prefill.argtypes = [vp, vp]
     lib.b2_engine_read_tokens.argtypes = [vp, vp, i]
@@ -460,6 +480,27 @@ class Engine:
 
     def run_steps(self, steps: int, stream=None):
         _check(self._lib.b2_engine_run_steps(self._h, steps, _stream(stream)), "b2_engine_run_steps")
+
+    def decode_step(self, tokens_in, next_out=None, stream=None):
+        """One step on caller-chosen input tokens (b2_engine_decode_step): tokens_in [batch]
+        int32 (a torch tensor on the device or on the host, or a numpy array); returns the
+        greedy next tokens (numpy int32 [batch]) unless next_out (a tensor) is given, which
+        is then filled asynchronously."""
+        import numpy as np
+
+        if isinstance(tokens_in, np.ndarray):
+            tin = np.ascontiguousarray(tokens_in, np.int32)
+            tin_p = tin.ctypes.data
+        else:
+            tin_p = _ptr(tokens_in)
+        if next_out is None:
+            out = np.zeros(self.batch, np.int32)
+            _check(self._lib.b2_engine_decode_step(self._h, tin_p, out.ctypes.data, _stream(stream)),
+                   "b2_engine_decode_step")
+            return out
+        _check(self._lib.b2_engine_decode_step(self._h, tin_p, _ptr(next_out), _stream(stream)),
+               "b2_engine_decode_step")
+        return next_out
 
     def profile_step(self) -> str:
         """One eager step with a CUDA event before every launch; returns the per-kernel-class

@@ -2,6 +2,7 @@
 // (include/b2_reference_api.h) over the sm_100a kernels.
 #include "common.cuh"
 #include "b2_reference_api.h"
+#include "engine_kernels.cuh"
 #include <mutex>
 #include <set>
 #include <utility>
@@ -126,6 +127,15 @@ int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t
                      b2_stream_t stream) {
     return gemm_launch(M, N, K, A_packed, BT_packed, nullptr, nullptr, nullptr, nullptr, C_acc, B2_EPI_PLAIN, true,
                        static_cast<cudaStream_t>(stream));
+}
+
+int b2_layernorm(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps, float* out,
+                 int32_t* q_packed, float* scales, b2_stream_t stream) {
+    if (rows < 0 || cols <= 0) return B2_ERR_INVALID;
+    if (rows == 0) return B2_OK;
+    if (!x || !gamma || !beta || (!out && !q_packed) || (q_packed && !scales)) return B2_ERR_INVALID;
+    if ((cols & 3) || cols > 8192) return B2_ERR_UNSUPPORTED;
+    return launch_ln_quant(rows, cols, x, gamma, beta, eps, q_packed, scales, out, static_cast<cudaStream_t>(stream));
 }
 
 unsigned int b2_get_device_error(int clear) {

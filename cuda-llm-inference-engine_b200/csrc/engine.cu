@@ -71,6 +71,7 @@ const NcclApi& nccl() {
 constexpr int kBlock = 16;        // KV block size (reference engine: block_size_ = 16)
 constexpr int kPrefillRows = 8192;  // prompt tokens per prefill pass (longer prompts run in chunks)
 constexpr int kPrefillItemRows = 16;  // rows of one sequence per prefill-attention CTA (PA_PQ)
+constexpr int kCandCap = 256;     // argmax candidates recorded per row and step
 constexpr float kLnEps = 1e-5f;   // reference LayerNorm eps (15_layernorm_residual.cuh default)
 
 // Device linear layer in the reference's QuantWeight format + bias.
@@ -153,6 +154,10 @@ struct b2_engine {
     int *forced = nullptr, *forced_len = nullptr, *out_tokens = nullptr;
     int forced_stride = 0;
     unsigned long long* keys = nullptr;
+    int* next_tok = nullptr;  // [max_batch] greedy token of the last step (b2_engine_decode_step)
+    float rs_delta = 0.f;     // candidate margin of the exact argmax (twice the bf16x3 error bound)
+    int* cand_cnt = nullptr;  // [max_batch] argmax candidates recorded by the vocab projection
+    void* cand = nullptr;     // [max_batch, kCandCap] (value bits, local vocab index)
     // activations
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *hbuf = nullptr, *xf = nullptr;
     float* logits = nullptr;
@@ -182,6 +187,8 @@ struct b2_engine {
     int32_t *pf_xq = nullptr, *pf_acc32 = nullptr;
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
+    // exact fp32 argmax after the tensor-core projection (B2_EXACT_ARGMAX=0: the bf16x3 argmax)
+    bool exact_argmax = !(getenv("B2_EXACT_ARGMAX") && strcmp(getenv("B2_EXACT_ARGMAX"), "0") == 0);
     // fused QKV split in the GEMM epilogue (B2_ENGINE_FUSE_QKV=0 runs GEMM + scatter kernel)
     bool fuse_qkv = !(getenv("B2_ENGINE_FUSE_QKV") && strcmp(getenv("B2_ENGINE_FUSE_QKV"), "0") == 0);
 
@@ -235,7 +242,10 @@ int alloc_runtime(b2_engine* e) {
     e->pos = e->alloc<int>(B);
     e->ctx = e->alloc<int>(B);
     e->block_table = e->alloc<int>((size_t)B * e->blocks_per_seq);
-    e->keys = e->alloc<unsigned long long>(B);
+    e->keys = e->alloc<unsigned long long>(2 * (size_t)B);  // approximate, then exact argmax keys
+    e->next_tok = e->alloc<int>(B);
+    e->cand_cnt = e->alloc<int>(B);
+    e->cand = e->alloc<int2>((size_t)B * kCandCap);
     e->x = e->alloc<float>((size_t)B * d);
     e->qkv = e->alloc<float>((size_t)B * 3 * e->dl);
     e->q = e->alloc<float>((size_t)B * d);
@@ -257,6 +267,7 @@ int alloc_runtime(b2_engine* e) {
     if (e->failed) return B2_ERR_CUDA;
     if (!e->k_pool || !e->v_pool || !e->attn_ws || !e->logits) return B2_ERR_CUDA;
     if (cudaMemset(e->attn_ws, 0, e->attn_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
+    if (cudaMemset(e->cand_cnt, 0, (size_t)B * sizeof(int)) != cudaSuccess) return B2_ERR_CUDA;
     if (cudaMemset(e->k_pool, 0, pool_bytes) != cudaSuccess || cudaMemset(e->v_pool, 0, pool_bytes) != cudaSuccess)
         return B2_ERR_CUDA;
     e->free_blocks.resize(e->num_blocks);
@@ -568,18 +579,29 @@ int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
                                  nccl_timeout_s());
     };
     M("ln_final");
-    B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, nullptr, st, e->xf_hi,
+    B2_TRY(launch_ln_quant(B, d, e->x, e->lnf_g, e->lnf_b, kLnEps, nullptr, nullptr, e->xf, st, e->xf_hi,
                            e->xf_lo));
     M("vocab_argmax");
-    B2_TRY((launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo,
-                               e->keep_logits ? e->logits : nullptr, e->keys, st, e->v0)));
+    float* logits = e->keep_logits ? e->logits : nullptr;
+    B2_TRY((launch_vocab_bf16x3(B, e->Vl, d, e->xf_hi, e->xf_lo, e->wte_hi, e->wte_lo, logits, e->keys, st, e->v0,
+                               e->rs_delta, e->exact_argmax ? e->cand_cnt : nullptr,
+                               e->exact_argmax ? e->cand : nullptr, kCandCap)));
+    // exact fp32 value of every argmax candidate (this rank's vocab rows), so the greedy token
+    // is the one the reference's fp32 projection picks
+    unsigned long long* keys_exact = e->keys;
+    if (e->exact_argmax) {
+        M("vocab_rescore");
+        keys_exact = e->keys + B;
+        B2_TRY(launch_vocab_rescore(B, e->Vl, d, e->v0, e->xf, e->wte, e->rs_delta, logits, e->keys, keys_exact,
+                                    e->cand_cnt, e->cand, kCandCap, st));
+    }
     if (tp) {
         M("allreduce_keys");
-        B2_TRY(allreduce(e->keys, B, ncclUint64, ncclMax));  // global argmax over the vocab shards
+        B2_TRY(allreduce(keys_exact, B, ncclUint64, ncclMax));  // global argmax over the vocab shards
     }
     M("advance");
-    B2_TRY(launch_advance(B, e->keys, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
-                          e->out_stride, c.max_seq_len, st));
+    B2_TRY(launch_advance(B, keys_exact, e->tokens, e->pos, e->forced, e->forced_len, e->forced_stride, e->out_tokens,
+                          e->out_stride, c.max_seq_len, st, e->next_tok));
 #undef B2_TRY
     return B2_OK;
 }
@@ -670,6 +692,24 @@ int finish_create(b2_engine* e, b2_engine** out) {
         delete e;
         return B2_ERR_CUDA;
     }
+    // margin of the exact argmax: 2 * 2^-10 * max ||h|| * max ||wte_v||, with the final
+    // LayerNorm's output bounded by ||h|| <= max|gamma| sqrt(d) + ||beta|| (its normalised row
+    // has norm sqrt(d) at most; 1.001 covers the rounding)
+    const int d = e->cfg.d_model;
+    const float wmax = row_norm_max(e->Vl, d, e->wte + (size_t)e->v0 * d);
+    std::vector<float> g(d), bt(d);
+    if (!(wmax >= 0.f) || cudaMemcpy(g.data(), e->lnf_g, d * 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(bt.data(), e->lnf_b, d * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        delete e;
+        return B2_ERR_CUDA;
+    }
+    double gmax = 0.0, bn = 0.0;
+    for (int i = 0; i < d; ++i) {
+        gmax = std::max(gmax, (double)std::fabs(g[i]));
+        bn += (double)bt[i] * bt[i];
+    }
+    const double hmax = 1.001 * gmax * std::sqrt((double)d) + std::sqrt(bn);
+    e->rs_delta = (float)(2.0 * std::ldexp(1.0, -10) * hmax * wmax);
     *out = e;
     return B2_OK;
 }
@@ -991,7 +1031,7 @@ int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
         e->pf_ctx = e->alloc<int>(cap);
         e->pf_bt = e->alloc<int>((size_t)cap * nbps);
         e->pf_items = e->alloc<int2>(cap);
-        e->pf_keys = e->alloc<unsigned long long>(cap);
+        e->pf_keys = e->alloc<unsigned long long>(2 * (size_t)cap);
         e->pf_x = e->alloc<float>((size_t)cap * d);
         e->pf_qkv = e->alloc<float>((size_t)cap * 3 * e->dl);
         e->pf_q = e->alloc<float>((size_t)cap * d);
@@ -1145,6 +1185,19 @@ int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream) {
     }
     for (int i = 0; i < steps; ++i)
         if (cudaGraphLaunch(e->graph, st) != cudaSuccess) return B2_ERR_CUDA;
+    return B2_OK;
+}
+
+int b2_engine_decode_step(b2_engine* e, const int32_t* tokens_in, int32_t* next_out, b2_stream_t stream) {
+    if (!e || e->batch <= 0 || !tokens_in) return B2_ERR_INVALID;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t n = (size_t)e->batch * sizeof(int32_t);
+    // the caller's tokens replace whatever the previous step (or the prompt) left as input
+    if (cudaMemcpyAsync(e->tokens, tokens_in, n, cudaMemcpyDefault, st) != cudaSuccess) return B2_ERR_CUDA;
+    const int r = b2_engine_run_steps(e, 1, stream);
+    if (r != B2_OK) return r;
+    if (next_out && cudaMemcpyAsync(next_out, e->next_tok, n, cudaMemcpyDefault, st) != cudaSuccess)
+        return B2_ERR_CUDA;
     return B2_OK;
 }
 

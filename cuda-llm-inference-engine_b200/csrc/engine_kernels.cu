@@ -20,9 +20,12 @@
 #include "engine_kernels.cuh"
 #include "epilogue.cuh"
 #include <algorithm>
+#include <cstring>
 #include <cuda_bf16.h>
 
 namespace b2 {
+
+bool set_smem_attr_once(const void* func, int bytes, int slot);
 
 // ------------------------------------------------------------------ embedding
 __global__ void embed_kernel(int d, const int* __restrict__ tokens, const int* __restrict__ pos,
@@ -39,24 +42,56 @@ __global__ void embed_kernel(int d, const int* __restrict__ tokens, const int* _
     for (int i = threadIdx.x; i < d; i += blockDim.x) o[i] = e[i] + w[i];
     if (threadIdx.x == 0) {
         ctx_lens[b] = p + 1;     // attention of this step covers positions [0, p]
-        argmax_keys[b] = 0ull;   // reset the greedy-sampling reduction for this step
+        argmax_keys[b] = 0ull;              // reset the greedy-sampling reductions of this step:
+        argmax_keys[gridDim.x + b] = 0ull;  // approximate keys [B], then exact keys [B]
     }
 }
 
 // ------------------------------------------------------------------ LayerNorm + int8 quantise
-// One CTA per row; the row stays in registers (cols <= LNQ_THREADS * LNQ_MAX_PER_THREAD).
+// The row statistics are summed in exactly the order of the reference's 256-thread
+// LayerNorm (kernels/layernorm/15_layernorm_residual.cu:59-103), so mean, variance and the
+// normalised row are bit-identical to it and the int8 bytes that follow match the
+// reference engine's:
+//   - "thread" t in [0, 256) accumulates columns t, t + 256, t + 512, ... in that order,
+//     starting from 0 (sum with adds, sum of squares with fused multiply-adds);
+//   - the 256 partials are combined by a halving tree: at stride s in 128, 64, ..., 1,
+//     partial[t] += partial[t + s] for t < s; the total is partial[0];
+//   - mean = sum / cols, var = sumsq / cols - mean * mean (one fused multiply-add),
+//     inv = rsqrtf(var + eps), y = fmaf(gamma * (x - mean), inv, beta).
+// Both kernels below keep that order: the CTA kernel with one thread per partial, the
+// warp kernel with each lane holding the 8 partials t = lane + 32 j.
 constexpr int LNQ_THREADS = 256;
 constexpr int LNQ_MAX_PER_THREAD = 32;
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    v = warp_sum(v);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+// Halving-tree sum of one value per thread of a 256-thread CTA (the order above): strides
+// 128, 64 and 32 through shared memory, then 16 .. 1 by shuffles within warp 0, whose lane 0
+// pairing is the same tree. Every thread gets the total.
+__device__ __forceinline__ float tree_sum256(float v, float* red) {
+    const int t = threadIdx.x;
+    red[t] = v;
     __syncthreads();
-    float t = 0.f;
+    if (t < 128) red[t] += red[t + 128];
+    __syncthreads();
+    if (t < 64) red[t] += red[t + 64];
+    __syncthreads();
+    if (t < 32) {
+        float x = red[t] + red[t + 32];
 #pragma unroll
-    for (int w = 0; w < LNQ_THREADS / 32; ++w) t += red[w];
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_down_sync(0xffffffffu, x, o);
+        if (t == 0) red[256] = x;
+    }
     __syncthreads();
-    return t;
+    const float total = red[256];
+    __syncthreads();
+    return total;
+}
+
+// LayerNorm statistics from the row sums (shared by both kernels).
+__device__ __forceinline__ void ln_stats(float sum, float sumsq, int cols, float eps, float& mean, float& inv) {
+    const float n = (float)cols;
+    mean = sum / n;
+    const float var = fmaf(-mean, mean, sumsq / n);
+    inv = rsqrtf(var + eps);
 }
 
 __global__ void __launch_bounds__(LNQ_THREADS)
@@ -64,7 +99,7 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
                 const float* __restrict__ beta, float eps, int32_t* __restrict__ q_out,
                 float* __restrict__ scale_out, float* __restrict__ y_out, __nv_bfloat16* __restrict__ y_hi,
                 __nv_bfloat16* __restrict__ y_lo) {
-    __shared__ float red[LNQ_THREADS / 32];
+    __shared__ float red[LNQ_THREADS + 1];
     griddep_wait();
     griddep_launch();
     const int row = blockIdx.x;
@@ -74,13 +109,16 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
 #pragma unroll
     for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
         const int c = threadIdx.x + k * LNQ_THREADS;
-        v[k] = c < cols ? xr[c] : 0.f;
-        s += v[k];
-        ss = fmaf(v[k], v[k], ss);
+        v[k] = 0.f;
+        if (c < cols) {
+            v[k] = xr[c];
+            s += v[k];
+            ss = fmaf(v[k], v[k], ss);
+        }
     }
-    const float mean = block_sum(s, red) / cols;
-    const float var = block_sum(ss, red) / cols - mean * mean;
-    const float inv = rsqrtf(var + eps);
+    float mean, inv;
+    const float sum = tree_sum256(s, red);
+    ln_stats(sum, tree_sum256(ss, red), cols, eps, mean, inv);
     float amax = 0.f;
 #pragma unroll
     for (int k = 0; k < LNQ_MAX_PER_THREAD; ++k) {
@@ -127,10 +165,13 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
     }
 }
 
-// One warp per row (32-thread CTA), the row in registers (cols <= 32 x 4 x NV4, 16-byte
-// aligned): the same LayerNorm and quantiser arithmetic as ln_quant_kernel with shuffle
-// reductions instead of CTA-wide ones (decode rows are short).
-template <int NV4>
+// One warp per row (32-thread CTA) for rows of at most 256 * KC columns (decode rows are
+// short), loaded as float4: lane l holds columns 4l + i + 128 h + 256 k (i < 4, h < 2,
+// k < KC), i.e. the 8 partials t = 4l + i + 128 h of the 256-partial order above, each over
+// its columns t + 256 k. The tree's stride 128 combines a lane's h = 0 and h = 1 partials;
+// strides 64 .. 4 pair lane l with lane l + 16, 8, 4, 2, 1 (shuffles, the same i); strides 2
+// and 1 combine lane 0's four i partials.
+template <int KC>
 __global__ void __launch_bounds__(32)
 ln_quant_warp_kernel(int cols, const float* __restrict__ x, const float* __restrict__ gamma,
                      const float* __restrict__ beta, float eps, int32_t* __restrict__ q_out,
@@ -139,53 +180,81 @@ ln_quant_warp_kernel(int cols, const float* __restrict__ x, const float* __restr
     griddep_wait();
     griddep_launch();
     const int row = blockIdx.x, lane = threadIdx.x;
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * cols);
-    const int c4 = cols >> 2;
-    float4 v[NV4];
-    float s = 0.f, ss = 0.f;
+    const float* xr = x + (size_t)row * cols;
+    float4 v[2][KC];
+    float ps[4] = {0.f, 0.f, 0.f, 0.f}, pq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int k = 0; k < NV4; ++k) {
-        const int i = lane + 32 * k;
-        v[k] = i < c4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-        ss = fmaf(v[k].x, v[k].x, ss);
-        ss = fmaf(v[k].y, v[k].y, ss);
-        ss = fmaf(v[k].z, v[k].z, ss);
-        ss = fmaf(v[k].w, v[k].w, ss);
-    }
-    const float mean = warp_sum(s) / cols;
-    const float var = warp_sum(ss) / cols - mean * mean;
-    const float inv = rsqrtf(var + eps);
-    float amax = 0.f;
+    for (int h = 0; h < 2; ++h) {
+        float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int k = 0; k < NV4; ++k) {
-        const int i = lane + 32 * k;
-        if (i < c4) {
-            const float4 g = reinterpret_cast<const float4*>(gamma)[i];
-            const float4 bb = reinterpret_cast<const float4*>(beta)[i];
-            v[k].x = fmaf(g.x * (v[k].x - mean), inv, bb.x);
-            v[k].y = fmaf(g.y * (v[k].y - mean), inv, bb.y);
-            v[k].z = fmaf(g.z * (v[k].z - mean), inv, bb.z);
-            v[k].w = fmaf(g.w * (v[k].w - mean), inv, bb.w);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
-        }
-    }
-    if (!q_out) {  // plain LayerNorm (final ln_f feeding the vocab projection), fp32 and/or bf16 hi/lo
+        for (int k = 0; k < KC; ++k) {
+            const int c = 4 * lane + 128 * h + 256 * k;
+            v[h][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c < cols) {
+                v[h][k] = *reinterpret_cast<const float4*>(xr + c);
+                const float t[4] = {v[h][k].x, v[h][k].y, v[h][k].z, v[h][k].w};
 #pragma unroll
-        for (int k = 0; k < NV4; ++k) {
-            const int i = lane + 32 * k;
-            if (i >= c4) continue;
-            const float t[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-            if (y_out) reinterpret_cast<float4*>(y_out + (size_t)row * cols)[i] = v[k];
-            if (y_hi) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const __nv_bfloat16 h = __float2bfloat16_rn(t[j]);
-                    y_hi[(size_t)row * cols + 4 * i + j] = h;
-                    y_lo[(size_t)row * cols + 4 * i + j] = __float2bfloat16_rn(t[j] - __bfloat162float(h));
+                for (int i = 0; i < 4; ++i) {
+                    s4[i] += t[i];
+                    q4[i] = fmaf(t[i], t[i], q4[i]);
                 }
             }
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // stride 128: partial t += partial t + 128
+            ps[i] = h == 0 ? s4[i] : ps[i] + s4[i];
+            pq[i] = h == 0 ? q4[i] : pq[i] + q4[i];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ps[i] += __shfl_down_sync(0xffffffffu, ps[i], o);
+            pq[i] += __shfl_down_sync(0xffffffffu, pq[i], o);
+        }
+    float s = (ps[0] + ps[2]) + (ps[1] + ps[3]);
+    float ss = (pq[0] + pq[2]) + (pq[1] + pq[3]);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    ss = __shfl_sync(0xffffffffu, ss, 0);
+    float mean, inv;
+    ln_stats(s, ss, cols, eps, mean, inv);
+    float amax = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < KC; ++k) {
+            const int c = 4 * lane + 128 * h + 256 * k;
+            if (c < cols) {
+                const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+                const float4 bb = *reinterpret_cast<const float4*>(beta + c);
+                float4& t = v[h][k];
+                t.x = fmaf(g.x * (t.x - mean), inv, bb.x);
+                t.y = fmaf(g.y * (t.y - mean), inv, bb.y);
+                t.z = fmaf(g.z * (t.z - mean), inv, bb.z);
+                t.w = fmaf(g.w * (t.w - mean), inv, bb.w);
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w))));
+            }
+        }
+    if (!q_out) {  // plain LayerNorm (final ln_f feeding the vocab projection), fp32 and/or bf16 hi/lo
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int k = 0; k < KC; ++k) {
+                const int c = 4 * lane + 128 * h + 256 * k;
+                if (c >= cols) continue;
+                const size_t o = (size_t)row * cols + c;
+                if (y_out) *reinterpret_cast<float4*>(y_out + o) = v[h][k];
+                if (y_hi) {
+                    const float t[4] = {v[h][k].x, v[h][k].y, v[h][k].z, v[h][k].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __nv_bfloat16 hb = __float2bfloat16_rn(t[i]);
+                        y_hi[o + i] = hb;
+                        y_lo[o + i] = __float2bfloat16_rn(t[i] - __bfloat162float(hb));
+                    }
+                }
+            }
         return;
     }
     amax = warp_max(amax);
@@ -193,21 +262,23 @@ ln_quant_warp_kernel(int cols, const float* __restrict__ x, const float* __restr
     const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     const float invs = __fdiv_rn(1.0f, scale);
     if (lane == 0) scale_out[row] = scale;
-    int32_t* qr = q_out + (size_t)row * c4;
+    int32_t* qr = q_out + (size_t)row * (cols >> 2);
 #pragma unroll
-    for (int k = 0; k < NV4; ++k) {
-        const int i = lane + 32 * k;
-        if (i >= c4) continue;
-        const float t[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-        uint32_t packed = 0;
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float qf = fminf(fmaxf(rintf(__fmul_rn(t[j], invs)), -128.f), 127.f);
-            packed |= (uint32_t)(uint8_t)(int8_t)(int)qf << (8 * j);
+        for (int k = 0; k < KC; ++k) {
+            const int c = 4 * lane + 128 * h + 256 * k;
+            if (c >= cols) continue;
+            const float t[4] = {v[h][k].x, v[h][k].y, v[h][k].z, v[h][k].w};
+            uint32_t packed = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float qf = fminf(fmaxf(rintf(__fmul_rn(t[i], invs)), -128.f), 127.f);
+                packed |= (uint32_t)(uint8_t)(int8_t)(int)qf << (8 * i);
+            }
+            qr[c >> 2] = (int32_t)packed;
+            if (y_out) *reinterpret_cast<float4*>(y_out + (size_t)row * cols + c) = v[h][k];
         }
-        qr[i] = (int32_t)packed;
-        if (y_out) reinterpret_cast<float4*>(y_out + (size_t)row * cols)[i] = v[k];
-    }
 }
 
 // ------------------------------------------------------------------ QKV split + paged KV write
@@ -302,10 +373,141 @@ vocab_argmax_kernel(int B, int V, int d, const float* __restrict__ h, const floa
     if (threadIdx.x < VP_TB && b0 + threadIdx.x < B) atomicMax(&keys[b0 + threadIdx.x], best[threadIdx.x]);
 }
 
+// Exact greedy choice after the tensor-core vocab projection. The bf16x3 logits differ from
+// the reference's fp32 ones (logits[v] = sum_k h[k] wte[v,k], sequential in k with one fused
+// multiply-add per term, src/gpt2_engine.cu:391-403) by at most
+//     err <= c * ||h||_2 * max_v ||wte_v||_2,  c = 2^-10
+// (bf16x3 drops the lo.lo term and the bits below 16 significant ones, about 3 * 2^-16 of
+// sum_k |h_k wte_vk|; fp32 accumulation in either order adds at most d * 2^-24 of it; by
+// Cauchy-Schwarz sum_k |h_k wte_vk| <= ||h|| ||wte_v||; c leaves a wide margin). So the
+// reference's argmax v* satisfies approx[v*] >= max approx - 2 err. The projection kernel
+// records, per row, every logit within delta = 2 err of the row's running maximum (a
+// superset of those within delta of the final maximum); one CTA per row keeps the recorded
+// candidates within delta of the final maximum, recomputes each exactly in the reference's
+// order and arithmetic (writing the exact value into the stored logits when they are kept),
+// and sets the row's exact argmax key to the best (lowest index on ties). The result is the
+// reference's token whenever the final hidden state h equals its own. ||h|| is bounded once
+// per model (LayerNorm output: ||h|| <= max|gamma| sqrt(d) + ||beta||), so delta is a
+// constant of the engine.
+constexpr int RS_THREADS = 256, RS_WARPS = RS_THREADS / 32, RS_MAX_CAND = 64;
+constexpr int RS_SMEM_FLOATS = 56 * 1024;  // dynamic shared memory: h row + one embedding row per staging warp
+
+// acc = sum_k h[k] * w[k], sequential in k, one fused multiply-add per term (the reference's
+// arithmetic), with h and w read from shared memory
+__device__ __forceinline__ float dot_sequential(const float* h, const float* w, int d) {
+    float acc = 0.f;
+#pragma unroll 16
+    for (int k = 0; k < d; ++k) acc = fmaf(h[k], w[k], acc);
+    return acc;
+}
+
+__global__ void __launch_bounds__(RS_THREADS)
+vocab_rescore_kernel(int V, int d, int n_offset, const float* __restrict__ h, const float* __restrict__ wte,
+                     float delta, float* __restrict__ logits, const unsigned long long* __restrict__ keys,
+                     unsigned long long* __restrict__ keys_exact, int* __restrict__ cand_cnt,
+                     const int2* __restrict__ cand_list, int cand_cap, int stage_warps) {
+    __shared__ unsigned long long best_s[RS_WARPS];
+    __shared__ int cand[RS_MAX_CAND];
+    __shared__ int n_cand;
+    extern __shared__ float rs_dyn[];
+    float* hs = rs_dyn;  // [d], then [stage_warps][d]
+    griddep_wait();
+    griddep_launch();
+    const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* hr = h + (size_t)b * d;
+    if (threadIdx.x == 0) n_cand = 0;
+#pragma unroll 4
+    for (int k = threadIdx.x; k < d / 4; k += RS_THREADS)
+        reinterpret_cast<float4*>(hs)[k] = reinterpret_cast<const float4*>(hr)[k];
+    // the row's approximate maximum, from its argmax key (order-preserving float encoding)
+    const unsigned long long key0 = keys[b];
+    uint32_t u = (uint32_t)(key0 >> 32);
+    u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+    const float thr = __uint_as_float(u) - delta;
+    const int recorded = cand_cnt[b];
+    __syncthreads();
+    // the recorded values were kept against the row's running maximum at the time; keep those
+    // within delta of the final one
+    if (recorded <= cand_cap) {
+        for (int i = threadIdx.x; i < recorded; i += RS_THREADS) {
+            const int2 c = cand_list[(size_t)b * cand_cap + i];
+            if (__int_as_float(c.x) >= thr) {
+                const int j = atomicAdd(&n_cand, 1);
+                if (j < RS_MAX_CAND) cand[j] = c.y;
+            }
+        }
+    }
+    __syncthreads();
+    const int nc = recorded <= cand_cap ? n_cand : RS_MAX_CAND + 1;
+    float* lr = logits ? logits + (size_t)b * V : nullptr;
+    unsigned long long best = 0ull;
+    if (nc <= RS_MAX_CAND) {
+        // one warp per candidate: the warp stages the candidate's embedding row in shared
+        // memory (coalesced), then one lane runs the sequential sum
+        float* wsw = rs_dyn + (size_t)(1 + warp) * d;
+        for (int j = warp; warp < stage_warps && j < nc; j += stage_warps) {
+            const int v = cand[j];
+            const float4* w4 = reinterpret_cast<const float4*>(wte + (size_t)(n_offset + v) * d);
+            float4* s4 = reinterpret_cast<float4*>(wsw);
+#pragma unroll 8
+            for (int k = lane; k < d / 4; k += 32) s4[k] = w4[k];  // all of a lane's loads in flight
+            __syncwarp();
+            if (lane == 0) {
+                const float acc = dot_sequential(hs, wsw, d);
+                if (lr) lr[v] = acc;
+                const unsigned long long kk = argmax_key(acc, n_offset + v);
+                best = kk > best ? kk : best;
+            }
+            __syncwarp();
+        }
+    } else {
+        // the candidate record overflowed (logits packed within delta of the maximum): every
+        // logit of the row is recomputed exactly (slow, and not expected in practice)
+        for (int v = threadIdx.x; v < V; v += RS_THREADS) {
+            const float* w = wte + (size_t)(n_offset + v) * d;
+            float acc = 0.f;
+            for (int k = 0; k < d; ++k) acc = fmaf(hs[k], w[k], acc);
+            if (lr) lr[v] = acc;
+            const unsigned long long kk = argmax_key(acc, n_offset + v);
+            best = kk > best ? kk : best;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if (lane == 0) best_s[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = best_s[0];
+#pragma unroll
+        for (int w = 1; w < RS_WARPS; ++w) m = best_s[w] > m ? best_s[w] : m;
+        keys_exact[b] = m;
+        cand_cnt[b] = 0;  // ready for the next step's record
+    }
+}
+
+// max over rows of ||wte_v||_2 for rows [0, V) of w [V, d] (one value, by atomicMax on the
+// non-negative float's bits)
+__global__ void row_norm_max_kernel(int V, int d, const float* __restrict__ w, unsigned int* __restrict__ out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    float m = 0.f;
+    for (int v = warp; v < V; v += nwarps) {
+        float s = 0.f;
+        for (int k = lane; k < d; k += 32) s = fmaf(w[(size_t)v * d + k], w[(size_t)v * d + k], s);
+        s = warp_sum(s);
+        m = fmaxf(m, sqrtf(s));
+    }
+    if (lane == 0) atomicMax(out, __float_as_uint(m));
+}
+
 // next token = argmax (or the forced prompt token while the prompt lasts); advance positions
 __global__ void advance_kernel(int B, const unsigned long long* __restrict__ keys, int* __restrict__ tokens,
                                int* __restrict__ pos, const int* __restrict__ forced, const int* __restrict__ forced_len,
-                               int forced_stride, int* __restrict__ out_tokens, int out_stride, int max_pos) {
+                               int forced_stride, int* __restrict__ out_tokens, int out_stride, int max_pos,
+                               int* __restrict__ next_out) {
     griddep_wait();
     griddep_launch();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -315,6 +517,7 @@ __global__ void advance_kernel(int B, const unsigned long long* __restrict__ key
     int tok = next;
     if (forced && p < forced_len[b]) tok = forced[(size_t)b * forced_stride + p];
     if (out_tokens && p < out_stride) out_tokens[(size_t)b * out_stride + p] = next;
+    if (next_out) next_out[b] = next;
     tokens[b] = tok;
     pos[b] = p;
 }
@@ -330,24 +533,27 @@ int launch_embed(int B, int d, const int* tokens, const int* pos, const float* w
 
 int launch_ln_quant(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
                     int32_t* q, float* scale, float* y, cudaStream_t st, void* y_hi, void* y_lo) {
-    if (cols > LNQ_THREADS * LNQ_MAX_PER_THREAD || (cols & 3)) return B2_ERR_UNSUPPORTED;
-    if (cols <= 4096 && ((uintptr_t)x & 15) == 0) {
-        const int c4 = cols / 4;
-        auto* hi = static_cast<__nv_bfloat16*>(y_hi);
-        auto* lo = static_cast<__nv_bfloat16*>(y_lo);
-        cudaError_t e;
-        if (c4 <= 64)
-            e = launch_kernel(ln_quant_warp_kernel<2>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
-        else if (c4 <= 256)
-            e = launch_kernel(ln_quant_warp_kernel<8>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
-        else
-            e = launch_kernel(ln_quant_warp_kernel<32>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
-        return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
-    }
-    return launch_kernel(ln_quant_kernel, dim3(rows), dim3(LNQ_THREADS), 0, st, cols, x, gamma, beta, eps, q, scale,
-                         y, static_cast<__nv_bfloat16*>(y_hi), static_cast<__nv_bfloat16*>(y_lo)) == cudaSuccess
-               ? B2_OK
-               : B2_ERR_CUDA;
+    if (rows < 0 || cols <= 0 || cols > LNQ_THREADS * LNQ_MAX_PER_THREAD || (cols & 3)) return B2_ERR_UNSUPPORTED;
+    if (rows == 0) return B2_OK;
+    auto* hi = static_cast<__nv_bfloat16*>(y_hi);
+    auto* lo = static_cast<__nv_bfloat16*>(y_lo);
+    cudaError_t e;
+    const bool a16 = (((uintptr_t)x | (uintptr_t)gamma | (uintptr_t)beta | (uintptr_t)y) & 15) == 0;
+    if (!a16)
+        e = launch_kernel(ln_quant_kernel, dim3(rows), dim3(LNQ_THREADS), 0, st, cols, x, gamma, beta, eps, q, scale,
+                          y, hi, lo);
+    else if (cols <= 256)
+        e = launch_kernel(ln_quant_warp_kernel<1>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+    else if (cols <= 512)
+        e = launch_kernel(ln_quant_warp_kernel<2>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+    else if (cols <= 768)
+        e = launch_kernel(ln_quant_warp_kernel<3>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+    else if (cols <= 1024)
+        e = launch_kernel(ln_quant_warp_kernel<4>, dim3(rows), dim3(32), 0, st, cols, x, gamma, beta, eps, q, scale, y, hi, lo);
+    else
+        e = launch_kernel(ln_quant_kernel, dim3(rows), dim3(LNQ_THREADS), 0, st, cols, x, gamma, beta, eps, q, scale,
+                          y, hi, lo);
+    return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
 int launch_qkv_scatter(int B, int d, int H, int dh, int block_size, int nbps, const float* qkv, const int* pos,
@@ -372,11 +578,43 @@ int launch_vocab_argmax(int B, int V, int d, const float* h, const float* wte, f
                : B2_ERR_CUDA;
 }
 
+int launch_vocab_rescore(int B, int V, int d, int n_offset, const float* h, const float* wte, float delta,
+                         float* logits, const unsigned long long* keys, unsigned long long* keys_exact,
+                         int* cand_cnt, const void* cand, int cand_cap, cudaStream_t st) {
+    const int stage_warps = d > 0 ? std::min(RS_WARPS, RS_SMEM_FLOATS / d - 1) : 0;
+    // float4 staging: d % 4 == 0 and 16-byte aligned rows
+    if (d <= 0 || (d & 3) || stage_warps < 1 || (((uintptr_t)h | (uintptr_t)wte) & 15)) return B2_ERR_UNSUPPORTED;
+    const int smem = (1 + stage_warps) * d * (int)sizeof(float);
+    if (!set_smem_attr_once((const void*)vocab_rescore_kernel, RS_SMEM_FLOATS * (int)sizeof(float), 0))
+        return B2_ERR_CUDA;
+    return launch_kernel(vocab_rescore_kernel, dim3(B), dim3(RS_THREADS), (size_t)smem, st, V, d, n_offset, h, wte,
+                         delta, logits, keys, keys_exact, cand_cnt, static_cast<const int2*>(cand), cand_cap,
+                         stage_warps) == cudaSuccess
+               ? B2_OK
+               : B2_ERR_CUDA;
+}
+
+float row_norm_max(int V, int d, const float* w) {
+    unsigned int* dv = nullptr;
+    unsigned int hv = 0;
+    if (cudaMalloc(&dv, sizeof(unsigned int)) != cudaSuccess) return -1.f;
+    bool ok = cudaMemset(dv, 0, sizeof(unsigned int)) == cudaSuccess;
+    if (ok) {
+        row_norm_max_kernel<<<592, 256>>>(V, d, w, dv);
+        ok = cudaGetLastError() == cudaSuccess &&
+             cudaMemcpy(&hv, dv, sizeof(unsigned int), cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    cudaFree(dv);
+    float f = -1.f;
+    if (ok) memcpy(&f, &hv, sizeof(f));
+    return f;
+}
+
 int launch_advance(int B, const unsigned long long* keys, int* tokens, int* pos, const int* forced,
                    const int* forced_len, int forced_stride, int* out_tokens, int out_stride, int max_pos,
-                   cudaStream_t st) {
+                   cudaStream_t st, int* next_out) {
     return launch_kernel(advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, B, keys, tokens, pos, forced,
-                         forced_len, forced_stride, out_tokens, out_stride, max_pos) == cudaSuccess
+                         forced_len, forced_stride, out_tokens, out_stride, max_pos, next_out) == cudaSuccess
                ? B2_OK
                : B2_ERR_CUDA;
 }

@@ -32,7 +32,9 @@ constexpr int VT_STAGE = 2 * VT_A + 2 * VT_B;  // A_hi, A_lo, W_hi, W_lo
 constexpr int VT_STAGES = 3;
 constexpr int VT_OFF_BAR = VT_STAGES * VT_STAGE;
 constexpr int VT_NBAR = 2 * VT_STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], drain
-constexpr int VT_SMEM = VT_OFF_BAR + VT_NBAR * 8 + 16 + 1024;
+constexpr int VT_OFF_XP = VT_OFF_BAR + 256;          // epilogue transpose blocks, one per epilogue warp
+constexpr int VT_XP_LD = 33;                          // padded row of a 32 x 32 fp32 block
+constexpr int VT_SMEM = VT_OFF_XP + 4 * 32 * VT_XP_LD * 4 + 1024;
 constexpr uint32_t VT_ACC_COLS = VT_BN, VT_TMEM_COLS = 2 * VT_BN;
 
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
@@ -63,6 +65,12 @@ struct VocabParams {
     float* logits;             // [M, N] or null
     unsigned long long* keys;  // [M] argmax keys (reset by the caller before the step)
     unsigned int* err;
+    // argmax candidates for the exact rescoring (null: none recorded): every logit within
+    // delta of its row's running maximum, as (value bits, local vocab index) pairs
+    float delta;
+    int* cand_cnt;             // [M] (reset by the caller before the step)
+    int2* cand;                // [M, cand_cap]
+    int cand_cap;
 };
 
 __global__ void __launch_bounds__(VT_THREADS, 1)
@@ -210,6 +218,8 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
             const bool row_ok = ok && row < p.M;
             const uint32_t tbase = tmem + a * VT_ACC_COLS + ((uint32_t)(quad * 32) << 16);
             unsigned long long best = 0ull;
+            float* xp = reinterpret_cast<float*>(smem + VT_OFF_XP) + quad * 32 * VT_XP_LD;
+            const int row0 = mt * VT_BM + quad * 32;
 #pragma unroll 1
             for (int c = 0; c < VT_BN / 16; c += 2) {
                 uint32_t r0[16], r1[16];
@@ -217,22 +227,62 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
                 tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
                 tmem_ld_wait();
                 const int n0 = nt * VT_BN + c * 16;
-                if (!row_ok) continue;
+                if (!ok) continue;
 #pragma unroll
                 for (int q = 0; q < 32; ++q) {
                     const int n = n0 + q;
                     const float v = __uint_as_float(q < 16 ? r0[q] : r1[q - 16]);
-                    if (n < p.N) {
+                    if (row_ok && n < p.N) {
                         const unsigned long long key = vt_key(v, p.n_offset + n);
                         best = key > best ? key : best;
-                        if (p.logits) p.logits[(size_t)row * p.N + n] = v;
+                    }
+                    xp[lane * VT_XP_LD + q] = v;
+                }
+                if (p.logits) {
+                    // transposed through shared memory so that each store writes 32 consecutive
+                    // logits of one row (128 bytes) instead of one logit of 32 rows
+                    __syncwarp();
+                    const int n = n0 + lane;
+#pragma unroll 4
+                    for (int r = 0; r < 32; ++r)
+                        if (row0 + r < p.M && n < p.N) p.logits[(size_t)(row0 + r) * p.N + n] = xp[r * VT_XP_LD + lane];
+                }
+                __syncwarp();
+            }
+            // the row's running maximum including this tile, then a second pass over the
+            // accumulator records every value within delta of it. The running maximum only
+            // grows, so whatever ends within delta of the row's final maximum is recorded.
+            // (tcgen05.ld is warp-wide: every lane of the warp runs the second pass' loads.)
+            float thr = INFINITY;
+            if (row_ok && best) {
+                const unsigned long long old = atomicMax(p.keys + row, best);
+                const unsigned long long m = old > best ? old : best;
+                uint32_t mu = (uint32_t)(m >> 32);
+                mu = (mu & 0x80000000u) ? (mu & 0x7fffffffu) : ~mu;
+                thr = __uint_as_float(mu) - p.delta;
+            }
+            if (p.cand && __any_sync(0xffffffffu, thr < INFINITY)) {
+#pragma unroll 1
+                for (int c = 0; c < VT_BN / 16; c += 2) {
+                    uint32_t r0[16], r1[16];
+                    tmem_ld16(tbase + (uint32_t)(c * 16), r0);
+                    tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
+                    tmem_ld_wait();
+                    const int n0 = nt * VT_BN + c * 16;
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) {
+                        const float v = __uint_as_float(q < 16 ? r0[q] : r1[q - 16]);
+                        if (n0 + q < p.N && v >= thr) {
+                            const int i = atomicAdd(p.cand_cnt + row, 1);
+                            if (i < p.cand_cap)
+                                p.cand[(size_t)row * p.cand_cap + i] = make_int2(__float_as_int(v), n0 + q);
+                        }
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acce_bar(a));
-            if (row_ok && best) atomicMax(p.keys + row, best);
         }
     }
     tc_fence_before();
@@ -286,7 +336,8 @@ int launch_split_bf16(const float* x, void* hi, void* lo, size_t n, cudaStream_t
 
 // logits/argmax of h [M, K] (as bf16 hi/lo) against W [N, K] (bf16 hi/lo). K % 8 == 0.
 int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo, const void* w_hi, const void* w_lo,
-                        float* logits, unsigned long long* keys, cudaStream_t st, int n_offset) {
+                        float* logits, unsigned long long* keys, cudaStream_t st, int n_offset, float cand_delta,
+                        int* cand_cnt, void* cand, int cand_cap) {
     if ((K & 7) || M <= 0 || N <= 0) return B2_ERR_UNSUPPORTED;
     CUtensorMap ah, al, wh, wl;
     if (!encode_bf16(&ah, h_hi, M, K, VT_BM) || !encode_bf16(&al, h_lo, M, K, VT_BM) ||
@@ -294,7 +345,8 @@ int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo,
         return B2_ERR_CUDA;
     if (!set_smem_attr_once((const void*)vocab_bf16x3_kernel, VT_SMEM, 60)) return B2_ERR_CUDA;
     const int tiles = ((M + VT_BM - 1) / VT_BM) * ((N + VT_BN - 1) / VT_BN);
-    VocabParams p{M, N, K, n_offset, logits, keys, device_error_ptr()};
+    VocabParams p{M, N, K, n_offset, logits, keys, device_error_ptr(), cand_delta, cand_cnt,
+                  static_cast<int2*>(cand), cand_cap};
     const int grid = std::min(tiles, num_sms_current_device());
     return launch_kernel(vocab_bf16x3_kernel, dim3(grid), dim3(VT_THREADS), (size_t)VT_SMEM, st, ah, al, wh, wl, p) ==
                    cudaSuccess

@@ -159,6 +159,20 @@ int b2_int8_gemm_ws(int M, int N, int K, const int32_t* A_packed, const int32_t*
 int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
                      int32_t* C_acc, b2_stream_t stream);
 
+/* ------------------------------------------------------------------ LayerNorm */
+
+/* Row-wise LayerNorm, optionally fused with the per-row int8 quantiser that follows it in
+ * every use of the decode step:
+ *   out[r, c] = gamma[c] * (x[r, c] - mean_r) * rsqrtf(var_r + eps) + beta[c]
+ * with mean_r and var_r = E[x^2] - mean^2 summed in the order of the reference's 256-thread
+ * kernel, so the result is bit-identical to run_layernorm
+ * (kernels/layernorm/15_layernorm_residual.cu:59-103, 115-125). When q_packed is not NULL the
+ * normalised rows are also quantised exactly as b2_quantize_fp32_to_int8 would
+ * (q_packed [rows, cols/4], scales [rows]); out may then be NULL. out may equal x (in place,
+ * as the reference engine uses it). cols % 4 == 0, cols <= 8192. */
+int b2_layernorm(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps, float* out,
+                 int32_t* q_packed, float* scales, b2_stream_t stream);
+
 /* ------------------------------------------------------------------ diagnostics */
 
 /* Returns the device error word of the current device (B2_DEVERR_* bits), synchronising

@@ -7,9 +7,12 @@
  * decode step advances every sequence of a batch by one token entirely on the device:
  * embedding, per layer [LayerNorm+quantise, INT8 QKV (+bias), QKV split + paged KV write,
  * K13 decode attention, quantise, INT8 out-proj (+bias+residual), LayerNorm+quantise, INT8
- * FC1 (+bias+GELU), quantise, INT8 FC2 (+bias+residual)], final LayerNorm, tied fp32 vocab
- * projection with a GPU argmax (lowest index on ties, like the reference's std::max_element,
- * src/sampler.cu:10-14), and the position advance. A step is a fixed launch sequence, so
+ * FC1 (+bias+GELU), quantise, INT8 FC2 (+bias+residual)], final LayerNorm, tied vocab
+ * projection (tensor cores, then every argmax candidate recomputed exactly in the reference's
+ * fp32 order) with a GPU argmax (lowest index on ties, like the reference's std::max_element,
+ * src/sampler.cu:10-14), and the position advance. LayerNorm sums in the reference kernel's
+ * order and the INT8 GEMM epilogues are bit-exact, so the int8 activations equal the
+ * reference engine's wherever the attention outputs (summed in another order) round alike. A step is a fixed launch sequence, so
  * b2_engine_run_steps replays it as a CUDA graph.
  *
  * Formats kept from the reference: the on-disk model directory (config.json + *.bin,
@@ -93,6 +96,18 @@ int b2_engine_step(b2_engine* e, b2_stream_t stream);
 
 /* `steps` decode steps, replayed from a CUDA graph of one step captured on first use. */
 int b2_engine_run_steps(b2_engine* e, int steps, b2_stream_t stream);
+
+/* One decode step with tokens chosen by the caller: tokens_in[b] (b < the batch given to
+ * b2_engine_start) is fed at sequence b's current position, the step runs (graph replay, as
+ * b2_engine_run_steps), every position advances by one, and the greedy next token of each
+ * sequence is written to next_out[b] (NULL: not copied). This is the reference's decode
+ * loop body (src/gpt2_engine.cu:716-750: copy the token in, embed, layers, final LayerNorm,
+ * logits, argmax) for a whole batch, with the token supplied by the caller instead of taken
+ * from the engine's own argmax or prompt; use it for teacher forcing, host-side sampling or
+ * continuation prompts. tokens_in and next_out may be device or host pointers (copied with
+ * cudaMemcpyDefault on `stream`; with pageable host memory the copies are synchronous).
+ * Asynchronous otherwise. */
+int b2_engine_decode_step(b2_engine* e, const int32_t* tokens_in, int32_t* next_out, b2_stream_t stream);
 
 /* Runs one decode step eagerly on a private stream with a CUDA event before every launch and
  * writes a text breakdown into report[report_bytes]: a first line "step_us <total> launches

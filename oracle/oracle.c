@@ -203,16 +203,31 @@ int oracle_max_threads(void) {
  * y = gamma*(x-mean)*inv + beta, the last step fused as in the reference build. */
 void oracle_layernorm(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps,
                       float* y) {
+    /* Sums in the reference kernel's order (kernels/layernorm/15_layernorm_residual.cu:59-103,
+       256 threads): thread t accumulates columns t, t+256, ... (sum of squares fused, as the
+       GPU build contracts it), then partial[t] += partial[t+s] for s = 128, 64, ..., 1. The
+       reference's rsqrtf is replaced by a correctly rounded 1/sqrt (they differ by at most a
+       couple of ulp), so rows agree with the GPU to about 1e-7 relative, not bit for bit. */
+    float ps[256], pq[256];
     for (int r = 0; r < rows; ++r) {
         const float* xr = x + (size_t)r * cols;
-        float s = 0.0f, ss = 0.0f;
-        for (int c = 0; c < cols; ++c) {
-            s += xr[c];
-            ss += xr[c] * xr[c];
+        for (int t = 0; t < 256; ++t) {
+            float s = 0.0f, q = 0.0f;
+            for (int c = t; c < cols; c += 256) {
+                s += xr[c];
+                q = fmaf(xr[c], xr[c], q);
+            }
+            ps[t] = s;
+            pq[t] = q;
         }
-        const float mean = s / cols;
-        const float var = ss / cols - mean * mean;
-        const float inv = 1.0f / sqrtf(var + eps);
+        for (int st = 128; st > 0; st >>= 1)
+            for (int t = 0; t < st; ++t) {
+                ps[t] += ps[t + st];
+                pq[t] += pq[t + st];
+            }
+        const float mean = ps[0] / (float)cols;
+        const float var = fmaf(-mean, mean, pq[0] / (float)cols);
+        const float inv = (float)(1.0 / sqrt((double)(var + eps)));
         for (int c = 0; c < cols; ++c) y[(size_t)r * cols + c] = fmaf(gamma[c] * (xr[c] - mean), inv, beta[c]);
     }
 }
@@ -226,7 +241,9 @@ void oracle_vocab_proj(int B, int V, int d, const float* h, const float* wte, fl
     for (int v = 0; v < V; ++v)
         for (int b = 0; b < B; ++b) {
             float sum = 0.0f;
-            for (int k = 0; k < d; ++k) sum += h[(size_t)b * d + k] * wte[(size_t)v * d + k];
+            /* sequential in k with a fused multiply-add per term, as the reference's kernel
+               compiles on the GPU */
+            for (int k = 0; k < d; ++k) sum = fmaf(h[(size_t)b * d + k], wte[(size_t)v * d + k], sum);
             logits[(size_t)b * V + v] = sum;
         }
 }

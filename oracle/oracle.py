@@ -4,7 +4,8 @@ Only tests/, __graft_entry__.smoke() and bench.py's CPU legs use this module, as
 checker. It wraps:
   - liboracle.so: the C restatement in oracle.c (numpy arrays in, numpy arrays out);
   - _ref/libref.so: the reference's own sources compiled by build_ref.sh — its CPU
-    attention harness, and its K13/K14/K12 CUDA kernels (device pointers in).
+    attention harness, and its K12/K13/K14/K15 CUDA kernels (device pointers in);
+  - _ref/libref_engine.so: the reference's GPT2Engine, greedy generation (model directory in).
 """
 from __future__ import annotations
 
@@ -16,6 +17,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref.so")
+REF_ENGINE_SO = os.path.join(HERE, "_ref", "libref_engine.so")
 
 _fp = ctypes.POINTER(ctypes.c_float)
 _ip = ctypes.POINTER(ctypes.c_int32)
@@ -59,9 +61,40 @@ def ref():
         R.ref_run_gqa_paged_attn.argtypes = [_i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]
         R.ref_run_quantize_fp32_to_int8.argtypes = [_i, _i, _vp, _vp, _vp]
         R.ref_run_int8_gemm.argtypes = [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i]
+        R.ref_run_layernorm.argtypes = [_i, _i, _vp, _vp, _vp, _vp, ctypes.c_float]
         R.ref_sync.restype = _i
         _ref = R
     return _ref
+
+
+_ref_engine = None
+
+
+def ref_engine_available() -> bool:
+    return os.path.exists(REF_ENGINE_SO)
+
+
+def ref_engine_generate(model_dir, prompt, max_new, want_logits=True, vocab=None, token_by_token=False):
+    """The reference's own GPT2Engine (src/gpt2_engine.cu, compiled unchanged into
+    oracle/_ref/libref_engine.so): greedy generate(prompt, max_new) on a fresh session, the
+    prompt through its FlashAttention prefill (or, token_by_token, through its decode path).
+    Returns (tokens [n], logits [n, vocab] or None); logits[i] chose tokens[i]. Needs a GPU."""
+    global _ref_engine
+    if _ref_engine is None:
+        if not ref_engine_available():
+            raise RuntimeError(f"{REF_ENGINE_SO} missing: run oracle/build_ref.sh where the reference is mounted")
+        R = ctypes.CDLL(REF_ENGINE_SO, mode=ctypes.RTLD_LOCAL)
+        R.ref_engine_generate.argtypes = [ctypes.c_char_p, _vp, _i, _i, _vp, _vp, _i]
+        R.ref_engine_generate.restype = _i
+        _ref_engine = R
+    p = np.ascontiguousarray(prompt, np.int32)
+    toks = np.zeros(max_new + 1, np.int32)
+    lg = np.zeros((max_new + 1, vocab), np.float32) if want_logits else None
+    n = _ref_engine.ref_engine_generate(model_dir.encode(), p.ctypes.data, len(p), max_new, toks.ctypes.data,
+                                        lg.ctypes.data if lg is not None else None, 1 if token_by_token else 0)
+    if n < 0:
+        raise RuntimeError("reference engine failed")
+    return toks[:n], (lg[:n] if lg is not None else None)
 
 
 def _c(a, dtype):

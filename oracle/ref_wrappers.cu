@@ -4,11 +4,12 @@
 //   - gqa_cpu_reference, the reference harness's CPU attention (tests/test_paged_attention.cu:138-179);
 //   - run_decode_attn (K13), run_quantize_fp32_to_int8 and run_int8_gemm* (K14), and
 //     run_paged_attn / run_gqa_paged_attn (K11/K12, the reference's GPU oracle for K13),
-//     built for sm_100a unchanged.
+//     and run_layernorm (K15), built for sm_100a unchanged.
 // Only the extern "C" ref_* symbols below are exported.
 #include "tests/test_paged_attention.cu"  // from the reference tree (-I REF)
 #include "decode/13_decode_attn.cuh"
 #include "quantization/14_int8_gemm.cuh"
+#include "layernorm/15_layernorm_residual.cuh"
 
 #define REF_API extern "C" __attribute__((visibility("default")))
 
@@ -45,6 +46,11 @@ REF_API void ref_run_int8_gemm(int M, int N, int K, const int32_t* A, const int3
         case 2: run_int8_gemm_bias_gelu(M, N, K, A, BT, sA, sB, bias, C); break;
         default: run_int8_gemm_bias_residual(M, N, K, A, BT, sA, sB, bias, residual, C); break;
     }
+}
+
+REF_API void ref_run_layernorm(int rows, int cols, const float* x, const float* gamma, const float* beta, float* out,
+                               float eps) {
+    run_layernorm(rows, cols, x, gamma, beta, out, eps);
 }
 
 REF_API int ref_sync(void) { return (int)cudaDeviceSynchronize(); }
