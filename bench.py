@@ -231,7 +231,7 @@ def time_cpu_attention(oracle, q, kc, vc, bt, lens, nthreads, budget_s, min_reps
             return el / reps
 
 
-def gemm_secondary(torch, b2, M, N, K, steps, peak_int8):
+def gemm_secondary(torch, b2, M, N, K, steps, peak_int8, hbm_peak):
     """TOPS of the INT8 GEMM (fp32 dequantised output, plain epilogue) at M x N x K."""
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(SEED + M + N + K)
@@ -265,8 +265,18 @@ def gemm_secondary(torch, b2, M, N, K, steps, peak_int8):
     ms = time_steps(torch, graph.replay, reps, 3)
     n = reps * copies
     tops = 2.0 * M * N * K / (ms / n * 1e-3) / 1e12
+    by = gemm_alg_bytes(M, N, K)
+    gbs = by / (ms / n * 1e-3) / 1e9
     return {"tops": round(tops, 2), "us_per_call": round(ms / n * 1e3, 2), "frac_of_int8_peak": round(tops / peak_int8, 4),
+            "algorithmic_bytes": by, "gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / hbm_peak, 4),
             "operand_copies": copies, "timing": "CUDA graph replays"}
+
+
+def gemm_alg_bytes(M, N, K):
+    """HBM bytes an INT8 GEMM must move once: int8 A [M, K] and B^T [N, K], the two fp32 scale
+    vectors, and the fp32 output C [M, N] (a decode-shape GEMM is bound by these, not by its
+    2MNK operations)."""
+    return M * K + N * K + 4 * (M + N) + 4 * M * N
 
 
 def run_gpu(args):
@@ -400,6 +410,23 @@ def secondary(torch, b2, np, args, kc, vc, q, btd, lensd, lens, bt, P, hbm_peak,
     out["gqa_config3_bf16_kv"] = {"gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / hbm_peak, 4),
                                   "us_per_call": round(ms / n * 1e3, 2), "algorithmic_bytes": by}
     del kb, vb
+    # the reference-named drop-in run_decode_attn (legacy default stream, the reference's
+    # caller-sized workspace [B, H_q, 16, d+2] floats) on the same fp32 batch
+    ws_ref = torch.empty(B * H_Q * 16 * (D + 2), dtype=torch.float32, device="cuda")
+    O_ref = torch.empty_like(q)
+    nbps = bt.shape[1]
+
+    def dropin():
+        b2.run_decode_attn(B, H_Q, H_KV, D, q, kc, vc, btd, lensd, max_ctx, BS, nbps, O_ref, ws_ref)
+
+    with torch.cuda.stream(torch.cuda.default_stream()):
+        ms = time_steps(torch, dropin, n, 3)
+    by = attn_alg_bytes(lens, H_KV, H_Q, D, 4, nbps)
+    gbs = by / (ms / n * 1e-3) / 1e9
+    out["dropin_run_decode_attn_config3"] = {
+        "gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / hbm_peak, 4), "us_per_call": round(ms / n * 1e3, 2),
+        "api": "run_decode_attn (reference signature, legacy default stream, reference-sized workspace)"}
+    del ws_ref, O_ref
     # config 1: MHA B1 H12 d64 ctx1024, 64-block random permutation; 6.3 MB fits in L2, so
     # 40 independent copies (250 MB) are rotated
     rng = np.random.default_rng(SEED)
@@ -433,11 +460,50 @@ def secondary(torch, b2, np, args, kc, vc, q, btd, lensd, lens, bt, P, hbm_peak,
                           "algorithmic_bytes": by1, "l2": "40 rotated copies (250 MB)",
                           "timing": "CUDA graph replays of 40 calls"}
     del sets
-    out["gpt2_small_config4"] = gpt2_config4(torch, b2, np, hbm_peak)
+    out["gpt2_small_config4"] = gpt2_config4(torch, b2, np, hbm_peak, cpu_step=True)
     peak_int8 = 2.0 * bf16_peak  # dense int8 rate is twice the bf16 rate on the same tensor cores
     for (M, N, K) in [(2048, 2048, 2048), (64, 3072, 768), (8192, 8192, 8192)]:
-        out[f"int8_gemm_{M}x{N}x{K}"] = gemm_secondary(torch, b2, M, N, K, args.steps, peak_int8)
+        out[f"int8_gemm_{M}x{N}x{K}"] = gemm_secondary(torch, b2, M, N, K, args.steps, peak_int8, hbm_peak)
     out["int8_peak_tops"] = peak_int8
+    out["cpu_baselines"] = cpu_secondary(np)
+    return out
+
+
+def host_cpu():
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"model": model, "nproc": os.cpu_count()}
+
+
+def cpu_secondary(np):
+    """CPU baselines of the other hot-path pieces (the oracle's scalar restatements; reported,
+    not targets): the int32 GEMM loop on the config-2 shapes, and one GPT-2 Small decode step
+    at batch 1 (config 4's model, the reference engine's B = 1 loop)."""
+    import tempfile
+
+    from oracle import oracle
+
+    out = {"host": host_cpu()}
+    rng = np.random.default_rng(SEED)
+    for (M, N, K, rows, reps) in ((64, 3072, 768, 64, 10), (2048, 2048, 2048, 256, 1)):
+        A = rng.integers(-127, 128, (rows, K), dtype=np.int8).view(np.int32)
+        Bt = rng.integers(-127, 128, (N, K), dtype=np.int8).view(np.int32)
+        oracle.int8_gemm_s32(A[:1], Bt, nthreads=1)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            oracle.int8_gemm_s32(A, Bt, nthreads=1)
+        sec = (time.perf_counter() - t0) / reps
+        gops = 2.0 * rows * N * K / sec / 1e9
+        out[f"int8_gemm_{M}x{N}x{K}_scalar"] = {
+            "gops": round(gops, 2), "cores": 1, "kind": "port",
+            "sample": f"{rows} of the {M} rows of A against all of B^T (int32 accumulators, scalar loop)",
+            "est_ms_full": round(2.0 * M * N * K / (gops * 1e9) * 1e3, 1)}
     return out
 
 
@@ -454,7 +520,33 @@ def gpt2_step_bytes(cfg, B, ctx_mean):
     return lin + vec + V * d * 4 + kv
 
 
-def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
+def gpt2_cpu_step(eng, np, cfg, steps=4):
+    """The oracle's restatement of the reference engine's decode step (GPT2Oracle, 1 thread)
+    on this model at batch 1, the reference engine's own batch: seconds per token over
+    `steps` steps at positions 0.. (short contexts, so the weights dominate)."""
+    import shutil
+    import tempfile
+
+    from oracle import oracle
+
+    d = tempfile.mkdtemp(prefix="b2gpt2_")
+    try:
+        eng.export(d)
+        orc = oracle.GPT2Oracle(d)
+        orc.reset(1)
+        orc.step(np.array([11]), np.array([0]), nthreads=1)
+        t0 = time.perf_counter()
+        for p in range(1, steps + 1):
+            orc.step(np.array([100 + p]), np.array([p]), nthreads=1)
+        sec = (time.perf_counter() - t0) / steps
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return {"tok_s": round(1.0 / sec, 2), "ms_per_token": round(sec * 1e3, 1), "cores": 1, "kind": "port",
+            "sample": f"GPT2Oracle (C restatement of the reference's decode step), batch 1, {steps} steps at "
+                      f"positions 1-{steps}"}
+
+
+def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64, cpu_step=False):
     """GPT-2 Small INT8, batch 64, 128-token prompts fed through the decode
     path, then 128 greedy steps (CUDA-graph replays); tok/s of the generation steps."""
     cfg = GPT2_SMALL
@@ -486,6 +578,7 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
     step_s = gen_ms / steps_new * 1e-3
     toks = eng.tokens()
     breakdown = parse_profile(eng.profile_step())
+    cpu = gpt2_cpu_step(eng, np, cfg) if cpu_step else None
     eng.close()
     return {"tok_s": round(B * steps_new / (gen_ms * 1e-3), 1), "ms_per_step": round(gen_ms / steps_new, 4),
             "prefill_tok_s": round(B * (prompt_len - 1) / (pre_ms * 1e-3), 1),
@@ -495,7 +588,7 @@ def gpt2_config4(torch, b2, np, hbm_peak, steps_new=128, prompt_len=128, B=64):
             "hbm_bound_tok_s": round(B / (by / (hbm_peak * 1e9)), 1),
             "generated_tokens_valid": bool((toks[:, prompt_len:prompt_len + steps_new] >= 0).all()),
             "timing": "CUDA graph replays of one decode step", "kv_block_seed": block_seed(),
-            "step_breakdown": breakdown}
+            "step_breakdown": breakdown, "cpu_baseline_b1": cpu}
 
 
 WIDE = dict(n_layers=32, n_heads=32, d_model=4096, d_ff=16384, vocab_size=50257, max_seq_len=4096 + 64 + 1,

@@ -3,6 +3,8 @@
 #include "common.cuh"
 #include "b2_reference_api.h"
 #include "engine_kernels.cuh"
+#include <algorithm>
+#include <cuda.h>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -171,6 +173,41 @@ int b2_version(void) { return 100; }
 // Same names and parameter lists as the reference; launches go to the legacy default
 // stream as the reference's do. Errors, which the reference drops, land in b2_last_status().
 
+namespace {
+
+// Whole KV blocks of `block_bytes` between `cache` and the end of the device allocation that
+// holds it (0 when unknown). The reference's run_decode_attn does not pass the pool size; the
+// allocation's extent bounds it, which lets the kernel stage blocks with TMA (a tensor map
+// needs the pool's extent) and check block-table entries against it.
+int pool_blocks_of(const void* cache, size_t block_bytes) {
+    typedef CUresult (*RangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static RangeFn fn = nullptr;
+    static bool resolved = false;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!resolved) {
+            void* ptr = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+                q == cudaDriverEntryPointSuccess)
+                fn = reinterpret_cast<RangeFn>(ptr);
+            resolved = true;
+        }
+    }
+    if (!fn || !cache || block_bytes == 0) return 0;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, (CUdeviceptr)(uintptr_t)cache) != CUDA_SUCCESS) {
+        cudaGetLastError();
+        return 0;
+    }
+    const size_t avail = (size_t)(base + size - (CUdeviceptr)(uintptr_t)cache);
+    return (int)std::min<size_t>(avail / block_bytes, 0x7fffffff);
+}
+
+}  // namespace
+
 void run_decode_attn(int B, int H_q, int H_kv, int d, const float* Q, const float* k_cache, const float* v_cache,
                      const int* block_table, const int* context_lens, int max_context_len, int block_size,
                      int num_blocks_per_seq, float* O, float* workspace) {
@@ -179,7 +216,9 @@ void run_decode_attn(int B, int H_q, int H_kv, int d, const float* Q, const floa
     a.Q = Q; a.k_cache = k_cache; a.v_cache = v_cache; a.kv_dtype = B2_KV_F32;
     a.block_table = block_table; a.context_lens = context_lens;
     a.max_context_len = max_context_len; a.block_size = block_size; a.num_blocks_per_seq = num_blocks_per_seq;
-    a.num_phys_blocks = 0; a.scale = 0.f; a.O = O;
+    const size_t block_bytes = (size_t)(block_size > 0 ? block_size : 0) * (H_kv > 0 ? H_kv : 0) * (d > 0 ? d : 0) * 4;
+    a.num_phys_blocks = std::min(pool_blocks_of(k_cache, block_bytes), pool_blocks_of(v_cache, block_bytes));
+    a.scale = 0.f; a.O = O;
     a.workspace = workspace;
     a.workspace_bytes = (size_t)(B > 0 ? B : 0) * (H_q > 0 ? H_q : 0) * DA_MAX_SPLITS * (d + 2) * sizeof(float);
     t_last_status = decode_attn_launch(&a, kDropInMaxSplits, false, 0);
