@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "engine_kernels.cuh"
 #include "epilogue.cuh"
+#include "rowops.cuh"
 #include <algorithm>
 #include <cstring>
 #include <cuda_bf16.h>
@@ -62,37 +63,6 @@ __global__ void embed_kernel(int d, const int* __restrict__ tokens, const int* _
 // warp kernel with each lane holding the 8 partials t = lane + 32 j.
 constexpr int LNQ_THREADS = 256;
 constexpr int LNQ_MAX_PER_THREAD = 32;
-
-// Halving-tree sum of one value per thread of a 256-thread CTA (the order above): strides
-// 128, 64 and 32 through shared memory, then 16 .. 1 by shuffles within warp 0, whose lane 0
-// pairing is the same tree. Every thread gets the total.
-__device__ __forceinline__ float tree_sum256(float v, float* red) {
-    const int t = threadIdx.x;
-    red[t] = v;
-    __syncthreads();
-    if (t < 128) red[t] += red[t + 128];
-    __syncthreads();
-    if (t < 64) red[t] += red[t + 64];
-    __syncthreads();
-    if (t < 32) {
-        float x = red[t] + red[t + 32];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) x += __shfl_down_sync(0xffffffffu, x, o);
-        if (t == 0) red[256] = x;
-    }
-    __syncthreads();
-    const float total = red[256];
-    __syncthreads();
-    return total;
-}
-
-// LayerNorm statistics from the row sums (shared by both kernels).
-__device__ __forceinline__ void ln_stats(float sum, float sumsq, int cols, float eps, float& mean, float& inv) {
-    const float n = (float)cols;
-    mean = sum / n;
-    const float var = fmaf(-mean, mean, sumsq / n);
-    inv = rsqrtf(var + eps);
-}
 
 __global__ void __launch_bounds__(LNQ_THREADS)
 ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__ gamma,
@@ -165,12 +135,8 @@ ln_quant_kernel(int cols, const float* __restrict__ x, const float* __restrict__
     }
 }
 
-// One warp per row (32-thread CTA) for rows of at most 256 * KC columns (decode rows are
-// short), loaded as float4: lane l holds columns 4l + i + 128 h + 256 k (i < 4, h < 2,
-// k < KC), i.e. the 8 partials t = 4l + i + 128 h of the 256-partial order above, each over
-// its columns t + 256 k. The tree's stride 128 combines a lane's h = 0 and h = 1 partials;
-// strides 64 .. 4 pair lane l with lane l + 16, 8, 4, 2, 1 (shuffles, the same i); strides 2
-// and 1 combine lane 0's four i partials.
+// One warp per row (32-thread CTA) for rows of at most 256 * KC columns: ln_row_warp
+// (rowops.cuh) on row blockIdx.x.
 template <int KC>
 __global__ void __launch_bounds__(32)
 ln_quant_warp_kernel(int cols, const float* __restrict__ x, const float* __restrict__ gamma,
@@ -179,106 +145,10 @@ ln_quant_warp_kernel(int cols, const float* __restrict__ x, const float* __restr
                      __nv_bfloat16* __restrict__ y_lo) {
     griddep_wait();
     griddep_launch();
-    const int row = blockIdx.x, lane = threadIdx.x;
-    const float* xr = x + (size_t)row * cols;
-    float4 v[2][KC];
-    float ps[4] = {0.f, 0.f, 0.f, 0.f}, pq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < KC; ++k) {
-            const int c = 4 * lane + 128 * h + 256 * k;
-            v[h][k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (c < cols) {
-                v[h][k] = *reinterpret_cast<const float4*>(xr + c);
-                const float t[4] = {v[h][k].x, v[h][k].y, v[h][k].z, v[h][k].w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    s4[i] += t[i];
-                    q4[i] = fmaf(t[i], t[i], q4[i]);
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {  // stride 128: partial t += partial t + 128
-            ps[i] = h == 0 ? s4[i] : ps[i] + s4[i];
-            pq[i] = h == 0 ? q4[i] : pq[i] + q4[i];
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            ps[i] += __shfl_down_sync(0xffffffffu, ps[i], o);
-            pq[i] += __shfl_down_sync(0xffffffffu, pq[i], o);
-        }
-    float s = (ps[0] + ps[2]) + (ps[1] + ps[3]);
-    float ss = (pq[0] + pq[2]) + (pq[1] + pq[3]);
-    s = __shfl_sync(0xffffffffu, s, 0);
-    ss = __shfl_sync(0xffffffffu, ss, 0);
-    float mean, inv;
-    ln_stats(s, ss, cols, eps, mean, inv);
-    float amax = 0.f;
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int k = 0; k < KC; ++k) {
-            const int c = 4 * lane + 128 * h + 256 * k;
-            if (c < cols) {
-                const float4 g = *reinterpret_cast<const float4*>(gamma + c);
-                const float4 bb = *reinterpret_cast<const float4*>(beta + c);
-                float4& t = v[h][k];
-                t.x = fmaf(g.x * (t.x - mean), inv, bb.x);
-                t.y = fmaf(g.y * (t.y - mean), inv, bb.y);
-                t.z = fmaf(g.z * (t.z - mean), inv, bb.z);
-                t.w = fmaf(g.w * (t.w - mean), inv, bb.w);
-                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w))));
-            }
-        }
-    if (!q_out) {  // plain LayerNorm (final ln_f feeding the vocab projection), fp32 and/or bf16 hi/lo
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int k = 0; k < KC; ++k) {
-                const int c = 4 * lane + 128 * h + 256 * k;
-                if (c >= cols) continue;
-                const size_t o = (size_t)row * cols + c;
-                if (y_out) *reinterpret_cast<float4*>(y_out + o) = v[h][k];
-                if (y_hi) {
-                    const float t[4] = {v[h][k].x, v[h][k].y, v[h][k].z, v[h][k].w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const __nv_bfloat16 hb = __float2bfloat16_rn(t[i]);
-                        y_hi[o + i] = hb;
-                        y_lo[o + i] = __float2bfloat16_rn(t[i] - __bfloat162float(hb));
-                    }
-                }
-            }
-        return;
-    }
-    amax = warp_max(amax);
-    // quantiser semantics of kernels/quantization/14_int8_gemm.cu:36-58
-    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-    const float invs = __fdiv_rn(1.0f, scale);
-    if (lane == 0) scale_out[row] = scale;
-    int32_t* qr = q_out + (size_t)row * (cols >> 2);
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int k = 0; k < KC; ++k) {
-            const int c = 4 * lane + 128 * h + 256 * k;
-            if (c >= cols) continue;
-            const float t[4] = {v[h][k].x, v[h][k].y, v[h][k].z, v[h][k].w};
-            uint32_t packed = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float qf = fminf(fmaxf(rintf(__fmul_rn(t[i], invs)), -128.f), 127.f);
-                packed |= (uint32_t)(uint8_t)(int8_t)(int)qf << (8 * i);
-            }
-            qr[c >> 2] = (int32_t)packed;
-            if (y_out) *reinterpret_cast<float4*>(y_out + (size_t)row * cols + c) = v[h][k];
-        }
+    const size_t row = blockIdx.x;
+    ln_row_warp<KC>(x + row * cols, cols, gamma, beta, eps, q_out ? q_out + row * (cols >> 2) : nullptr,
+                    q_out ? scale_out + row : nullptr, y_out ? y_out + row * cols : nullptr,
+                    y_hi ? y_hi + row * cols : nullptr, y_lo ? y_lo + row * cols : nullptr, threadIdx.x);
 }
 
 // ------------------------------------------------------------------ QKV split + paged KV write

@@ -22,6 +22,7 @@
 //   share A and B tiles in L2.
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "rowops.cuh"
 #include "engine_kernels.cuh"
 #include <cuda_bf16.h>
 #include <algorithm>
@@ -90,36 +91,8 @@ quantize_rows_warp_kernel(int cols, const float* __restrict__ in, int32_t* __res
                           float* __restrict__ scales) {
     griddep_wait();
     griddep_launch();
-    const int row = blockIdx.x, lane = threadIdx.x;
-    const float4* x4 = reinterpret_cast<const float4*>(in + (size_t)row * cols);
-    const int c4 = cols >> 2;
-    float4 v[NV4];
-    float amax = 0.f;
-#pragma unroll
-    for (int k = 0; k < NV4; ++k) {
-        const int i = lane + 32 * k;
-        v[k] = i < c4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
-    }
-    amax = warp_max(amax);
-    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-    const float inv = __fdiv_rn(1.0f, scale);
-    if (lane == 0) scales[row] = scale;
-    int32_t* o = out + (size_t)row * c4;
-#pragma unroll
-    for (int k = 0; k < NV4; ++k) {
-        const int i = lane + 32 * k;
-        if (i < c4) {
-            const float t[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-            uint32_t packed = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float q = fminf(fmaxf(rintf(__fmul_rn(t[j], inv)), -128.f), 127.f);
-                packed |= (uint32_t)(uint8_t)(int8_t)(int)q << (8 * j);
-            }
-            o[i] = (int32_t)packed;
-        }
-    }
+    const size_t row = blockIdx.x;
+    quant_row_warp<NV4>(in + row * cols, cols, out + row * (cols >> 2), scales + row, threadIdx.x);
 }
 
 int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st) {
