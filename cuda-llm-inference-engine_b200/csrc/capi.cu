@@ -68,6 +68,11 @@ bool& pdl_enabled() {
     return on;
 }
 
+bool& weights_constant() {
+    static thread_local bool on = false;
+    return on;
+}
+
 constexpr int kAbiMaxSplits = 64;
 // The reference workspace holds DA_MAX_SPLITS rows per head; the drop-in wrapper keeps one
 // row's worth for the arrival counters.
@@ -108,6 +113,9 @@ int b2_quantize_fp32_to_int8(int rows, int cols, const float* input, int32_t* ou
 int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, const float* scale_A,
                  const float* scale_B, const float* bias, const float* residual, float* C, int epilogue,
                  b2_stream_t stream) {
+    // programmatic dependent launch: set-up overlaps the previous kernel; no global memory is
+    // read before the kernel waits for it
+    PdlOn pdl;
     return gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C, epilogue, false,
                        static_cast<cudaStream_t>(stream));
 }
@@ -121,12 +129,14 @@ int b2_int8_gemm_ws(int M, int N, int K, const int32_t* A_packed, const int32_t*
                     const float* scale_B, const float* bias, const float* residual, float* C, int epilogue,
                     void* workspace, size_t workspace_bytes, b2_stream_t stream) {
     if (workspace && ((uintptr_t)workspace & 255)) return B2_ERR_INVALID;
+    PdlOn pdl;
     return gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C, epilogue, false,
                        static_cast<cudaStream_t>(stream), workspace, workspace_bytes);
 }
 
 int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, int32_t* C_acc,
                      b2_stream_t stream) {
+    PdlOn pdl;
     return gemm_launch(M, N, K, A_packed, BT_packed, nullptr, nullptr, nullptr, nullptr, C_acc, B2_EPI_PLAIN, true,
                        static_cast<cudaStream_t>(stream));
 }

@@ -334,8 +334,26 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Host: whether launches made by this thread use programmatic dependent launch (set by the
-// decode engine around its step, whose data dependencies it knows).
+// decode engine around its step, whose data dependencies it knows, and by public entry points
+// whose kernels read nothing before griddep_wait()).
 bool& pdl_enabled();
+
+// Host: whether GEMMs launched by this thread may read their weights before waiting on the
+// previous grid (the decode engine's step: its weights never change).
+bool& weights_constant();
+
+// Host: sets pdl_enabled() (and optionally weights_constant()) for a scope.
+struct PdlOn {
+    bool saved_pdl, saved_w;
+    explicit PdlOn(bool constant_weights = false) : saved_pdl(pdl_enabled()), saved_w(weights_constant()) {
+        pdl_enabled() = true;
+        weights_constant() = constant_weights;
+    }
+    ~PdlOn() {
+        pdl_enabled() = saved_pdl;
+        weights_constant() = saved_w;
+    }
+};
 
 // Host: launch `kern` on `st`, with programmatic stream serialisation when pdl_enabled().
 template <typename... KArgs, typename... Args>

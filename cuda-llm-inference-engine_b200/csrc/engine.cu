@@ -382,10 +382,8 @@ namespace {
 // One decode step: a fixed sequence of launches on `st` (capturable as a CUDA graph).
 // Enables programmatic dependent launch for the launches of one decode step: every kernel in
 // the step reads only constant weights before its griddep_wait().
-struct PdlScope {
-    bool saved;
-    PdlScope() : saved(pdl_enabled()) { pdl_enabled() = true; }
-    ~PdlScope() { pdl_enabled() = saved; }
+struct PdlScope : PdlOn {
+    PdlScope() : PdlOn(/*constant_weights=*/true) {}
 };
 
 // Optional per-launch timing of one eager step: an event is recorded on the step's stream

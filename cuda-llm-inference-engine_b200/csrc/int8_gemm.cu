@@ -150,6 +150,10 @@ struct GemmParams {
     // accumulator rows the epilogue never stores)
     int a_rows;
     QkvScatter sc;  // sc.q != nullptr: the engine's fused QKV split + paged KV write
+    // the weights (B) are constant, so their first ring stages may be requested before the
+    // kernel waits on the previous grid (the decode engine); otherwise every global read
+    // follows the wait, which makes programmatic dependent launch safe for any producer
+    int b_early;
 };
 
 template <int BN>
@@ -320,7 +324,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             // B tiles are requested before waiting on it (programmatic dependent launch),
             // the activation (A) tiles after.
             int npre = 0;
-            if ((int)blockIdx.x < num_units) {
+            if (p.b_early && (int)blockIdx.x < num_units) {
                 const int w = blockIdx.x;
                 const int kb0 = (w % p.k_splits) * p.kb_per_split;
                 const int kb1 = min(nk, kb0 + p.kb_per_split);
@@ -646,6 +650,7 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     griddep_wait();
+    griddep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -1028,6 +1033,7 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
     }
     GemmParams p{M, N, K, sA, sB, bias, residual, C, device_error_ptr(), 1, 0, nullptr, nullptr,
                  M <= GM_BM ? ((M + 7) & ~7) : GM_BM};
+    p.b_early = weights_constant() ? 1 : 0;
     if (s32) return gemm_dispatch<B2_EPI_PLAIN, true>(p, A, BT, ws, ws_bytes, st);
     switch (epi) {
         case B2_EPI_PLAIN: return gemm_dispatch<B2_EPI_PLAIN, false>(p, A, BT, ws, ws_bytes, st);
@@ -1048,6 +1054,7 @@ int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, co
         return B2_ERR_INVALID;
     if (sc.d <= 0 || sc.d % 16 || N != 3 * sc.d || M > GM_BM) return B2_ERR_UNSUPPORTED;
     GemmParams p{M, N, K, sA, sB, bias, nullptr, sc.q, device_error_ptr(), 1, 0, nullptr, nullptr, (M + 7) & ~7};
+    p.b_early = weights_constant() ? 1 : 0;
     p.sc.q = sc.q;
     p.sc.k = sc.k;
     p.sc.v = sc.v;
