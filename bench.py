@@ -183,6 +183,20 @@ def time_steps(torch, fn, steps, warmup, dist=None):
     return ms
 
 
+def graph_of(torch, fn, warm=3):
+    """A CUDA graph holding one call of fn (after `warm` eager calls set up the kernels'
+    attributes and tensor maps): replaying it runs one step with no Python launch cost, so a
+    short step is timed on the device, not on the host's call rate."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
 def make_kv_shard(torch, P, h0, h1, dtype, device):
     """K/V cache [P, BS, h1-h0, D] for KV heads [h0, h1); each head's values come from its
     own seeded generator, so a shard equals the same heads of the unsharded cache."""
@@ -320,8 +334,10 @@ def run_gpu(args):
     def step():
         b2.decode_attn(q, kc, vc, btd, lensd, max_ctx, O=O, workspace=ws)
 
+    # one step = one replay of a graph holding the one decode_attn launch
+    step_graph = graph_of(torch, step)
     with ClockMonitor(local) as mon:
-        ms = time_steps(torch, step, args.steps, args.warmup, dist)
+        ms = time_steps(torch, step_graph.replay, args.steps, args.warmup, dist)
     clocks = mon.summary()
     assert b2.device_error() == 0, "device error during the timed region"
     bytes_rank = attn_alg_bytes(lens, hkv, hq, D, 4, nbps)
@@ -360,7 +376,8 @@ def run_gpu(args):
         "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, ragged lengths U[512,8192], random block table)",
         "config": {"workload": "gqa_decode_attn_config3", "batch": B, "h_q": H_Q, "h_kv": H_KV, "head_dim": D,
                    "block_size": BS, "ctx_lens": "U[512,8192] seed 42", "sum_ctx": int(lens.sum()),
-                   "kv_dtype": "fp32", "parallelism": f"kv-heads x{world}", "l2": "inputs larger than L2 "
+                   "kv_dtype": "fp32", "parallelism": f"kv-heads x{world}",
+                   "timing": "one CUDA-graph replay (one decode_attn launch) per step", "l2": "inputs larger than L2 "
                    f"({bytes_rank / 1e9:.3f} GB per rank per step vs 126 MB L2)", "algorithmic_bytes": bytes_total},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
@@ -845,7 +862,7 @@ def run_only(args):
         C = torch.empty(M, N, device=dev)
         fn = lambda: b2.int8_gemm(A, Bt, sA, sB, C=C)  # noqa: E731
         by = 2 * M * N * K
-    ms = time_steps(torch, fn, args.steps, args.warmup)
+    ms = time_steps(torch, graph_of(torch, fn).replay, args.steps, args.warmup)
     assert b2.device_error() == 0
     print(f"{args.only}: {ms / args.steps * 1e3:.2f} us/launch, {by / (ms / args.steps * 1e-3) / 1e9:.1f} "
           f"{'GB/s' if args.only.startswith('attn') else 'GOP/s'} (not a bench value)", flush=True)

@@ -14,9 +14,8 @@ namespace b2 {
 // The library's device error word (B2_DEVERR_* bits), one per device.
 __device__ unsigned int g_device_error = 0;
 
-int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counters_zeroed, cudaStream_t st);
-size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size, int max_splits,
-                                  int kv_bytes);
+int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaStream_t st);
+size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size);
 int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st);
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
                 const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
@@ -73,10 +72,6 @@ bool& weights_constant() {
     return on;
 }
 
-constexpr int kAbiMaxSplits = 64;
-// The reference workspace holds DA_MAX_SPLITS rows per head; the drop-in wrapper keeps one
-// row's worth for the arrival counters.
-constexpr int kDropInMaxSplits = DA_MAX_SPLITS - 1;
 
 static thread_local int t_last_status = B2_OK;
 
@@ -89,8 +84,8 @@ extern "C" {
 
 size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim, int max_context_len, int block_size) {
     if (B <= 0 || H_q <= 0 || H_kv <= 0 || head_dim <= 0 || block_size <= 0 || max_context_len < 0) return 0;
-    // sized for the fp32 plan, which never has fewer splits than the bf16 one
-    return decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size, kAbiMaxSplits, 4);
+    if (H_q % H_kv != 0) return 0;
+    return decode_attn_workspace_size(B, H_q, H_kv, head_dim, max_context_len, block_size);
 }
 
 int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream) {
@@ -100,7 +95,7 @@ int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream) {
     // the previous kernel's tail (about 0.15 us per call, 1-2% on long batches).
     const bool saved = pdl_enabled();
     pdl_enabled() = true;
-    const int r = decode_attn_launch(args, kAbiMaxSplits, true, static_cast<cudaStream_t>(stream));
+    const int r = decode_attn_launch(args, true, static_cast<cudaStream_t>(stream));
     pdl_enabled() = saved;
     return r;
 }
@@ -231,7 +226,7 @@ void run_decode_attn(int B, int H_q, int H_kv, int d, const float* Q, const floa
     a.scale = 0.f; a.O = O;
     a.workspace = workspace;
     a.workspace_bytes = (size_t)(B > 0 ? B : 0) * (H_q > 0 ? H_q : 0) * DA_MAX_SPLITS * (d + 2) * sizeof(float);
-    t_last_status = decode_attn_launch(&a, kDropInMaxSplits, false, 0);
+    t_last_status = decode_attn_launch(&a, false, 0);
 }
 
 void run_quantize_fp32_to_int8(int rows, int cols, const float* input, int32_t* output_packed, float* scales) {

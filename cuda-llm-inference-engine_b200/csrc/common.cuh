@@ -322,6 +322,18 @@ __device__ __forceinline__ void named_barrier(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also ORs a predicate over the participating threads: every thread
+// gets the same answer, so a decision taken on it keeps the threads together.
+__device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\t"
+                 "setp.ne.u32 p, %1, 0;\n\t"
+                 "barrier.red.or.pred q, %2, %3, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
+    return r != 0;
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // A kernel launched with programmatic stream serialisation may start while the previous
 // kernel on the stream is still running. Everything before griddep_wait() must touch only

@@ -40,6 +40,8 @@ constexpr int DA_NW = 8;                 // consumer warps
 constexpr int DA_NT = (DA_NW + 1) * 32;  // + producer warp
 constexpr int DA_MINB = 3;               // CTAs per SM the register budget is sized for (G <= 4)
 
+constexpr int DA_MAX_B = 256;           // sequences per launch of the kernel (larger batches are chunked)
+
 struct DecodeAttnParams {
     const float* Q;
     const unsigned char* k_cache;
@@ -47,10 +49,12 @@ struct DecodeAttnParams {
     const int* block_table;
     const int* context_lens;
     float* O;
-    float* ws_partial;          // [B, H_q, num_splits, D + 2]
-    unsigned int* ws_counter;   // [B, H_kv]
+    float* ws_partial;          // [pieces][G][D + 2] partial (o, m, l) of every piece of a unit
+    unsigned int* ws_counter;   // [B * H_kv] arrival tickets
+    int B;                      // sequences of this launch (<= DA_MAX_B)
     int H_q, H_kv, block_size, num_blocks_per_seq, num_phys_blocks;
-    int num_splits, blocks_per_split;
+    int chunk_min;              // fewest cache blocks a CTA streams (balanced plan)
+    int unit_mode;              // 1: CTA u serves (sequence, KV head) unit u whole, no workspace
     float scale_log2;           // softmax scale * log2(e)
     unsigned int* err;          // device error word
 };
@@ -75,11 +79,13 @@ struct DACfg {
     static constexpr int OFF_ML = OFF_X + DA_NW * 32 * 4;                // f32 [NW][G][2]
     static constexpr int OFF_BT = OFF_ML + DA_NW * G * 2 * 4;            // i32 [BT_CAP] block-table slice
     static constexpr int BT_CAP = 256;
-    static constexpr int OFF_MISC = OFF_BT + BT_CAP * 4;                 // u32 flags
+    static constexpr int OFF_P = OFF_BT + BT_CAP * 4;                    // i32 [DA_MAX_B + 1] block prefix
+    static constexpr int OFF_CTX = OFF_P + (DA_MAX_B + 4) * 4;           // i32 [DA_MAX_B] context lengths
+    static constexpr int OFF_MISC = OFF_CTX + DA_MAX_B * 4;              // u32 flags
     static constexpr int OFF_BAR = (OFF_MISC + 16 + 7) & ~7;             // u64 full[S], empty[S]
     static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8;
     static_assert(D % 32 == 0, "head_dim must be 64 or 128");
-    static_assert(DA_NW * G * D * 4 <= STAGES * STAGE, "final reduction must fit the ring");
+    static_assert(DA_NW * G * D * 4 <= STAGE, "the warps' merge must fit one ring stage");
     static_assert(TW % TPW == 0 && T % 32 == 0, "tile must split evenly over the consumer warps");
 };
 
@@ -321,14 +327,21 @@ struct DAWarp {
     }
 };
 
-// Final stage of a (sequence, KV head) split, by the NC consumer threads: `get(i, o, M, L)`
-// gives the split's merged unnormalised output o, max M and sum L for element i = g*D + d.
-// One split: O = o / L. Otherwise the split's partial goes to the workspace and the last of
-// the nsplit CTAs (or work items) to arrive (atomic ticket) merges all partials into O and
-// leaves the counter at zero.
+// Floats of one piece in the workspace: o [G][D], then (M, L) [G][2] padded to 16 bytes, so
+// every piece and every head's o row starts 16-byte aligned.
+template <int G, int D>
+constexpr int da_piece_floats() { return G * D + ((2 * G + 3) & ~3); }
+
+// Final stage of a piece of a (sequence, KV head) unit, by the NC consumer threads:
+// `get(i, o, M, L)` gives the piece's merged unnormalised output o, max M and sum L for
+// element i = g*D + d. A unit in one piece: O = o / L. Otherwise the piece goes to workspace
+// row `slot0 + split` and the last of the unit's nsplit pieces to arrive (atomic ticket on
+// the unit's counter) merges all of them into O and leaves the counter at zero. `scratch`
+// (shared memory, >= 2 * nsplit * G floats) may alias what `get` reads.
 template <int G, int D, int NC, typename Get>
-__device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int kvh, int split, int nsplit, int tid,
-                                          volatile unsigned int* ticket, Get get) {
+__device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int kvh, int split, int nsplit,
+                                          int slot0, int tid, volatile unsigned int* ticket, float* scratch,
+                                          Get get) {
     const int hq0 = kvh * G;
     float* O = p.O + ((size_t)b * p.H_q + hq0) * D;
     if (nsplit == 1) {
@@ -339,42 +352,174 @@ __device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int 
         }
         return;
     }
-    const size_t rowlen = D + 2;
-    for (int i = tid; i < G * D; i += NC) {
-        const int g = i / D, d = i - g * D;
-        float o, M, L;
-        get(i, o, M, L);
-        float* ws = p.ws_partial + (((size_t)b * p.H_q + hq0 + g) * p.num_splits + split) * rowlen;
-        ws[d] = o;
-        if (d == 0) { ws[D] = M; ws[D + 1] = L; }
+    constexpr int piece = da_piece_floats<G, D>();
+    float* ws0 = p.ws_partial + (size_t)slot0 * piece;
+    {
+        float* ws = ws0 + (size_t)split * piece;
+        for (int i = tid; i < G * D; i += NC) {
+            float o, M, L;
+            get(i, o, M, L);
+            ws[i] = o;
+            if ((i & (D - 1)) == 0) {
+                ws[G * D + 2 * (i / D)] = M;
+                ws[G * D + 2 * (i / D) + 1] = L;
+            }
+        }
     }
     __threadfence();
     named_barrier(1, NC);
     unsigned int* counter = p.ws_counter + (size_t)b * p.H_kv + kvh;
     if (tid == 0) *ticket = atomicAdd(counter, 1u);
     named_barrier(1, NC);
-    if (*ticket != (unsigned)(nsplit - 1)) return;
+    const bool last = *ticket == (unsigned)(nsplit - 1);
+    named_barrier(1, NC);  // every thread has read the ticket (and is done with `get`)
+    if (!last) return;
     __threadfence();
-    for (int i = tid; i < G * D; i += NC) {
-        const int g = i / D, d = i - g * D;
-        const float* ws = p.ws_partial + ((size_t)b * p.H_q + hq0 + g) * p.num_splits * rowlen;
+    // (M, L) of every piece into shared memory in one round of independent loads
+    float* Ms = scratch;               // [nsplit][G]
+    float* Ls = scratch + nsplit * G;  // [nsplit][G]
+    for (int j = tid; j < nsplit * G; j += NC) {
+        const int sp = j / G, g = j - sp * G;
+        const float* ml = ws0 + (size_t)sp * piece + G * D + 2 * g;
+        Ms[j] = __ldcg(ml);
+        Ls[j] = __ldcg(ml + 1);
+    }
+    named_barrier(1, NC);
+    // each thread merges 4 consecutive outputs of one head with 16-byte loads
+    for (int i4 = tid; i4 < G * D / 4; i4 += NC) {
+        const int g = (i4 * 4) / D;
         float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(ws + s * rowlen + D));
-        float L = 0.f, o = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float w = fast_exp2(__ldcg(ws + s * rowlen + D) - M);
-            L = fmaf(__ldcg(ws + s * rowlen + D + 1), w, L);
-            o = fmaf(__ldcg(ws + s * rowlen + d), w, o);
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, Ms[sp * G + g]);
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int sp = 0; sp < nsplit; ++sp) {
+            const float w = fast_exp2(Ms[sp * G + g] - M);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(ws0 + (size_t)sp * piece) + i4);
+            L = fmaf(Ls[sp * G + g], w, L);
+            acc.x = fmaf(v.x, w, acc.x);
+            acc.y = fmaf(v.y, w, acc.y);
+            acc.z = fmaf(v.z, w, acc.z);
+            acc.w = fmaf(v.w, w, acc.w);
         }
-        O[i] = L > 0.f ? o / L : 0.f;
+        float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (L > 0.f) r = make_float4(acc.x / L, acc.y / L, acc.z / L, acc.w / L);
+        reinterpret_cast<float4*>(O)[i4] = r;
     }
     if (tid == 0) *counter = 0u;  // every sibling has arrived: leave the counter reusable
 }
 
+// ------------------------------------------------------------------ work schedule
+// The units are the (sequence, KV head) pairs u = b * H_kv + h, laid end to end as one
+// array of cache blocks (unit u holds ceil(ctx_b / block_size) of them, starting at
+// P[b] + h * nblk_b with P the prefix over sequences of nblk * H_kv). CTA i streams blocks
+// [i c, (i+1) c) of that array, c = max(chunk_min, ceil(total / gridDim.x)), so every CTA
+// gets the same number of blocks whatever the context lengths. A CTA's range covers pieces
+// of one or more units; a unit cut by CTA boundaries is merged by log-sum-exp from its
+// pieces, which sit in workspace rows (CTA index + unit index): along the chain of pieces
+// that sum grows by at least one per piece, so the rows are distinct and fewer than
+// gridDim.x + units.
+struct DAItem {
+    int b, h;        // sequence, KV head
+    int lo, hi;      // cache blocks [lo, hi) of the unit
+    int ctx;         // the sequence's context length
+    int split, nsplit, slot0;
+};
+
+struct DASched {
+    int pos, end, c, b;  // flattened block range of this CTA; chunk; current sequence
+
+    // warp 0: clamped context lengths and the block prefix P[0..B] into shared memory
+    __device__ __forceinline__ static void scan(const DecodeAttnParams& p, int* P_s, int* ctx_s, int lane,
+                                                bool report) {
+        constexpr int PER = DA_MAX_B / 32;
+        int nb[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int b = k * 32 + lane;
+            nb[k] = 0;
+            if (b < p.B) {
+                const int ctx = da_context(p, b, report);
+                ctx_s[b] = ctx;
+                nb[k] = (ctx + p.block_size - 1) / p.block_size * p.H_kv;
+            }
+        }
+        int carry = 0;
+        if (lane == 0) P_s[0] = 0;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            if (k * 32 >= p.B) break;
+            int v = nb[k];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += t;
+            }
+            if (k * 32 + lane < p.B) P_s[k * 32 + lane + 1] = carry + v;
+            carry += __shfl_sync(0xffffffffu, v, 31);
+        }
+    }
+
+    __device__ __forceinline__ void init(const DecodeAttnParams& p, const int* P_s) {
+        if (p.unit_mode) {  // P_s[1] holds this unit's block count
+            b = (int)blockIdx.x / p.H_kv;
+            pos = 0;
+            end = P_s[1];
+            c = 0;
+            return;
+        }
+        const int total = P_s[p.B];
+        c = max(p.chunk_min, (total + (int)gridDim.x - 1) / (int)gridDim.x);
+        pos = min(total, (int)blockIdx.x * c);
+        end = min(total, pos + c);
+        // first sequence whose blocks reach past pos
+        int lo = 0, hi = p.B;  // P_s[lo] <= pos < P_s[hi] when pos < total
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (P_s[mid] <= pos) lo = mid; else hi = mid;
+        }
+        b = lo;
+    }
+
+    __device__ __forceinline__ bool next(const DecodeAttnParams& p, const int* P_s, const int* ctx_s, DAItem& it) {
+        if (pos >= end) return false;
+        if (c == 0) {  // unit mode: the whole unit, one piece
+            it.b = b;
+            it.h = (int)blockIdx.x % p.H_kv;
+            it.lo = 0;
+            it.hi = end;
+            it.ctx = ctx_s[0];
+            it.split = 0;
+            it.nsplit = 1;
+            it.slot0 = 0;
+            pos = end;
+            return true;
+        }
+        while (P_s[b + 1] <= pos) ++b;  // skips empty sequences
+        const int nb = (P_s[b + 1] - P_s[b]) / p.H_kv;
+        const int rel = pos - P_s[b];
+        it.b = b;
+        it.h = rel / nb;
+        it.lo = rel - it.h * nb;
+        it.hi = min(nb, it.lo + (end - pos));
+        it.ctx = ctx_s[b];
+        const int off = P_s[b] + it.h * nb;  // the unit's first block in the array
+        const int first = off / c;
+        it.nsplit = (off + nb - 1) / c - first + 1;
+        it.split = (int)blockIdx.x - first;
+        it.slot0 = first + b * p.H_kv + it.h;
+        pos += it.hi - it.lo;
+        return true;
+    }
+};
+
 // ------------------------------------------------------------------ the kernel
-// Grid (KV head, split, sequence): the CTA's warps merge through the ring's memory once the
-// producer is done.
-// TMA = true: the producer's lane 0 moves each cache block of the tile with two 3-D TMA loads
+// Grid: the balanced schedule's CTAs (or one per unit in unit mode). Warp 8 produces the
+// tiles of the CTA's items in order into the ring; warps 0..7 consume them, and at the end
+// of each item merge their partial softmax states through the ring stage of the item's last
+// tile, which they release only after the merge, so the producer keeps streaming the next
+// item into the other stages meanwhile.
+// TMA = true: the producer's lane 0 moves each cache block of a tile with two 3-D TMA loads
 // (box head_dim x 1 head x block_size tokens of a tensor map over [P * block_size, H_kv,
 // head_dim]) into the same dense rows, completion counted in bytes on the stage's barrier;
 // used when tiles hold whole blocks and the pool size is known. Otherwise the warp gathers
@@ -385,34 +530,11 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                    const DecodeAttnParams p) {
     using C = DACfg<G, D, KV>;
     extern __shared__ __align__(1024) unsigned char smem[];
-    // KV head fastest in the grid: the CTAs of one token range run side by side
-    const int kvh = blockIdx.x;
-    const int split = blockIdx.y;
-    const int b = blockIdx.z;
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-
-    griddep_wait();
-    griddep_launch();
-    // ---- this CTA's token range (whole blocks, as the reference splits, 13_decode_attn.cu:63-65)
-    const int ctx = da_context(p, b, tid == 0 && split == 0 && kvh == 0);
-    const int nblk = (ctx + p.block_size - 1) / p.block_size;
-    const int nsplit = (nblk + p.blocks_per_split - 1) / p.blocks_per_split;  // non-empty splits
-    const int hq0 = kvh * G;
-
-    if (nblk == 0) {  // empty context: O = 0 (reference reduce writes o * 0, 13_decode_attn.cu:48-52)
-        float* O = p.O + ((size_t)b * p.H_q + hq0) * D;
-        if (split == 0)
-            for (int i = tid; i < G * D; i += DA_NT) O[i] = 0.f;
-        return;
-    }
-    if (split >= nsplit) return;  // empty split: contributes nothing
-
-    const int tok_begin = split * p.blocks_per_split * p.block_size;
-    const int tok_end = min(ctx, (split + 1) * p.blocks_per_split * p.block_size);
-    const int ntiles = (tok_end - tok_begin + C::T - 1) / C::T;
-
+    int* P_s = reinterpret_cast<int*>(smem + C::OFF_P);
+    int* ctx_s = reinterpret_cast<int*>(smem + C::OFF_CTX);
     volatile unsigned int* misc = reinterpret_cast<volatile unsigned int*>(smem + C::OFF_MISC);
     const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -428,181 +550,258 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         misc[1] = 0;  // merge ticket
         fence_mbar_init();
     }
+    griddep_wait();  // everything above touches only this CTA's shared memory
+    griddep_launch();
+    if (p.unit_mode) {
+        if (tid == 0) {
+            const int b = (int)blockIdx.x / p.H_kv;
+            const int ctx = da_context(p, b, (int)blockIdx.x % p.H_kv == 0);
+            ctx_s[0] = ctx;
+            P_s[0] = 0;
+            P_s[1] = (ctx + p.block_size - 1) / p.block_size;
+        }
+    } else if (warp == 0) {
+        DASched::scan(p, P_s, ctx_s, lane, blockIdx.x == 0);
+    }
     __syncthreads();
 
-    if constexpr (TMA) {
-        if (warp == DA_NW) {
-            // the split's slice of the block table in shared memory (all lanes), then lane 0
-            // issues the copies
-            const int* btg = p.block_table + (size_t)b * p.num_blocks_per_seq;
-            const int blk0 = tok_begin / p.block_size;
-            const int nbt = (tok_end - 1) / p.block_size - blk0 + 1;
-            int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT);
-            const bool staged = nbt <= C::BT_CAP;
-            if (staged) {
-                for (int j = lane; j < nbt; j += 32) bt_s[j] = btg[blk0 + j];
-                __syncwarp();
-            }
-            if (lane == 0) {
-                prefetch_tensormap(&kmap);
-                prefetch_tensormap(&vmap);
-                const uint64_t pol = policy_evict_first();
-                const int bs = p.block_size;
-                const uint32_t block_bytes = (uint32_t)(bs * C::ROW);
-                int issued = 0;  // tiles whose copies were all requested
-                for (int i = 0; i < ntiles; ++i) {
-                    const int st = i % C::STAGES;
-                    if (i >= C::STAGES &&
-                        (misc[0] != 0 || !mbar_wait(empty_bar(st), ((i / C::STAGES) - 1) & 1, p.err))) {
-                        misc[0] = 1;
-                        break;
-                    }
-                    const int t0 = tok_begin + i * C::T;
-                    const int n = min(C::T, tok_end - t0);
-                    const int nb = (n + bs - 1) / bs;  // whole blocks (the last may run past the context)
-                    const uint32_t sK = ring + st * C::STAGE;
-                    mbar_arrive_expect_tx(full_bar(st), 2u * nb * block_bytes);
-                    for (int j = 0; j < nb; ++j) {
-                        int phys = staged ? bt_s[t0 / bs + j - blk0] : btg[t0 / bs + j];
-                        if ((unsigned)phys >= (unsigned)p.num_phys_blocks) {
-                            raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
-                            phys = 0;
-                        }
-                        tma_load_3d(sK + j * block_bytes, &kmap, 0, kvh, phys * bs, full_bar(st), pol);
-                        tma_load_3d(sK + C::T * C::ROW + j * block_bytes, &vmap, 0, kvh, phys * bs, full_bar(st), pol);
-                    }
-                    issued = i + 1;
-                }
-                // drain: the last fill of every stage this thread requested has landed before
-                // the CTA can exit, also when a consumer gave up waiting on one
-                for (int j = max(0, issued - C::STAGES); j < issued; ++j)
-                    mbar_wait_drain(full_bar(j % C::STAGES), (j / C::STAGES) & 1);
-            }
-            return;
+    DASched sc;
+    sc.init(p, P_s);
+    // empty contexts: O = 0 (reference reduce writes o * 0, 13_decode_attn.cuh:48-52)
+    if (p.unit_mode) {
+        if (sc.end == 0) {
+            float* O = p.O + ((size_t)sc.b * p.H_q + ((int)blockIdx.x % p.H_kv) * G) * D;
+            for (int i = tid; i < G * D; i += DA_NT) O[i] = 0.f;
         }
+    } else {
+        for (int b = blockIdx.x; b < p.B; b += gridDim.x)
+            if (ctx_s[b] == 0) {
+                float* O = p.O + (size_t)b * p.H_q * D;
+                for (int i = tid; i < p.H_q * D; i += DA_NT) O[i] = 0.f;
+            }
     }
+    if (sc.pos >= sc.end) return;  // no blocks for this CTA
+
+    const int bs = p.block_size;
     if (warp == DA_NW) {
         // ------------------------------------------------------------ producer warp
-        // The split's slice of the block table is staged in shared memory once, so no tile
-        // waits on a dependent global load (long splits fall back to global reads); every lane
-        // arrives on the stage's full barrier once its copies have landed.
-        const int* bt = p.block_table + (size_t)b * p.num_blocks_per_seq;
-        const int blk0 = tok_begin / p.block_size;
-        const int nbt = (tok_end - 1) / p.block_size - blk0 + 1;
+        // Each item's slice of the block table is staged in shared memory, so no tile waits on
+        // a dependent global load (slices longer than BT_CAP blocks are read from global).
         int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT);
-        const bool staged = nbt <= C::BT_CAP;
-        if (staged) {
-            for (int j = lane; j < nbt; j += 32) bt_s[j] = bt[blk0 + j];
-            __syncwarp();
-        }
         const uint64_t pol = policy_evict_first();
-        for (int i = 0; i < ntiles; ++i) {
-            const int st = i % C::STAGES;
-            if (i >= C::STAGES) {
-                const uint32_t par = ((i / C::STAGES) - 1) & 1;
-                bool ok = misc[0] == 0 && mbar_wait(empty_bar(st), par, p.err);
-                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-                if (!ok) { if (lane == 0) misc[0] = 1; break; }
-            }
-            const uint32_t sK = ring + st * C::STAGE;
-            da_issue_tile<C>(p, b, kvh, tok_begin, tok_end, i, sK, sK + C::T * C::ROW, bt_s, staged, lane, pol);
-            cp_async_mbar_arrive_noinc(full_bar(st));
+        if (TMA && lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
         }
-        cp_async_wait_all();  // nothing may still be landing in the ring when the warp exits
+        int issued = 0;  // tiles whose copies were all requested
+        bool ok = true;
+        DAItem it;
+        while (ok && sc.next(p, P_s, ctx_s, it)) {
+            const int* btg = p.block_table + (size_t)it.b * p.num_blocks_per_seq;
+            const int nbt = it.hi - it.lo;
+            const bool staged = nbt <= C::BT_CAP;
+            __syncwarp();  // the previous item's slice is no longer read
+            if (staged) {
+                for (int j = lane; j < nbt; j += 32) bt_s[j] = btg[it.lo + j];
+                __syncwarp();
+            }
+            const int tok_begin = it.lo * bs;
+            const int tok_end = min(it.ctx, it.hi * bs);
+            const int ntiles = (tok_end - tok_begin + C::T - 1) / C::T;
+            if constexpr (TMA) {
+                if (lane == 0) {
+                    const uint32_t block_bytes = (uint32_t)(bs * C::ROW);
+                    for (int i = 0; i < ntiles; ++i) {
+                        const int st = issued % C::STAGES;
+                        if (issued >= C::STAGES &&
+                            (misc[0] != 0 || !mbar_wait(empty_bar(st), ((issued / C::STAGES) - 1) & 1, p.err))) {
+                            misc[0] = 1;
+                            ok = false;
+                            break;
+                        }
+                        const int t0 = tok_begin + i * C::T;
+                        const int n = min(C::T, tok_end - t0);
+                        const int nb = (n + bs - 1) / bs;  // whole blocks (the last may run past the context)
+                        const uint32_t sK = ring + st * C::STAGE;
+                        mbar_arrive_expect_tx(full_bar(st), 2u * nb * block_bytes);
+                        for (int j = 0; j < nb; ++j) {
+                            const int blk = t0 / bs + j;
+                            int phys = staged ? bt_s[blk - it.lo] : btg[blk];
+                            if ((unsigned)phys >= (unsigned)p.num_phys_blocks) {
+                                raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
+                                phys = 0;
+                            }
+                            tma_load_3d(sK + j * block_bytes, &kmap, 0, it.h, phys * bs, full_bar(st), pol);
+                            tma_load_3d(sK + C::T * C::ROW + j * block_bytes, &vmap, 0, it.h, phys * bs,
+                                        full_bar(st), pol);
+                        }
+                        ++issued;
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            } else {
+                for (int i = 0; i < ntiles; ++i) {
+                    const int st = issued % C::STAGES;
+                    if (issued >= C::STAGES) {
+                        const uint32_t par = ((issued / C::STAGES) - 1) & 1;
+                        bool w_ok = misc[0] == 0 && mbar_wait(empty_bar(st), par, p.err);
+                        w_ok = __shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0) != 0;
+                        if (!w_ok) {
+                            if (lane == 0) misc[0] = 1;
+                            ok = false;
+                            break;
+                        }
+                    }
+                    const uint32_t sK = ring + st * C::STAGE;
+                    da_issue_tile<C>(p, it.b, it.h, tok_begin, tok_end, i, sK, sK + C::T * C::ROW, bt_s, staged,
+                                     lane, pol);
+                    cp_async_mbar_arrive_noinc(full_bar(st));
+                    ++issued;
+                }
+            }
+        }
+        if constexpr (TMA) {
+            // drain: the last fill of every stage this thread requested has landed before
+            // the CTA can exit, also when a consumer gave up waiting on one
+            if (lane == 0)
+                for (int j = max(0, issued - C::STAGES); j < issued; ++j)
+                    mbar_wait_drain(full_bar(j % C::STAGES), (j / C::STAGES) & 1);
+        } else {
+            cp_async_wait_all();  // nothing may still be landing in the ring when the warp exits
+        }
         return;
     }
 
     // ---------------------------------------------------------------- consumer warps
     constexpr int NC = DA_NW * 32;
     float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
+    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);           // [NW][G][2]
     DAWarp<G, D, KV> w;
-    w.begin(p, b, hq0, lane);
-    for (int i = 0; i < ntiles; ++i) {
-        const int st = i % C::STAGES;
-        const int n = min(C::T, tok_end - (tok_begin + i * C::T));
-        if (misc[0] == 0) {
-            if (!mbar_wait(full_bar(st), (i / C::STAGES) & 1, p.err)) misc[0] = 1;
+    int used = 0;  // tiles consumed
+    DAItem it;
+    while (sc.next(p, P_s, ctx_s, it)) {
+        w.begin(p, it.b, it.h * G, lane);
+        const int tok_begin = it.lo * bs;
+        const int tok_end = min(it.ctx, it.hi * bs);
+        const int ntiles = (tok_end - tok_begin + C::T - 1) / C::T;
+        int st = 0;
+        for (int i = 0; i < ntiles; ++i, ++used) {
+            st = used % C::STAGES;
+            const int n = min(C::T, tok_end - (tok_begin + i * C::T));
+            if (misc[0] == 0) {
+                if (!mbar_wait(full_bar(st), (used / C::STAGES) & 1, p.err)) misc[0] = 1;
+            }
+            const unsigned char* Kt = smem + st * C::STAGE;
+            w.tile(Kt, Kt + C::T * C::ROW, n, warp, lane, xw);
+            __syncwarp();
+            if (i + 1 < ntiles && lane == 0) mbar_arrive(empty_bar(st));
         }
-        const unsigned char* Kt = smem + st * C::STAGE;
-        w.tile(Kt, Kt + C::T * C::ROW, n, warp, lane, xw);
+
+        // ---- merge the 8 warps through the stage of the item's last tile (still held)
+        const float l_tot = w.l_total();
+        named_barrier(1, NC);  // every warp is done reading the stage
+        float* red = reinterpret_cast<float*>(smem + st * C::STAGE);  // [NW][G][D]
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < DAWarp<G, D, KV>::VP; ++j) {
+                red[(warp * G + g) * D + lane * C::VPL + 2 * j] = w.acc[g][j].x;
+                red[(warp * G + g) * D + lane * C::VPL + 2 * j + 1] = w.acc[g][j].y;
+            }
+        if (w.owner && w.my_t == 0) {
+            ml_s[(warp * G + w.my_g) * 2] = w.m_run;
+            ml_s[(warp * G + w.my_g) * 2 + 1] = l_tot;
+        }
+        // a wait that gave up sets the error bit and leaves O untouched; the decision is
+        // taken on the barrier's OR so that every consumer thread takes the same branch
+        const bool abort = named_barrier_or(1, NC, misc[0] != 0);
+        if (!abort) {
+            // log-sum-exp merge of the 8 warps for element i = g*D + d -> (o, M, L)
+            auto merge_warps = [&](int i, float& o, float& M, float& L) {
+                const int g = i / D;
+                M = -INFINITY;
+#pragma unroll
+                for (int v = 0; v < DA_NW; ++v) M = fmaxf(M, ml_s[(v * G + g) * 2]);
+                o = 0.f;
+                L = 0.f;
+                if (M == -INFINITY) return;
+#pragma unroll
+                for (int v = 0; v < DA_NW; ++v) {
+                    const float mw = ml_s[(v * G + g) * 2];
+                    if (mw == -INFINITY) continue;
+                    const float sc2 = fast_exp2(mw - M);
+                    o = fmaf(red[v * G * D + i], sc2, o);
+                    L = fmaf(ml_s[(v * G + g) * 2 + 1], sc2, L);
+                }
+            };
+            da_finish<G, D, NC>(p, it.b, it.h, it.split, it.nsplit, it.slot0, tid, misc + 1, red, merge_warps);
+        }
+        // The stage is refilled only after all 8 warps released it, and ml_s is next written
+        // after the next item's first barrier, which every warp reaches only when done here.
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(st));
+        if (abort) break;
     }
-
-    // ---- merge the 8 warps through the ring's memory (the producer is done with it)
-    const float l_tot = w.l_total();
-    named_barrier(1, NC);  // every warp is done reading the ring
-    float* red = reinterpret_cast<float*>(smem);               // [NW][G][D]
-    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);  // [NW][G][2]
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int j = 0; j < DAWarp<G, D, KV>::VP; ++j) {
-            red[(warp * G + g) * D + lane * C::VPL + 2 * j] = w.acc[g][j].x;
-            red[(warp * G + g) * D + lane * C::VPL + 2 * j + 1] = w.acc[g][j].y;
-        }
-    if (w.owner && w.my_t == 0) {
-        ml_s[(warp * G + w.my_g) * 2] = w.m_run;
-        ml_s[(warp * G + w.my_g) * 2 + 1] = l_tot;
-    }
-    named_barrier(1, NC);
-    if (misc[0] != 0) return;  // a wait gave up: the error bit is set, O is left untouched
-    // log-sum-exp merge of the 8 warps for element i = g*D + d -> (o, M, L)
-    auto merge_warps = [&](int i, float& o, float& M, float& L) {
-        const int g = i / D;
-        M = -INFINITY;
-#pragma unroll
-        for (int v = 0; v < DA_NW; ++v) M = fmaxf(M, ml_s[(v * G + g) * 2]);
-        o = 0.f;
-        L = 0.f;
-        if (M == -INFINITY) return;
-#pragma unroll
-        for (int v = 0; v < DA_NW; ++v) {
-            const float mw = ml_s[(v * G + g) * 2];
-            if (mw == -INFINITY) continue;
-            const float sc = fast_exp2(mw - M);
-            o = fmaf(red[v * G * D + i], sc, o);
-            L = fmaf(ml_s[(v * G + g) * 2 + 1], sc, L);
-        }
-    };
-    da_finish<G, D, NC>(p, b, kvh, split, nsplit, tid, misc + 1, merge_warps);
 }
 
 // ------------------------------------------------------------------ host side
 
-struct SplitPlan {
-    int num_splits;
-    int blocks_per_split;
+// Schedule of one launch (at most DA_MAX_B sequences). Balanced: `grid` CTAs, each streaming
+// an equal share of the batch's cache blocks (at least chunk_min of them), found on the device
+// from the actual context lengths; a unit cut across CTAs is merged through the workspace.
+// Unit mode: one CTA per (sequence, KV head), no workspace; used when the workspace cannot
+// hold the balanced plan's pieces.
+struct AttnPlan {
+    int grid;
+    int unit_mode;
+    int chunk_min;
 };
 
-// Split policy: enough CTAs to fill the GPU a few times over, and no CTA streaming more
-// than ~512 KB of K+V, so ragged batches balance; capped by max_splits and by a floor of
-// 64 tokens per split. When the
-// (sequence, KV head) pairs cannot fill the SMs (a shard of the heads on one of several
-// GPUs), CTAs shrink (down to 256 tokens) so that the upper bound B * H_kv * max_ctx of the
-// work spans ~4 waves of 3 CTAs per SM.
-static SplitPlan plan_splits(int B, int H_kv, int head_dim, int kv_bytes, int max_ctx, int block_size,
-                             int max_splits, int num_sms) {
-    const int max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
-    const long long pairs = (long long)B * H_kv;
-    const long long row_bytes = 2LL * head_dim * kv_bytes;           // K + V bytes per token
-    const long long cap_tok = (512LL * 1024) / row_bytes;
-    const long long waves_tok = pairs * max_ctx / (4LL * DA_MINB * num_sms);
-    const long long tok_per_cta =
-        pairs >= num_sms ? std::max<long long>(64, cap_tok)
-                         : std::max<long long>(256, std::min<long long>(waves_tok, cap_tok));
-    long long want = std::max<long long>((4LL * num_sms + pairs - 1) / pairs,
-                                         ((long long)max_ctx + tok_per_cta - 1) / tok_per_cta);
-    // at least 2 blocks and 64 tokens of work per split: below that a CTA's fixed start-up
-    // and the wider merge cost more than the parallelism gains (config 1, B1 H12 ctx 1024:
-    // 32 splits 8.2 us, 16 splits 7.2 us, 8 splits 7.1 us, 4 splits 8.9 us)
-    want = std::min<long long>(want, std::max(1, max_blocks / 2));
-    want = std::min<long long>(want, std::max(1, (max_ctx + 63) / 64));
-    want = std::max<long long>(1, std::min<long long>(want, max_splits));
-    SplitPlan sp;
-    sp.blocks_per_split = (int)((max_blocks + want - 1) / want);
-    sp.num_splits = (max_blocks + sp.blocks_per_split - 1) / sp.blocks_per_split;
-    return sp;
+// CTAs resident per SM (the kernel's launch bounds; the shared-memory ring allows as many)
+static int da_ctas_per_sm(int G) { return G >= 8 ? 2 : DA_MINB; }
+
+// Bytes of one workspace piece (da_piece_floats) and of the counters of U units.
+static size_t da_piece_bytes(int G, int D) { return (size_t)(G * D + ((2 * G + 3) & ~3)) * sizeof(float); }
+static size_t da_counter_bytes(long long U) { return ((size_t)U * sizeof(unsigned int) + 255) & ~(size_t)255; }
+
+// A CTA streams at least 128 tokens (and 2 blocks): below that its start-up and merge cost
+// more than the parallelism gains (config 1, B1 H12 ctx 1024: 64-token CTAs 7.2 us,
+// 128-token 7.1 us, 256-token 8.9 us).
+static int da_chunk_min(int block_size) { return std::max(2, (128 + block_size - 1) / block_size); }
+
+// Balanced grid wanted for a launch of Bc sequences: one CTA per resident slot, fewer when
+// the longest possible batch has fewer chunks.
+static long long da_grid_wanted(int Bc, int H_kv, int G, int max_ctx, int block_size, int num_sms) {
+    const long long max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
+    const long long chunks = ((long long)Bc * H_kv * max_blocks + da_chunk_min(block_size) - 1) / da_chunk_min(block_size);
+    // the final merge stages (M, L) of up to gridDim.x pieces per head in one 32 KB ring stage
+    const long long merge_cap = 4096 / G;
+    // one wave: 1.5, 2 and 3 waves of smaller CTAs measured 4-18% slower (config 3 and its
+    // 4- and 8-way head shards), each CTA adding its start-up and merge
+    const long long slots = (long long)da_ctas_per_sm(G) * num_sms;
+    return std::max(1LL, std::min<long long>(std::min<long long>(slots, chunks), merge_cap));
+}
+
+static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int max_ctx, int block_size, size_t ws_bytes,
+                          int num_sms) {
+    static const bool force_unit = getenv("B2_ATTN_PLAN") && strcmp(getenv("B2_ATTN_PLAN"), "unit") == 0;
+    const long long U = (long long)Bc * H_kv;
+    const long long want = da_grid_wanted(Bc, H_kv, G, max_ctx, block_size, num_sms);
+    const size_t cnt = da_counter_bytes(U);
+    const long long cap = ws_bytes > cnt ? (long long)((ws_bytes - cnt) / da_piece_bytes(G, D)) : 0;
+    AttnPlan pl;
+    pl.chunk_min = da_chunk_min(block_size);
+    // balanced when the workspace holds its pieces (grid + U rows) for a grid at least as
+    // wide as one CTA per unit would be (or as wanted, when that is narrower)
+    const long long g = std::min(want, cap - U);
+    if (!force_unit && g >= std::min(want, U) && g >= 1) {
+        pl.grid = (int)g;
+        pl.unit_mode = 0;
+    } else {
+        pl.grid = (int)U;
+        pl.unit_mode = 1;
+    }
+    return pl;
 }
 
 bool set_smem_attr_once(const void* func, int bytes, int slot);
@@ -659,9 +858,9 @@ static bool kv_map(CUtensorMap* map, const void* cache, long long tokens, int H_
 }
 
 template <int G, int D, typename KV>
-static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int B, cudaStream_t st) {
+static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int grid_x, cudaStream_t st) {
     using C = DACfg<G, D, KV>;
-    dim3 grid(prm.H_kv, prm.num_splits, B);
+    dim3 grid(grid_x);
     CUtensorMap km, vm;
     static const bool tma_off = getenv("B2_ATTN_TMA") && strcmp(getenv("B2_ATTN_TMA"), "0") == 0;
     const bool tma = !tma_off && prm.num_phys_blocks > 0 && prm.block_size <= 256 && C::T % prm.block_size == 0 &&
@@ -679,44 +878,30 @@ static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int B, cuda
 }
 
 template <int D, typename KV>
-static cudaError_t dispatch_group(int G, const DecodeAttnParams& prm, int B, cudaStream_t st) {
+static cudaError_t dispatch_group(int G, const DecodeAttnParams& prm, int grid, cudaStream_t st) {
     switch (G) {
-        case 1: return launch_decode_attn_t<1, D, KV>(prm, B, st);
-        case 2: return launch_decode_attn_t<2, D, KV>(prm, B, st);
-        case 4: return launch_decode_attn_t<4, D, KV>(prm, B, st);
-        case 8: return launch_decode_attn_t<8, D, KV>(prm, B, st);
+        case 1: return launch_decode_attn_t<1, D, KV>(prm, grid, st);
+        case 2: return launch_decode_attn_t<2, D, KV>(prm, grid, st);
+        case 4: return launch_decode_attn_t<4, D, KV>(prm, grid, st);
+        case 8: return launch_decode_attn_t<8, D, KV>(prm, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
 
-// Workspace layout: [B, H_q, num_splits, D+2] f32 partials, then [B, H_kv] u32 counters
-// (256-byte aligned).
-static size_t partial_bytes(int B, int H_q, int D, int S) {
-    size_t b = (size_t)B * H_q * S * (D + 2) * sizeof(float);
-    return (b + 255) & ~(size_t)255;
+// Workspace layout: the arrival counters of one launch's units (256-byte aligned), then the
+// piece rows [grid + units][G][D + 2] f32. Launches of a chunked batch reuse it in stream order.
+size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size) {
+    if (B <= 0 || H_kv <= 0 || H_q % H_kv != 0 || block_size <= 0) return 0;
+    const int G = H_q / H_kv;
+    const int Bc = std::min(B, DA_MAX_B);
+    const long long U = (long long)Bc * H_kv;
+    const long long g = da_grid_wanted(Bc, H_kv, G, max_ctx, block_size, num_sms_current_device());
+    return da_counter_bytes(U) + (size_t)(g + U) * da_piece_bytes(G, D);
 }
 
-
-// Largest split count whose workspace fits the allocation-free entry point's fixed array
-// (1 when not even two splits fit: a single split needs no workspace).
-int noalloc_max_splits(int B, int H_q, int H_kv, int D) {
-    if (B <= 0 || H_q <= 0 || H_kv <= 0 || D <= 0) return 1;
-    const size_t counters = (size_t)B * H_kv * sizeof(unsigned int);
-    int s = 64;
-    while (s > 1 && partial_bytes(B, H_q, D, s) + counters > (size_t)B2_DECODE_NOALLOC_SCRATCH_BYTES) --s;
-    return s;
-}
-
-size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size,
-                                  int max_splits, int kv_bytes) {
-    SplitPlan sp = plan_splits(B, H_kv, D, kv_bytes, max_ctx, block_size, max_splits, num_sms_current_device());
-    return partial_bytes(B, H_q, D, sp.num_splits) + (size_t)B * H_kv * sizeof(unsigned int);
-}
-
-// Validates, plans and launches. `max_splits` bounds the split count (the drop-in
-// wrapper passes the reference workspace's capacity). `counters_zeroed` false makes the
-// launcher clear the counter region first (stream-ordered memset).
-int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counters_zeroed, cudaStream_t st) {
+// Validates, plans and launches (in chunks of DA_MAX_B sequences). `counters_zeroed` false
+// makes the launcher clear the counter region first (stream-ordered memset).
+int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaStream_t st) {
     if (!a) return B2_ERR_INVALID;
     if (a->B < 0 || a->H_q <= 0 || a->H_kv <= 0 || a->block_size <= 0 || a->num_blocks_per_seq < 0 ||
         a->max_context_len < 0)
@@ -731,48 +916,56 @@ int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counte
     if (a->kv_dtype != B2_KV_F32 && a->kv_dtype != B2_KV_BF16) return B2_ERR_UNSUPPORTED;
     if (((uintptr_t)a->k_cache | (uintptr_t)a->v_cache) & 15) return B2_ERR_INVALID;  // bulk-copy alignment
     if (((uintptr_t)a->Q | (uintptr_t)a->O) & 15) return B2_ERR_INVALID;
+    if (a->workspace && ((uintptr_t)a->workspace & 255)) return B2_ERR_INVALID;
     const int kvb = a->kv_dtype == B2_KV_F32 ? 4 : 2;
+    const int D = a->head_dim;
+    const size_t ws_bytes = a->workspace ? a->workspace_bytes : 0;
+    const int sms = num_sms_current_device();
 
-    SplitPlan sp = plan_splits(a->B, a->H_kv, a->head_dim, kvb, a->max_context_len, a->block_size, max_splits,
-                               num_sms_current_device());
     DecodeAttnParams prm;
-    prm.Q = a->Q;
     prm.k_cache = static_cast<const unsigned char*>(a->k_cache);
     prm.v_cache = static_cast<const unsigned char*>(a->v_cache);
-    prm.block_table = a->block_table;
-    prm.context_lens = a->context_lens;
-    prm.O = a->O;
     prm.H_q = a->H_q;
     prm.H_kv = a->H_kv;
     prm.block_size = a->block_size;
     prm.num_blocks_per_seq = a->num_blocks_per_seq;
     prm.num_phys_blocks = a->num_phys_blocks;
-    prm.num_splits = sp.num_splits;
-    prm.blocks_per_split = sp.blocks_per_split;
-    const float scale = a->scale != 0.f ? a->scale : 1.0f / sqrtf((float)a->head_dim);
+    const float scale = a->scale != 0.f ? a->scale : 1.0f / sqrtf((float)D);
     prm.scale_log2 = scale * 1.4426950408889634f;
     prm.err = device_error_ptr();
-    prm.ws_partial = nullptr;
-    prm.ws_counter = nullptr;
-    if (sp.num_splits > 1) {
-        const size_t pb = partial_bytes(a->B, a->H_q, a->head_dim, sp.num_splits);
-        const size_t need = pb + (size_t)a->B * a->H_kv * sizeof(unsigned int);
-        if (!a->workspace || a->workspace_bytes < need) return B2_ERR_WORKSPACE;
-        if ((uintptr_t)a->workspace & 255) return B2_ERR_INVALID;
-        prm.ws_partial = static_cast<float*>(a->workspace);
-        prm.ws_counter = reinterpret_cast<unsigned int*>(static_cast<char*>(a->workspace) + pb);
-        if (!counters_zeroed) {
-            if (cudaMemsetAsync(prm.ws_counter, 0, (size_t)a->B * a->H_kv * sizeof(unsigned int), st) !=
-                cudaSuccess)
-                return B2_ERR_CUDA;
+    bool zeroed = counters_zeroed;
+    for (int b0 = 0; b0 < a->B; b0 += DA_MAX_B) {
+        const int Bc = std::min(DA_MAX_B, a->B - b0);
+        const AttnPlan pl = plan_attn(Bc, a->H_kv, G, D, a->max_context_len, a->block_size, ws_bytes, sms);
+        prm.Q = a->Q + (size_t)b0 * a->H_q * D;
+        prm.O = a->O + (size_t)b0 * a->H_q * D;
+        prm.block_table = a->block_table + (size_t)b0 * a->num_blocks_per_seq;
+        prm.context_lens = a->context_lens + b0;
+        prm.B = Bc;
+        prm.chunk_min = pl.chunk_min;
+        prm.unit_mode = pl.unit_mode;
+        prm.ws_partial = nullptr;
+        prm.ws_counter = nullptr;
+        if (!pl.unit_mode) {
+            const size_t cnt = da_counter_bytes((long long)Bc * a->H_kv);
+            prm.ws_counter = static_cast<unsigned int*>(a->workspace);
+            prm.ws_partial = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + cnt);
+            if (!zeroed) {
+                // counters end every launch at zero, so one clear serves all chunks
+                if (cudaMemsetAsync(a->workspace, 0, cnt, st) != cudaSuccess) return B2_ERR_CUDA;
+                zeroed = true;
+            }
         }
+        cudaError_t e;
+        if (D == 64)
+            e = kvb == 4 ? dispatch_group<64, float>(G, prm, pl.grid, st)
+                         : dispatch_group<64, __nv_bfloat16>(G, prm, pl.grid, st);
+        else
+            e = kvb == 4 ? dispatch_group<128, float>(G, prm, pl.grid, st)
+                         : dispatch_group<128, __nv_bfloat16>(G, prm, pl.grid, st);
+        if (e != cudaSuccess) return B2_ERR_CUDA;
     }
-    cudaError_t e;
-    if (a->head_dim == 64)
-        e = kvb == 4 ? dispatch_group<64, float>(G, prm, a->B, st) : dispatch_group<64, __nv_bfloat16>(G, prm, a->B, st);
-    else
-        e = kvb == 4 ? dispatch_group<128, float>(G, prm, a->B, st) : dispatch_group<128, __nv_bfloat16>(G, prm, a->B, st);
-    return e == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    return B2_OK;
 }
 
 }  // namespace b2
@@ -812,12 +1005,10 @@ extern "C" int b2_decode_attn_noalloc(const b2_decode_attn_args* args, b2_stream
     b2_decode_attn_args a = *args;
     a.workspace = scratch;
     a.workspace_bytes = B2_DECODE_NOALLOC_SCRATCH_BYTES;
-    // The split count is capped by what the fixed array holds: the largest S whose partials
-    // [B, H_q, S, d+2] plus the [B, H_kv] counters fit, at most b2_decode_attn's cap of 64.
-    // A plan with one split uses no scratch, so no shape is refused for its size; large
-    // batches simply run with fewer splits. The arrival counters are cleared with a
+    // The schedule is planned against what the fixed array holds: when the balanced plan's
+    // pieces do not fit, each (sequence, KV head) runs whole in one CTA, which needs no
+    // scratch, so no shape is refused for its size. The arrival counters are cleared with a
     // stream-ordered memset on every call, since the array keeps whatever the previous
     // call left in it.
-    return b2::decode_attn_launch(&a, b2::noalloc_max_splits(a.B, a.H_q, a.H_kv, a.head_dim),
-                                  false, static_cast<cudaStream_t>(stream));
+    return b2::decode_attn_launch(&a, false, static_cast<cudaStream_t>(stream));
 }

@@ -21,9 +21,8 @@
 
 namespace b2 {
 
-int decode_attn_launch(const b2_decode_attn_args* a, int max_splits, bool counters_zeroed, cudaStream_t st);
-size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size, int max_splits,
-                                  int kv_bytes);
+int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaStream_t st);
+size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size);
 int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st);
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
                 const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
@@ -262,7 +261,7 @@ int alloc_runtime(b2_engine* e) {
     e->xf_hi = e->alloc<uint16_t>((size_t)B * d);
     e->xf_lo = e->alloc<uint16_t>((size_t)B * d);
     e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, e->Hl, e->Hl, c.d_head, c.max_seq_len,
-                                                                         kBlock, 64, 4));
+                                                                         kBlock));
     e->attn_ws = e->alloc<unsigned char>(e->attn_ws_bytes);
     if (e->failed) return B2_ERR_CUDA;
     if (!e->k_pool || !e->v_pool || !e->attn_ws || !e->logits) return B2_ERR_CUDA;
@@ -518,7 +517,7 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
             B2_TRY(launch_prefill_attention(R.items, R.n_items, Hl, dh, e->kv_dtype, R.q, kc, vc, R.block_table,
                                             e->blocks_per_seq, kBlock, R.pos, R.attn, st));
         else
-            B2_TRY(decode_attn_launch(&a, 64, true, st));
+            B2_TRY(decode_attn_launch(&a, true, st));
         if (tp) {
             B2_TRY(row_parallel(R.attn, dl, L.out, "gemm_out"));
         } else {
@@ -1040,7 +1039,7 @@ int b2_engine_prefill(b2_engine* e, b2_stream_t stream) {
         e->pf_xq = e->alloc<int32_t>((size_t)cap * std::max(d, c.d_ff) / 4);
         e->pf_acc32 = e->alloc<int32_t>((size_t)cap * d);
         e->pf_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(cap, e->Hl, e->Hl, c.d_head, c.max_seq_len,
-                                                                          kBlock, 64, 4));
+                                                                          kBlock));
         e->pf_ws = e->alloc<unsigned char>(e->pf_ws_bytes);
         if (e->failed || cudaMemset(e->pf_ws, 0, e->pf_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
         e->pf_cap = cap;

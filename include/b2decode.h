@@ -70,7 +70,7 @@ typedef struct {
     int kv_dtype;                    /* B2_KV_F32 or B2_KV_BF16 */
     const int* block_table;          /* [B, num_blocks_per_seq] */
     const int* context_lens;         /* [B] (device) */
-    int max_context_len;             /* host upper bound of context_lens; sizes the split count */
+    int max_context_len;             /* host upper bound of context_lens; sizes the workspace */
     int block_size;                  /* tokens per KV block (engine: 16) */
     int num_blocks_per_seq;          /* block-table row stride */
     int num_phys_blocks;             /* P, for device bounds checks; 0 = unchecked */
@@ -80,18 +80,22 @@ typedef struct {
     size_t workspace_bytes;
 } b2_decode_attn_args;
 
-/* Bytes of workspace b2_decode_attn needs for these shapes. The workspace holds per-split
- * partial results and one arrival counter per (sequence, KV head). The counters must be
- * zero before the first call (cudaMemset once); every call leaves them zero again.
- * The size is that of the split plan for an fp32 cache; a bf16 cache plans at most as many
- * splits, so this size serves both element types. A shape that plans a single split needs
- * no workspace at all (workspace may then be NULL).
+/* Bytes of workspace b2_decode_attn needs for these shapes (either KV element type). The
+ * kernel gives every CTA an equal share of the batch's cache blocks, found on the device
+ * from context_lens, so one (sequence, KV head) may be cut across CTAs; the workspace holds
+ * one arrival counter per (sequence, KV head) of a launch (at the start, 256-byte aligned)
+ * and the cut pieces' partial results. The counters must be zero before the first call
+ * (cudaMemset once); every call leaves them zero again. With no workspace (NULL) or one too
+ * small for the balanced schedule, each (sequence, KV head) runs whole in one CTA, which
+ * needs none (slower when few long sequences cannot fill the GPU). Batches above 256
+ * sequences run as several launches that reuse the workspace.
  * Replaces the caller-side sizing `B*H_q*DA_MAX_SPLITS*(d+2)` floats
  * (reference src/gpt2_engine.cu:156, tests/test_decode_attention.cu:91). */
 size_t b2_decode_attn_workspace_size(int B, int H_q, int H_kv, int head_dim,
                                      int max_context_len, int block_size);
 
-/* Split-K paged decode attention, one launch (split merge fused into the kernel).
+/* Split-K paged decode attention, one launch per 256 sequences (split merge fused into the
+ * kernel).
  * Replaces run_decode_attn (reference kernels/decode/13_decode_attn.cu:84-109). */
 int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream);
 
@@ -105,13 +109,11 @@ int b2_decode_attn(const b2_decode_attn_args* args, b2_stream_t stream);
  * a workspace buffer of their own.
  *   - The caller still passes Q, the caches, the block table, context_lens and O;
  *     args->workspace and args->workspace_bytes are ignored.
- *   - The split workspace is a file-scope device array of B2_DECODE_NOALLOC_SCRATCH_BYTES
- *     held by every GPU that loads the library until the process exits. The split count is
- *     the one b2_decode_attn would plan, capped at the largest S whose partials
- *     (B * H_q * S * (head_dim + 2) floats, rounded up to 256 bytes) plus B * H_kv 4-byte
- *     counters fit the array. One split needs no workspace, so no shape is refused for its
- *     size: a batch too large for the default plan runs with fewer splits (slower on long
- *     contexts, same results within fp32 rounding).
+ *   - The workspace is a file-scope device array of B2_DECODE_NOALLOC_SCRATCH_BYTES held by
+ *     every GPU that loads the library until the process exits, planned like a caller
+ *     workspace of that size: when the balanced schedule's pieces do not fit, each
+ *     (sequence, KV head) runs whole in one CTA, which needs none, so no shape is refused
+ *     for its size (slower on few long sequences, same results within fp32 rounding).
  *   - The first call on each device looks up the array's device address; make that first
  *     call before any stream capture that should contain this entry point. Each kernel
  *     variant (GQA group, head_dim, KV dtype) also sets its shared-memory limit on its own

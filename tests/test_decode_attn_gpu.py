@@ -328,3 +328,74 @@ def test_bench_workload_full_size_against_oracle(b2, oracle, cuda, kv):
     tol = F32_TOL if kv == "f32" else BF16_TOL
     np.testing.assert_allclose(got, want, **tol)
     np.testing.assert_allclose(got_na, want, **tol)
+
+
+def _run_abi(b2, torch, device, q, kc, vc, bt, lens, max_ctx, ws_bytes):
+    """b2_decode_attn through the C ABI with a caller workspace of ws_bytes (0: none)."""
+    tq, tk, tv, tbt, tl = (to_dev(torch, a, device) for a in (q, kc, vc, bt, lens))
+    O = torch.full_like(tq, float("nan"))
+    ws = torch.zeros(max(256, ws_bytes), dtype=torch.uint8, device=device)
+    kvt = b2.B2_KV_BF16 if tk.dtype == torch.bfloat16 else b2.B2_KV_F32
+    B, H_q, d = tq.shape
+    a = b2.DecodeAttnArgs(B, H_q, tk.shape[2], d, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), kvt,
+                          tbt.data_ptr(), tl.data_ptr(), int(max_ctx), tk.shape[1], tbt.shape[1], tk.shape[0],
+                          0.0, O.data_ptr(), ws.data_ptr() if ws_bytes else None, ws_bytes)
+    assert b2.load_library().b2_decode_attn(ctypes.byref(a), None) == b2.B2_OK
+    torch.cuda.synchronize()
+    assert b2.device_error() == 0
+    return O.cpu().numpy()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_balanced_schedule_cuts_and_groups_units(b2, oracle, cuda, dtype):
+    """Config-4 shape (B64, 12 heads, d64, contexts 100-260 with some empty): the balanced
+    schedule gives each CTA an equal share of the blocks, so CTAs hold several short
+    (sequence, head) units and units are cut across CTAs; every result matches the oracle,
+    equals the one-CTA-per-unit schedule (no workspace) within rounding, and a second call
+    reproduces the first bit for bit (counters back at zero)."""
+    import torch
+
+    rng = np.random.default_rng(64)
+    lens = rng.integers(100, 261, 64)
+    lens[[3, 17, 40]] = 0
+    q, kc, vc, bt, lens = random_paged(rng, 64, 12, 12, 64, lens, dtype=dtype)
+    want = oracle.decode_attn(q, kc, vc, bt, lens, nthreads=0)
+    tol = F32_TOL if dtype == "f32" else BF16_TOL
+    max_ctx = 1024
+    need = b2.decode_attn_workspace_size(64, 12, 12, 64, max_ctx)
+    got = _run_abi(b2, torch, cuda, q, kc, vc, bt, lens, max_ctx, need)
+    np.testing.assert_allclose(got, want, **tol)
+    assert np.all(got[[3, 17, 40]] == 0)
+    again = _run_abi(b2, torch, cuda, q, kc, vc, bt, lens, max_ctx, need)
+    np.testing.assert_array_equal(got, again)
+    whole = _run_abi(b2, torch, cuda, q, kc, vc, bt, lens, max_ctx, 0)
+    np.testing.assert_allclose(whole, want, **tol)
+    np.testing.assert_allclose(whole, got, rtol=1e-5, atol=1e-6)
+
+
+def test_balanced_schedule_few_long_sequences(b2, oracle, cuda):
+    """Two long sequences and one short, one KV head of G 4 (a head shard): each long unit is
+    cut into many equal pieces merged through the workspace; matches the oracle."""
+    import torch
+
+    rng = np.random.default_rng(8)
+    lens = [6000, 33, 8192]
+    q, kc, vc, bt, lens = random_paged(rng, 3, 4, 1, 128, lens)
+    want = oracle.decode_attn(q, kc, vc, bt, lens, nthreads=0)
+    need = b2.decode_attn_workspace_size(3, 4, 1, 128, 8192)
+    got = _run_abi(b2, torch, cuda, q, kc, vc, bt, lens, 8192, need)
+    np.testing.assert_allclose(got, want, **F32_TOL)
+
+
+def test_batch_above_one_launch(b2, oracle, cuda):
+    """300 sequences run as two launches (256 + 44) that reuse one workspace; empty and
+    one-token contexts included."""
+    import torch
+
+    rng = np.random.default_rng(300)
+    lens = rng.integers(0, 90, 300)
+    lens[[0, 255, 256, 299]] = [0, 1, 0, 89]
+    q, kc, vc, bt, lens = random_paged(rng, 300, 4, 2, 64, lens)
+    want = oracle.decode_attn(q, kc, vc, bt, lens, nthreads=0)
+    got = run_b2(b2, torch, cuda, q, kc, vc, bt, lens)
+    np.testing.assert_allclose(got, want, **F32_TOL)

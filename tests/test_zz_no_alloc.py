@@ -92,13 +92,13 @@ def test_noalloc_matches_oracle_and_workspace_entry_point(b2, oracle, cuda, case
 
 @pytest.mark.parametrize("bf16", [False, True])
 def test_noalloc_caps_splits_to_the_scratch(b2, oracle, cuda, bf16):
-    """A batch whose default split plan needs more workspace than the fixed array holds runs
-    with fewer splits (here a single one, which needs no scratch) and still matches."""
+    """A batch whose balanced schedule needs more workspace than the fixed array holds runs
+    each (sequence, KV head) whole in one CTA, which needs no scratch, and still matches."""
     import torch
 
-    B, H_q, H_kv, d, max_ctx = 256, 64, 8, 128, 32768
+    B, H_q, H_kv, d, max_ctx = 256, 128, 16, 128, 32768
     assert b2.decode_attn_workspace_size(B, H_q, H_kv, d, max_ctx) > b2.DECODE_NOALLOC_SCRATCH_BYTES
-    lens = np.random.default_rng(9).integers(0, 200, B)
+    lens = np.random.default_rng(9).integers(0, 100, B)
     q, kc, vc, bt, lens = _inputs(77, B, H_q, H_kv, d, lens, bf16)
     _check_two_calls(b2, torch, cuda, oracle, q, kc, vc, bt, lens, max_ctx, BF16_TOL if bf16 else F32_TOL)
 
