@@ -841,6 +841,39 @@ def run_only(args):
         ws = b2.make_decode_workspace(Bw, Hw, Hw, D, mcw, BS, device=dev)
         fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, mcw, O=O, workspace=ws)  # noqa: E731
         by = attn_alg_bytes(np.full(Bw, ctxw), Hw, Hw, D, 2, nb)
+    elif args.only == "attn_gpt2":
+        # config 4's per-layer attention: B64, 12 heads x 64, fp32 KV, every sequence at the
+        # same context (B2_GPT2_CTX, default 192: the middle of the 128 decode steps); twelve
+        # caches (one per layer) are cycled so that, as in the decode step, the KV is not
+        # L2-resident between launches
+        import numpy as np
+
+        ctx = int(os.environ.get("B2_GPT2_CTX", "192"))
+        Bg, Hg, Dg, NL = 64, 12, 64, 12
+        nb = (ctx + BS - 1) // BS
+        P = Bg * nb
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        caches = [(torch.randn(P, BS, Hg, Dg, generator=g, device=dev),
+                   torch.randn(P, BS, Hg, Dg, generator=g, device=dev)) for _ in range(NL)]
+        q = torch.randn(Bg, Hg, Dg, device=dev)
+        O = torch.empty_like(q)
+        btd = torch.randperm(P, generator=g, device=dev).to(torch.int32).view(Bg, nb)
+        lensd = torch.full((Bg,), ctx, dtype=torch.int32, device=dev)
+        ws = b2.make_decode_workspace(Bg, Hg, Hg, Dg, 1024, BS, device=dev)
+        it = [0]
+
+        def fn():
+            kc, vc = caches[it[0] % NL]
+            it[0] += 1
+            b2.decode_attn(q, kc, vc, btd, lensd, 1024, O=O, workspace=ws)
+
+        by = attn_alg_bytes(np.full(Bg, ctx), Hg, Hg, Dg, 4, nb)
+        graph = graph_of(torch, lambda: [fn() for _ in range(NL)])
+        ms = time_steps(torch, graph.replay, max(1, args.steps // NL), args.warmup) / NL
+        steps = max(1, args.steps // NL)
+        print(f"attn_gpt2 ctx {ctx}: {ms / steps * 1e3:.2f} us/launch, {by / (ms / steps * 1e-3) / 1e9:.1f} GB/s "
+              "(12 caches cycled; not a bench value)", flush=True)
+        return
     elif args.only.startswith("attn"):
         dt = torch.bfloat16 if args.only == "attn_bf16" else torch.float32
         # B2_ATTN_SHARD=n: the KV-head shard one rank of n holds (the per-rank launch of --gpus n)
@@ -875,7 +908,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--only", default=None,
-                    choices=["attn", "attn_bf16", "attn_wide", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
+                    choices=["attn", "attn_bf16", "attn_wide", "attn_gpt2", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
                     help="run one workload for a few steps with no JSON line (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -791,10 +791,16 @@ static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int max_ctx, int block
     const long long cap = ws_bytes > cnt ? (long long)((ws_bytes - cnt) / da_piece_bytes(G, D)) : 0;
     AttnPlan pl;
     pl.chunk_min = da_chunk_min(block_size);
+    // Short units that fill the GPU 1.5 times or more by themselves run one CTA per unit:
+    // cutting and grouping them costs more in item merges than the last wave loses (GPT-2
+    // Small layer, B64 x 12 heads, contexts 129-256 with max_context_len 1024: 16.1-21.4 us
+    // per launch one CTA per unit, 19.1-25.0 us balanced).
+    const long long max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
+    const bool short_units = max_blocks <= 64 && 2 * U >= 3LL * da_ctas_per_sm(G) * num_sms;
     // balanced when the workspace holds its pieces (grid + U rows) for a grid at least as
     // wide as one CTA per unit would be (or as wanted, when that is narrower)
     const long long g = std::min(want, cap - U);
-    if (!force_unit && g >= std::min(want, U) && g >= 1) {
+    if (!force_unit && !short_units && g >= std::min(want, U) && g >= 1) {
         pl.grid = (int)g;
         pl.unit_mode = 0;
     } else {
