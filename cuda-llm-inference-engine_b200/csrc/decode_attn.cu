@@ -61,31 +61,36 @@ struct DecodeAttnParams {
 
 constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
 
-template <int G, int D, typename KV>
+// GR: independent warp groups per CTA, each streaming its own unit through its own half of
+// the ring (GR = 2 for short units: two units per CTA, so a GPT-2 layer's 768 units fit in
+// one wave of 3 CTAs per SM).
+template <int G, int D, typename KV, int GR = 1>
 struct DACfg {
     static constexpr int ES = (int)sizeof(KV);
     static constexpr int ROW = D * ES;                 // bytes of one K or V row
-    // tokens per tile: about 32 KB of K+V per tile whatever the element size
-    static constexpr int T = (16384 / ROW) < 32 ? 32 : ((16384 / ROW) > 128 ? 128 : (16384 / ROW));
+    static constexpr int NWG = DA_NW / GR;             // consumer warps per group
+    // tokens per tile: about 32 KB of K+V per tile (per CTA) whatever the element size
+    static constexpr int T1 = (16384 / ROW) < 32 ? 32 : ((16384 / ROW) > 128 ? 128 : (16384 / ROW));
+    static constexpr int T = T1 / GR;
     static constexpr int STAGE = 2 * T * ROW;          // K tile then V tile, rows dense
-    static constexpr int STAGES_RAW = (64 * 1024) / STAGE;  // 64 KB ring: 3 CTAs per SM
+    static constexpr int STAGES_RAW = (64 * 1024) / (GR * STAGE);  // 64 KB ring: 3 CTAs per SM
     static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
     static constexpr int VPL = D / 32;                 // head_dim columns per lane
-    static constexpr int TW = T / DA_NW;               // tokens of a tile per consumer warp
+    static constexpr int TW = T / NWG;                 // tokens of a tile per consumer warp
     // tokens per consumer group: as many as keep TPW * G <= 16 dot products per reduction
     static constexpr int TPW = (16 / G) < TW ? (16 / G) : TW;
     // shared-memory carve-up (bytes)
-    static constexpr int OFF_X = STAGES * STAGE;                         // f32 [NW][32] p / alpha exchange
+    static constexpr int OFF_X = GR * STAGES * STAGE;                    // f32 [NW][32] p / alpha exchange
     static constexpr int OFF_ML = OFF_X + DA_NW * 32 * 4;                // f32 [NW][G][2]
     static constexpr int OFF_BT = OFF_ML + DA_NW * G * 2 * 4;            // i32 [BT_CAP] block-table slice
-    static constexpr int BT_CAP = 256;
+    static constexpr int BT_CAP = 256;                                   // (BT_CAP / GR per group)
     static constexpr int OFF_P = OFF_BT + BT_CAP * 4;                    // i32 [DA_MAX_B + 1] block prefix
     static constexpr int OFF_CTX = OFF_P + (DA_MAX_B + 4) * 4;           // i32 [DA_MAX_B] context lengths
     static constexpr int OFF_MISC = OFF_CTX + DA_MAX_B * 4;              // u32 flags
-    static constexpr int OFF_BAR = (OFF_MISC + 16 + 7) & ~7;             // u64 full[S], empty[S]
-    static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8;
+    static constexpr int OFF_BAR = (OFF_MISC + 16 + 7) & ~7;             // u64 full[GR][S], empty[GR][S]
+    static constexpr int SMEM = OFF_BAR + 2 * GR * STAGES * 8;
     static_assert(D % 32 == 0, "head_dim must be 64 or 128");
-    static_assert(DA_NW * G * D * 4 <= STAGE, "the warps' merge must fit one ring stage");
+    static_assert(NWG * G * D * 4 <= STAGE, "the warps' merge must fit one ring stage");
     static_assert(TW % TPW == 0 && T % 32 == 0, "tile must split evenly over the consumer warps");
 };
 
@@ -218,9 +223,9 @@ __device__ __forceinline__ void da_issue_tile(const DecodeAttnParams& p, int b, 
 // a token group are reduced across the warp with a transposed butterfly (about one shuffle
 // per dot product), p and alpha are exchanged through warp-private shared memory, and no
 // CTA-wide barrier is taken inside the tile loop.
-template <int G, int D, typename KV>
+template <int G, int D, typename KV, int GR = 1>
 struct DAWarp {
-    using C = DACfg<G, D, KV>;
+    using C = DACfg<G, D, KV, GR>;
     static constexpr int VP = C::VPL / 2;  // q and the accumulator as fp32 pairs (packed f32x2 FMA)
     static constexpr int TPW = C::TPW;     // tokens per group
     static constexpr int NV = TPW * G;     // dot products per group (<= 16)
@@ -744,6 +749,172 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     }
 }
 
+// Two units per CTA (unit mode, TMA producer only): consumer warps 0-3 serve unit
+// 2 * blockIdx.x and warps 4-7 unit 2 * blockIdx.x + 1, each group through its own half of
+// the ring with its own barriers; lanes 0 and 1 of the producer warp feed the two groups
+// independently. For short units (a few hundred tokens) whose count exceeds one wave of
+// CTAs: the GPU streams every unit at once instead of in 1.7 waves.
+template <int G, int D, typename KV>
+__global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
+decode_attn_pair_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        const DecodeAttnParams p) {
+    using C = DACfg<G, D, KV, 2>;
+    constexpr int NWG = C::NWG;
+    constexpr int NCG = NWG * 32;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    int* ctx_s = reinterpret_cast<int*>(smem + C::OFF_CTX);  // [2] context of each group's unit (-1: none)
+    volatile unsigned int* misc = reinterpret_cast<volatile unsigned int*>(smem + C::OFF_MISC);
+    const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
+    auto full_bar = [&](int gr, int s) { return bar0 + 8u * (gr * C::STAGES + s); };
+    auto empty_bar = [&](int gr, int s) { return bar0 + 8u * (2 * C::STAGES + gr * C::STAGES + s); };
+    auto stage = [&](int gr, int s) { return (gr * C::STAGES + s) * C::STAGE; };
+    const int U = p.B * p.H_kv;
+
+    if (tid == 0) {
+        for (int gr = 0; gr < 2; ++gr)
+            for (int s = 0; s < C::STAGES; ++s) {
+                mbar_init(full_bar(gr, s), 1);
+                mbar_init(empty_bar(gr, s), NWG);
+            }
+        misc[0] = 0;  // abort flag
+        misc[1] = 0;  // merge tickets (one per group; unused: a unit is never cut here)
+        misc[2] = 0;
+        fence_mbar_init();
+    }
+    griddep_wait();  // everything above touches only this CTA's shared memory
+    griddep_launch();
+    if (tid < 2) {
+        const int u = (int)blockIdx.x * 2 + tid;
+        ctx_s[tid] = u < U ? da_context(p, u / p.H_kv, u % p.H_kv == 0) : -1;
+    }
+    __syncthreads();
+    // empty contexts: O = 0 (reference reduce writes o * 0, 13_decode_attn.cuh:48-52)
+    for (int gr = 0; gr < 2; ++gr)
+        if (ctx_s[gr] == 0) {
+            const int u = (int)blockIdx.x * 2 + gr;
+            float* O = p.O + ((size_t)(u / p.H_kv) * p.H_q + (u % p.H_kv) * G) * D;
+            for (int i = tid; i < G * D; i += DA_NT) O[i] = 0.f;
+        }
+
+    const int bs = p.block_size;
+    if (warp == DA_NW) {
+        // ------------------------------------------------------------ producer lanes 0, 1
+        if (lane < 2 && ctx_s[lane] > 0) {
+            const int gr = lane;
+            const int u = (int)blockIdx.x * 2 + gr;
+            const int b = u / p.H_kv, h = u % p.H_kv;
+            const int ctx = ctx_s[gr];
+            const int nb = (ctx + bs - 1) / bs;
+            const int* btg = p.block_table + (size_t)b * p.num_blocks_per_seq;
+            int* bt_s = reinterpret_cast<int*>(smem + C::OFF_BT) + gr * (C::BT_CAP / 2);
+            const bool staged = nb <= C::BT_CAP / 2;
+            if (staged)
+                for (int j = 0; j < nb; ++j) bt_s[j] = btg[j];  // independent loads, one latency
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+            const uint64_t pol = policy_evict_first();
+            const uint32_t block_bytes = (uint32_t)(bs * C::ROW);
+            const uint32_t ring = smem_u32(smem);
+            const int ntiles = (ctx + C::T - 1) / C::T;
+            int issued = 0;
+            for (int i = 0; i < ntiles; ++i) {
+                const int st = i % C::STAGES;
+                if (i >= C::STAGES &&
+                    (misc[0] != 0 || !mbar_wait(empty_bar(gr, st), ((i / C::STAGES) - 1) & 1, p.err))) {
+                    misc[0] = 1;
+                    break;
+                }
+                const int t0 = i * C::T;
+                const int n = min(C::T, ctx - t0);
+                const int nbt = (n + bs - 1) / bs;
+                const uint32_t sK = ring + stage(gr, st);
+                mbar_arrive_expect_tx(full_bar(gr, st), 2u * nbt * block_bytes);
+                for (int j = 0; j < nbt; ++j) {
+                    const int blk = t0 / bs + j;
+                    int phys = staged ? bt_s[blk] : btg[blk];
+                    if ((unsigned)phys >= (unsigned)p.num_phys_blocks) {
+                        raise_error(p.err, B2_DEVERR_BLOCK_RANGE);
+                        phys = 0;
+                    }
+                    tma_load_3d(sK + j * block_bytes, &kmap, 0, h, phys * bs, full_bar(gr, st), pol);
+                    tma_load_3d(sK + C::T * C::ROW + j * block_bytes, &vmap, 0, h, phys * bs, full_bar(gr, st), pol);
+                }
+                issued = i + 1;
+            }
+            // drain: the last fill of every stage requested has landed before exit
+            for (int j = max(0, issued - C::STAGES); j < issued; ++j)
+                mbar_wait_drain(full_bar(gr, j % C::STAGES), (j / C::STAGES) & 1);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumer groups
+    const int gr = warp / NWG;
+    const int wl = warp - gr * NWG;
+    const int ctx = ctx_s[gr];
+    if (ctx <= 0) return;  // the whole group leaves together
+    const int u = (int)blockIdx.x * 2 + gr;
+    const int b = u / p.H_kv, h = u % p.H_kv;
+    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
+    float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);           // [NW][G][2]
+    DAWarp<G, D, KV, 2> w;
+    w.begin(p, b, h * G, lane);
+    const int ntiles = (ctx + C::T - 1) / C::T;
+    int st = 0;
+    for (int i = 0; i < ntiles; ++i) {
+        st = i % C::STAGES;
+        const int n = min(C::T, ctx - i * C::T);
+        if (misc[0] == 0) {
+            if (!mbar_wait(full_bar(gr, st), (i / C::STAGES) & 1, p.err)) misc[0] = 1;
+        }
+        const unsigned char* Kt = smem + stage(gr, st);
+        w.tile(Kt, Kt + C::T * C::ROW, n, wl, lane, xw);
+        __syncwarp();
+        if (i + 1 < ntiles && lane == 0) mbar_arrive(empty_bar(gr, st));
+    }
+    // merge the group's warps through the stage of its last tile (still held)
+    const float l_tot = w.l_total();
+    named_barrier(1 + gr, NCG);
+    float* red = reinterpret_cast<float*>(smem + stage(gr, st));  // [NWG][G][D]
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DAWarp<G, D, KV, 2>::VP; ++j) {
+            red[(wl * G + g) * D + lane * C::VPL + 2 * j] = w.acc[g][j].x;
+            red[(wl * G + g) * D + lane * C::VPL + 2 * j + 1] = w.acc[g][j].y;
+        }
+    if (w.owner && w.my_t == 0) {
+        ml_s[(warp * G + w.my_g) * 2] = w.m_run;
+        ml_s[(warp * G + w.my_g) * 2 + 1] = l_tot;
+    }
+    const bool abort = named_barrier_or(1 + gr, NCG, misc[0] != 0);
+    if (!abort) {
+        auto merge_warps = [&](int i, float& o, float& M, float& L) {
+            const int g = i / D;
+            M = -INFINITY;
+#pragma unroll
+            for (int v = 0; v < NWG; ++v) M = fmaxf(M, ml_s[((gr * NWG + v) * G + g) * 2]);
+            o = 0.f;
+            L = 0.f;
+            if (M == -INFINITY) return;
+#pragma unroll
+            for (int v = 0; v < NWG; ++v) {
+                const float mw = ml_s[((gr * NWG + v) * G + g) * 2];
+                if (mw == -INFINITY) continue;
+                const float sc2 = fast_exp2(mw - M);
+                o = fmaf(red[v * G * D + i], sc2, o);
+                L = fmaf(ml_s[((gr * NWG + v) * G + g) * 2 + 1], sc2, L);
+            }
+        };
+        da_finish<G, D, NCG>(p, b, h, 0, 1, 0, tid - gr * NCG, misc + 1 + gr, red, merge_warps);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar(gr, st));
+}
+
 // ------------------------------------------------------------------ host side
 
 // Schedule of one launch (at most DA_MAX_B sequences). Balanced: `grid` CTAs, each streaming
@@ -755,6 +926,7 @@ struct AttnPlan {
     int grid;
     int unit_mode;
     int chunk_min;
+    int pair;  // unit mode with two units per CTA (decode_attn_pair_kernel), when TMA is usable
 };
 
 // CTAs resident per SM (the kernel's launch bounds; the shared-memory ring allows as many)
@@ -800,12 +972,16 @@ static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int max_ctx, int block
     // balanced when the workspace holds its pieces (grid + U rows) for a grid at least as
     // wide as one CTA per unit would be (or as wanted, when that is narrower)
     const long long g = std::min(want, cap - U);
+    pl.pair = 0;
     if (!force_unit && !short_units && g >= std::min(want, U) && g >= 1) {
         pl.grid = (int)g;
         pl.unit_mode = 0;
     } else {
         pl.grid = (int)U;
         pl.unit_mode = 1;
+        // short units of head_dim 64 stream two per CTA (one wave instead of 1.5 or more)
+        static const bool pair_off = getenv("B2_ATTN_PAIR") && strcmp(getenv("B2_ATTN_PAIR"), "0") == 0;
+        pl.pair = short_units && D == 64 && !pair_off;
     }
     return pl;
 }
@@ -864,9 +1040,8 @@ static bool kv_map(CUtensorMap* map, const void* cache, long long tokens, int H_
 }
 
 template <int G, int D, typename KV>
-static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int grid_x, cudaStream_t st) {
+static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, const AttnPlan& pl, cudaStream_t st) {
     using C = DACfg<G, D, KV>;
-    dim3 grid(grid_x);
     CUtensorMap km, vm;
     static const bool tma_off = getenv("B2_ATTN_TMA") && strcmp(getenv("B2_ATTN_TMA"), "0") == 0;
     const bool tma = !tma_off && prm.num_phys_blocks > 0 && prm.block_size <= 256 && C::T % prm.block_size == 0 &&
@@ -874,22 +1049,33 @@ static cudaError_t launch_decode_attn_t(const DecodeAttnParams& prm, int grid_x,
                                 prm.block_size) &&
                      kv_map<KV>(&vm, prm.v_cache, (long long)prm.num_phys_blocks * prm.block_size, prm.H_kv, D,
                                 prm.block_size);
+    if constexpr (D == 64) {  // the pair variant's half tiles need head_dim 64
+        using C2 = DACfg<G, D, KV, 2>;
+        if (tma && pl.pair && pl.unit_mode && C2::T % prm.block_size == 0) {
+            if (!set_smem_attr_once((const void*)decode_attn_pair_kernel<G, D, KV>, C2::SMEM, 0))
+                return cudaErrorInvalidValue;
+            return launch_kernel(decode_attn_pair_kernel<G, D, KV>, dim3((pl.grid + 1) / 2), dim3(DA_NT),
+                                 (size_t)C2::SMEM, st, km, vm, prm);
+        }
+    }
     if (tma) {
         if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV, true>, C::SMEM, 0)) return cudaErrorInvalidValue;
-        return launch_kernel(decode_attn_kernel<G, D, KV, true>, grid, dim3(DA_NT), (size_t)C::SMEM, st, km, vm, prm);
+        return launch_kernel(decode_attn_kernel<G, D, KV, true>, dim3(pl.grid), dim3(DA_NT), (size_t)C::SMEM, st, km,
+                             vm, prm);
     }
     memset(&km, 0, sizeof(km));
     if (!set_smem_attr_once((const void*)decode_attn_kernel<G, D, KV, false>, C::SMEM, 0)) return cudaErrorInvalidValue;
-    return launch_kernel(decode_attn_kernel<G, D, KV, false>, grid, dim3(DA_NT), (size_t)C::SMEM, st, km, km, prm);
+    return launch_kernel(decode_attn_kernel<G, D, KV, false>, dim3(pl.grid), dim3(DA_NT), (size_t)C::SMEM, st, km, km,
+                         prm);
 }
 
 template <int D, typename KV>
-static cudaError_t dispatch_group(int G, const DecodeAttnParams& prm, int grid, cudaStream_t st) {
+static cudaError_t dispatch_group(int G, const DecodeAttnParams& prm, const AttnPlan& pl, cudaStream_t st) {
     switch (G) {
-        case 1: return launch_decode_attn_t<1, D, KV>(prm, grid, st);
-        case 2: return launch_decode_attn_t<2, D, KV>(prm, grid, st);
-        case 4: return launch_decode_attn_t<4, D, KV>(prm, grid, st);
-        case 8: return launch_decode_attn_t<8, D, KV>(prm, grid, st);
+        case 1: return launch_decode_attn_t<1, D, KV>(prm, pl, st);
+        case 2: return launch_decode_attn_t<2, D, KV>(prm, pl, st);
+        case 4: return launch_decode_attn_t<4, D, KV>(prm, pl, st);
+        case 8: return launch_decode_attn_t<8, D, KV>(prm, pl, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -964,11 +1150,11 @@ int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaS
         }
         cudaError_t e;
         if (D == 64)
-            e = kvb == 4 ? dispatch_group<64, float>(G, prm, pl.grid, st)
-                         : dispatch_group<64, __nv_bfloat16>(G, prm, pl.grid, st);
+            e = kvb == 4 ? dispatch_group<64, float>(G, prm, pl, st)
+                         : dispatch_group<64, __nv_bfloat16>(G, prm, pl, st);
         else
-            e = kvb == 4 ? dispatch_group<128, float>(G, prm, pl.grid, st)
-                         : dispatch_group<128, __nv_bfloat16>(G, prm, pl.grid, st);
+            e = kvb == 4 ? dispatch_group<128, float>(G, prm, pl, st)
+                         : dispatch_group<128, __nv_bfloat16>(G, prm, pl, st);
         if (e != cudaSuccess) return B2_ERR_CUDA;
     }
     return B2_OK;

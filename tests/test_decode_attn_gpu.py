@@ -361,7 +361,7 @@ def test_balanced_schedule_cuts_and_groups_units(b2, oracle, cuda, dtype):
     q, kc, vc, bt, lens = random_paged(rng, 64, 12, 12, 64, lens, dtype=dtype)
     want = oracle.decode_attn(q, kc, vc, bt, lens, nthreads=0)
     tol = F32_TOL if dtype == "f32" else BF16_TOL
-    max_ctx = 1024
+    max_ctx = 2048  # long enough a bound that the balanced schedule is planned
     need = b2.decode_attn_workspace_size(64, 12, 12, 64, max_ctx)
     got = _run_abi(b2, torch, cuda, q, kc, vc, bt, lens, max_ctx, need)
     np.testing.assert_allclose(got, want, **tol)
@@ -399,3 +399,24 @@ def test_batch_above_one_launch(b2, oracle, cuda):
     want = oracle.decode_attn(q, kc, vc, bt, lens, nthreads=0)
     got = run_b2(b2, torch, cuda, q, kc, vc, bt, lens)
     np.testing.assert_allclose(got, want, **F32_TOL)
+
+
+@pytest.mark.parametrize("G,dtype", [(1, "f32"), (2, "f32"), (1, "bf16")])
+def test_two_units_per_cta(b2, oracle, cuda, G, dtype):
+    """Short units that fill the GPU 1.5 times (max_context_len <= 1024, head_dim 64) run two
+    per CTA: an odd unit count (61 x 11 KV heads), empty and one-token contexts, blocks not
+    filling the last tile; matches the oracle."""
+    import torch
+
+    rng = np.random.default_rng(61 + G)
+    B, H_kv = 61, 11
+    lens = rng.integers(1, 300, B)
+    lens[[0, 30]] = 0
+    lens[5] = 1
+    q, kc, vc, bt, lens = random_paged(rng, B, G * H_kv, H_kv, 64, lens, dtype=dtype)
+    want = oracle.decode_attn(q, kc, vc, bt, lens, nthreads=0)
+    tol = F32_TOL if dtype == "f32" else BF16_TOL
+    need = b2.decode_attn_workspace_size(B, G * H_kv, H_kv, 64, 1024)
+    got = _run_abi(b2, torch, cuda, q, kc, vc, bt, lens, 1024, need)
+    np.testing.assert_allclose(got, want, **tol)
+    assert np.all(got[[0, 30]] == 0)
