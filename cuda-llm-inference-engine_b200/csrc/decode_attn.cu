@@ -54,6 +54,7 @@ struct DecodeAttnParams {
     int B;                      // sequences of this launch (<= DA_MAX_B)
     int H_q, H_kv, block_size, num_blocks_per_seq, num_phys_blocks;
     int chunk_min;              // fewest cache blocks a CTA streams (balanced plan)
+    int unit_cost;              // blocks' worth of time a CTA spends starting and merging a unit
     int unit_mode;              // 1: CTA u serves (sequence, KV head) unit u whole, no workspace
     float scale_log2;           // softmax scale * log2(e)
     unsigned int* err;          // device error word
@@ -446,7 +447,8 @@ struct DASched {
             if (b < p.B) {
                 const int ctx = da_context(p, b, report);
                 ctx_s[b] = ctx;
-                nb[k] = (ctx + p.block_size - 1) / p.block_size * p.H_kv;
+                const int nblk = (ctx + p.block_size - 1) / p.block_size;
+                nb[k] = (nblk > 0 ? nblk + p.unit_cost : 0) * p.H_kv;
             }
         }
         int carry = 0;
@@ -500,21 +502,33 @@ struct DASched {
             pos = end;
             return true;
         }
-        while (P_s[b + 1] <= pos) ++b;  // skips empty sequences
-        const int nb = (P_s[b + 1] - P_s[b]) / p.H_kv;
-        const int rel = pos - P_s[b];
-        it.b = b;
-        it.h = rel / nb;
-        it.lo = rel - it.h * nb;
-        it.hi = min(nb, it.lo + (end - pos));
-        it.ctx = ctx_s[b];
-        const int off = P_s[b] + it.h * nb;  // the unit's first block in the array
-        const int first = off / c;
-        it.nsplit = (off + nb - 1) / c - first + 1;
-        it.split = (int)blockIdx.x - first;
-        it.slot0 = first + b * p.H_kv + it.h;
-        pos += it.hi - it.lo;
-        return true;
+        // Each unit occupies unit_cost cost-only positions before its blocks, so a CTA that
+        // starts (and merges) a unit streams correspondingly fewer blocks; a range holding
+        // only such positions of a unit has no piece of it.
+        while (pos < end) {
+            while (P_s[b + 1] <= pos) ++b;  // skips empty sequences
+            const int nbv = (P_s[b + 1] - P_s[b]) / p.H_kv;  // positions per unit of sequence b
+            const int rel = pos - P_s[b];
+            const int h = rel / nbv;
+            const int vlo = rel - h * nbv;
+            const int vhi = min(nbv, vlo + (end - pos));
+            pos += vhi - vlo;
+            const int lo = max(0, vlo - p.unit_cost), hi = max(0, vhi - p.unit_cost);
+            if (hi <= lo) continue;
+            const int nb = nbv - p.unit_cost;
+            it.b = b;
+            it.h = h;
+            it.lo = lo;
+            it.hi = hi;
+            it.ctx = ctx_s[b];
+            const int off = P_s[b] + h * nbv + p.unit_cost;  // the unit's first block in the array
+            const int first = off / c;
+            it.nsplit = (off + nb - 1) / c - first + 1;
+            it.split = (int)blockIdx.x - first;
+            it.slot0 = first + b * p.H_kv + h;
+            return true;
+        }
+        return false;
     }
 };
 
@@ -926,6 +940,7 @@ struct AttnPlan {
     int grid;
     int unit_mode;
     int chunk_min;
+    int unit_cost;  // cost-only blocks charged per unit (balanced schedule)
     int pair;  // unit mode with two units per CTA (decode_attn_pair_kernel), when TMA is usable
 };
 
@@ -954,8 +969,8 @@ static long long da_grid_wanted(int Bc, int H_kv, int G, int max_ctx, int block_
     return std::max(1LL, std::min<long long>(std::min<long long>(slots, chunks), merge_cap));
 }
 
-static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int max_ctx, int block_size, size_t ws_bytes,
-                          int num_sms) {
+static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int kv_bytes, int max_ctx, int block_size,
+                          size_t ws_bytes, int num_sms) {
     static const bool force_unit = getenv("B2_ATTN_PLAN") && strcmp(getenv("B2_ATTN_PLAN"), "unit") == 0;
     const long long U = (long long)Bc * H_kv;
     const long long want = da_grid_wanted(Bc, H_kv, G, max_ctx, block_size, num_sms);
@@ -963,6 +978,14 @@ static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int max_ctx, int block
     const long long cap = ws_bytes > cnt ? (long long)((ws_bytes - cnt) / da_piece_bytes(G, D)) : 0;
     AttnPlan pl;
     pl.chunk_min = da_chunk_min(block_size);
+    // A CTA spends ~4 us starting and merging each unit it touches (q load, warp merge,
+    // partial write, fence and ticket), about what it streams of ~56 KB of K+V at its
+    // one-CTA-per-slot share of HBM: that many blocks are charged per unit (8-way head shard
+    // of config 3: 36.3 -> 34.8 us; CTAs holding two units no longer finish last). Taking
+    // the tickets in one batch at the end of each CTA instead was measured slower (36.1 us,
+    // config 3 bf16 146 -> 151 us): the final merges then all land in the kernel's tail.
+    const int block_bytes = 2 * block_size * D * kv_bytes;
+    pl.unit_cost = std::max(0, (56 * 1024 + block_bytes / 2) / block_bytes);
     // Short units that fill the GPU 1.5 times or more by themselves run one CTA per unit:
     // cutting and grouping them costs more in item merges than the last wave loses (GPT-2
     // Small layer, B64 x 12 heads, contexts 129-256 with max_context_len 1024: 16.1-21.4 us
@@ -1128,13 +1151,14 @@ int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaS
     bool zeroed = counters_zeroed;
     for (int b0 = 0; b0 < a->B; b0 += DA_MAX_B) {
         const int Bc = std::min(DA_MAX_B, a->B - b0);
-        const AttnPlan pl = plan_attn(Bc, a->H_kv, G, D, a->max_context_len, a->block_size, ws_bytes, sms);
+        const AttnPlan pl = plan_attn(Bc, a->H_kv, G, D, kvb, a->max_context_len, a->block_size, ws_bytes, sms);
         prm.Q = a->Q + (size_t)b0 * a->H_q * D;
         prm.O = a->O + (size_t)b0 * a->H_q * D;
         prm.block_table = a->block_table + (size_t)b0 * a->num_blocks_per_seq;
         prm.context_lens = a->context_lens + b0;
         prm.B = Bc;
         prm.chunk_min = pl.chunk_min;
+        prm.unit_cost = pl.unit_mode ? 0 : pl.unit_cost;
         prm.unit_mode = pl.unit_mode;
         prm.ws_partial = nullptr;
         prm.ws_counter = nullptr;
