@@ -841,6 +841,31 @@ def run_only(args):
         ws = b2.make_decode_workspace(Bw, Hw, Hw, D, mcw, BS, device=dev)
         fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, mcw, O=O, workspace=ws)  # noqa: E731
         by = attn_alg_bytes(np.full(Bw, ctxw), Hw, Hw, D, 2, nb)
+    elif args.only == "attn_c1":
+        # MHA B1 H12 d64 ctx 1024, 64-block random permutation, 40 rotated
+        # copies (250 MB) in one graph, as the default run's secondary line
+        import numpy as np
+
+        rng = np.random.default_rng(SEED)
+        copies = 40
+        bt1 = torch.from_numpy(rng.permutation(64).astype(np.int32).reshape(1, 64)).to(dev)
+        l1 = torch.tensor([1024], dtype=torch.int32, device=dev)
+        sets = [(torch.randn(64, 16, 12, 64, device=dev), torch.randn(64, 16, 12, 64, device=dev),
+                 torch.randn(1, 12, 64, device=dev)) for _ in range(copies)]
+        O1 = torch.empty(1, 12, 64, device=dev)
+        ws1 = b2.make_decode_workspace(1, 12, 12, 64, 1024, 16)
+        it = [0]
+
+        def fn1():
+            k, v, qq = sets[it[0] % copies]
+            it[0] += 1
+            b2.decode_attn(qq, k, v, bt1, l1, 1024, O=O1, workspace=ws1)
+
+        graph = graph_of(torch, lambda: [fn1() for _ in range(copies)])
+        steps = max(1, args.steps // copies)
+        ms = time_steps(torch, graph.replay, steps, args.warmup) / copies
+        print(f"attn_c1: {ms / steps * 1e3:.2f} us/launch (40 copies rotated; not a bench value)", flush=True)
+        return
     elif args.only == "attn_gpt2":
         # config 4's per-layer attention: B64, 12 heads x 64, fp32 KV, every sequence at the
         # same context (B2_GPT2_CTX, default 192: the middle of the 128 decode steps); twelve
@@ -908,7 +933,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--only", default=None,
-                    choices=["attn", "attn_bf16", "attn_wide", "attn_gpt2", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
+                    choices=["attn", "attn_bf16", "attn_wide", "attn_gpt2", "attn_c1", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
                     help="run one workload for a few steps with no JSON line (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -343,7 +343,7 @@ constexpr int da_piece_floats() { return G * D + ((2 * G + 3) & ~3); }
 // element i = g*D + d. A unit in one piece: O = o / L. Otherwise the piece goes to workspace
 // row `slot0 + split` and the last of the unit's nsplit pieces to arrive (atomic ticket on
 // the unit's counter) merges all of them into O and leaves the counter at zero. `scratch`
-// (shared memory, >= 2 * nsplit * G floats) may alias what `get` reads.
+// (shared memory, >= 2 * nsplit * G + 4 * NC floats) may alias what `get` reads.
 template <int G, int D, int NC, typename Get>
 __device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int kvh, int split, int nsplit,
                                           int slot0, int tid, volatile unsigned int* ticket, float* scratch,
@@ -391,22 +391,40 @@ __device__ __forceinline__ void da_finish(const DecodeAttnParams& p, int b, int 
         Ls[j] = __ldcg(ml + 1);
     }
     named_barrier(1, NC);
-    // each thread merges 4 consecutive outputs of one head with 16-byte loads
-    for (int i4 = tid; i4 < G * D / 4; i4 += NC) {
+    // Outputs in groups of 4 (NQ of them); the NC threads form SG piece groups, thread
+    // (sg, i4) summing pieces sg, sg + SG, ... of group i4 with 16-byte loads, so the loads of
+    // all pieces are in flight together; the SG partial sums then meet in shared memory.
+    constexpr int NQ = G * D / 4;
+    constexpr int SG = NC / NQ > 0 ? NC / NQ : 1;
+    float4* part = reinterpret_cast<float4*>(scratch + ((2 * nsplit * G + 3) & ~3));  // [SG][NQ]
+    for (int j = tid; j < SG * NQ; j += NC) {
+        const int sg = j / NQ, i4 = j - sg * NQ;
         const int g = (i4 * 4) / D;
         float M = -INFINITY;
         for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, Ms[sp * G + g]);
-        float L = 0.f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-        for (int sp = 0; sp < nsplit; ++sp) {
+        for (int sp = sg; sp < nsplit; sp += SG) {
             const float w = fast_exp2(Ms[sp * G + g] - M);
             const float4 v = __ldcg(reinterpret_cast<const float4*>(ws0 + (size_t)sp * piece) + i4);
-            L = fmaf(Ls[sp * G + g], w, L);
             acc.x = fmaf(v.x, w, acc.x);
             acc.y = fmaf(v.y, w, acc.y);
             acc.z = fmaf(v.z, w, acc.z);
             acc.w = fmaf(v.w, w, acc.w);
+        }
+        part[j] = acc;
+    }
+    named_barrier(1, NC);
+    for (int i4 = tid; i4 < NQ; i4 += NC) {
+        const int g = (i4 * 4) / D;
+        float M = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, Ms[sp * G + g]);
+        float L = 0.f;
+        for (int sp = 0; sp < nsplit; ++sp) L = fmaf(Ls[sp * G + g], fast_exp2(Ms[sp * G + g] - M), L);
+        float4 acc = part[i4];
+        for (int k = 1; k < SG; ++k) {
+            const float4 v = part[k * NQ + i4];
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
         }
         float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
         if (L > 0.f) r = make_float4(acc.x / L, acc.y / L, acc.z / L, acc.w / L);
@@ -962,7 +980,7 @@ static long long da_grid_wanted(int Bc, int H_kv, int G, int max_ctx, int block_
     const long long max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
     const long long chunks = ((long long)Bc * H_kv * max_blocks + da_chunk_min(block_size) - 1) / da_chunk_min(block_size);
     // the final merge stages (M, L) of up to gridDim.x pieces per head in one 32 KB ring stage
-    const long long merge_cap = 4096 / G;
+    const long long merge_cap = 3584 / G;  // 2 grid G floats of (M, L) + 4 KB of partial sums
     // one wave: 1.5, 2 and 3 waves of smaller CTAs measured 4-18% slower (config 3 and its
     // 4- and 8-way head shards), each CTA adding its start-up and merge
     const long long slots = (long long)da_ctas_per_sm(G) * num_sms;
@@ -985,7 +1003,11 @@ static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int kv_bytes, int max_
     // the tickets in one batch at the end of each CTA instead was measured slower (36.1 us,
     // config 3 bf16 146 -> 151 us): the final merges then all land in the kernel's tail.
     const int block_bytes = 2 * block_size * D * kv_bytes;
-    pl.unit_cost = std::max(0, (56 * 1024 + block_bytes / 2) / block_bytes);
+    // Charged only when the grid fills every slot: a narrower grid (short batches such as
+    // config 1) gives each CTA more than a slot's share, and there the charge cut pieces
+    // finer than the units' own shape (config 1: 10.7 us with it, 8.9 without).
+    pl.unit_cost = want >= (long long)da_ctas_per_sm(G) * num_sms
+                       ? std::max(0, (56 * 1024 + block_bytes / 2) / block_bytes) : 0;
     // Short units that fill the GPU 1.5 times or more by themselves run one CTA per unit:
     // cutting and grouping them costs more in item merges than the last wave loses (GPT-2
     // Small layer, B64 x 12 heads, contexts 129-256 with max_context_len 1024: 16.1-21.4 us
