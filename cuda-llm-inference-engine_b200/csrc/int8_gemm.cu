@@ -594,14 +594,18 @@ constexpr int P2_BN = 256;                         // accumulator columns per CT
 constexpr int P2_OFF_BAR = P2_STAGES * P2_STAGE;
 constexpr int P2_NBAR = 2 * P2_STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], drain
 constexpr int P2_OFF_COL = P2_OFF_BAR + P2_NBAR * 8 + 16;
-// epilogue staging: per epilogue warp 2 buffers of 32 rows x 32 fp32 (128-byte swizzled)
+// 8 epilogue warps (2-9): warp w reads TMEM lanes 32 (w % 4) .. +32 (its quadrant), warps 2-5
+// columns 0-127 and warps 6-9 columns 128-255 of the accumulator
+constexpr int P2_EPI_WARPS = 8;
+constexpr int P2_THREADS = (2 + P2_EPI_WARPS) * 32;
+// epilogue staging: per epilogue warp one buffer of 32 rows x 32 fp32 (128-byte swizzled)
 constexpr int P2_OFF_EPI = (P2_OFF_COL + 2 * P2_BN * 4 + 1023) & ~1023;
 constexpr int P2_EPI_BUF = 32 * 32 * 4;
-constexpr int P2_SMEM = P2_OFF_EPI + 4 * 2 * P2_EPI_BUF + 1024;
+constexpr int P2_SMEM = P2_OFF_EPI + P2_EPI_WARPS * P2_EPI_BUF + 1024;
 constexpr uint32_t P2_TMEM_COLS = 2 * P2_BN;
 
 template <int EPI, bool S32>
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(P2_THREADS, 1)
 int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                      const __grid_constant__ CUtensorMap mapC, const GemmParams p, const int c_tma) {
     extern __shared__ unsigned char smem_raw[];
@@ -634,7 +638,7 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(accf_bar(a), 1);
-            mbar_init(acce_bar(a), 8);  // 4 epilogue warps x 2 CTAs
+            mbar_init(acce_bar(a), 2 * P2_EPI_WARPS);  // epilogue warps x 2 CTAs
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -719,24 +723,27 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
         }
         __syncwarp();
     } else {
+        constexpr int NE = P2_EPI_WARPS * 32;
         const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;  // column half of the accumulator
         const int et = threadIdx.x - 64;
         float* sB_s = reinterpret_cast<float*>(smem + P2_OFF_COL);
         float* bias_s = sB_s + P2_BN;
         const uint32_t lead_acce0 = mapa_shared(acce_bar(0), 0), lead_acce1 = mapa_shared(acce_bar(1), 0);
+        unsigned char* buf = smem + P2_OFF_EPI + (warp - 2) * P2_EPI_BUF;
         int j = 0;
         for (int t = pair; t < num_tiles; t += npairs, ++j) {
             const int a = j & 1, u = j >> 1;
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, mt, nt);
             if constexpr (!S32) {
-                for (int c = et; c < P2_BN; c += 128) {
+                for (int c = et; c < P2_BN; c += NE) {
                     const int n = nt * P2_BN + c;
                     sB_s[c] = n < p.N ? __ldg(p.scale_B + n) : 0.f;
                     if (EPI != B2_EPI_PLAIN) bias_s[c] = n < p.N ? __ldg(p.bias + n) : 0.f;
                 }
             }
-            named_barrier(2, 128);
+            named_barrier(2, NE);
             const bool ok = !*abort_flag && mbar_wait(accf_bar(a), u & 1, p.err);
             if (!ok) *abort_flag = 1;
             tc_fence_after();
@@ -745,37 +752,43 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
             const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
             const uint32_t tbase = tmem + a * P2_BN + ((uint32_t)(quad * 32) << 16);
             const int row0 = mt * 2 * P2_ROWS + (int)rank * P2_ROWS + quad * 32;  // this warp's first row
-            unsigned char* stage_w = smem + P2_OFF_EPI + (warp - 2) * 2 * P2_EPI_BUF;
-#pragma unroll 1
-            for (int c = 0; c < P2_BN / 16; c += 2) {
-                uint32_t r0[16], r1[16];
-                tmem_ld16(tbase + (uint32_t)(c * 16), r0);
-                tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
-                tmem_ld_wait();
-                const int n = nt * P2_BN + c * 16;
-                float rs0[16], rs1[16];
+            // 32-column chunks c0 = 8 half .. 8 half + 7 (in 16-column units): the next chunk's
+            // TMEM load is in flight while this one is converted and stored
+            constexpr int NCH = P2_BN / 32 / 2;  // chunks per warp
+            uint32_t r[2][2][16];
+            tmem_ld16(tbase + (uint32_t)(half * NCH * 32), r[0][0]);
+            tmem_ld16(tbase + (uint32_t)(half * NCH * 32 + 16), r[0][1]);
+            tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) { rs0[i] = 0.f; rs1[i] = 0.f; }
+            for (int k = 0; k < NCH; ++k) {
+                const int cc = half * NCH + k;  // 32-column chunk index in the tile
+                if (k + 1 < NCH) {
+                    tmem_ld16(tbase + (uint32_t)((cc + 1) * 32), r[(k + 1) & 1][0]);
+                    tmem_ld16(tbase + (uint32_t)((cc + 1) * 32 + 16), r[(k + 1) & 1][1]);
+                }
+                uint32_t (&rc)[2][16] = r[k & 1];
+                const int n = nt * P2_BN + cc * 32;
+                float rs[2][16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { rs[0][i] = 0.f; rs[1][i] = 0.f; }
                 if constexpr (EPI == B2_EPI_BIAS_RESIDUAL && !S32) {
-                    if (row_ok && n < p.N) load_res16(p, row, n, rs0);
-                    if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
+                    if (row_ok && n < p.N) load_res16(p, row, n, rs[0]);
+                    if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs[1]);
                 }
                 if (c_tma) {
                     // 32 x 32 block of this warp through swizzled shared memory, stored by TMA
                     // (rows >= M and columns >= N are clipped by the tensor map)
-                    unsigned char* buf = stage_w + ((c >> 1) & 1) * P2_EPI_BUF;
-                    if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
+                    if (lane == 0) bulk_wait_read<0>();  // the buffer's previous store has read it
                     __syncwarp();
                     uint32_t w[32];
 #pragma unroll
                     for (int q = 0; q < 32; ++q) {
-                        const uint32_t acc = q < 16 ? r0[q] : r1[q - 16];
                         if constexpr (S32) {
-                            w[q] = acc;
+                            w[q] = rc[q >> 4][q & 15];
                         } else {
-                            w[q] = __float_as_uint(epilogue<EPI>((int32_t)acc, sa, sB_s[c * 16 + q],
-                                                                 EPI != B2_EPI_PLAIN ? bias_s[c * 16 + q] : 0.f,
-                                                                 q < 16 ? rs0[q] : rs1[q - 16]));
+                            w[q] = __float_as_uint(epilogue<EPI>((int32_t)rc[q >> 4][q & 15], sa, sB_s[cc * 32 + q],
+                                                                 EPI != B2_EPI_PLAIN ? bias_s[cc * 32 + q] : 0.f,
+                                                                 rs[q >> 4][q & 15]));
                         }
                     }
 #pragma unroll
@@ -789,15 +802,18 @@ int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_cons
                         bulk_commit();
                     }
                 } else {
-                    if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p);
+                    if (row_ok && n < p.N)
+                        store16<EPI, S32>(rc[0], row, n, sa, sB_s + cc * 32, bias_s + cc * 32, rs[0], p);
                     if (row_ok && n + 16 < p.N)
-                        store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p);
+                        store16<EPI, S32>(rc[1], row, n + 16, sa, sB_s + cc * 32 + 16, bias_s + cc * 32 + 16,
+                                          rs[1], p);
                 }
+                tmem_ld_wait();
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(a ? lead_acce1 : lead_acce0);
-            named_barrier(2, 128);
+            named_barrier(2, NE);
         }
     }
     if (warp >= 2 && lane == 0) bulk_wait_all();  // epilogue stores complete before exit
@@ -956,16 +972,18 @@ static int launch_tc2(const GemmParams& p, const int32_t* A, const int32_t* BT, 
     const int pairs = std::min(tiles, num_sms_current_device() / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(GM_THREADS);
+    cfg.blockDim = dim3(P2_THREADS);
     cfg.dynamicSmemBytes = P2_SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kfn, ma, mb, mc, p, c_tma) == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
