@@ -78,6 +78,34 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// Bounded wait with cluster-scope acquire: for a barrier that CTAs of the cluster arrive on
+// with release.cluster after writing into this CTA's shared memory.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, unsigned int* err) {
+    auto try_once = [&]() {
+        uint32_t ok;
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+        return ok != 0;
+    };
+    if (try_once()) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (try_once()) return true;
+        if (globaltimer() - t0 > B2_WAIT_NS) {
+            raise_error(err, B2_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// 16-byte store into another cluster CTA's shared memory (address from mapa_shared).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};"
+                 :: "r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
 // After a timed-out wait a kernel drains before it exits: every copy and MMA it issued
 // must have landed before its shared memory and tensor memory are released. These waits
 // are bounded too (B2_DRAIN_NS each) and report nothing more: the timeout is already in

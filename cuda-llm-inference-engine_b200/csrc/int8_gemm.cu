@@ -154,6 +154,9 @@ struct GemmParams {
     // kernel waits on the previous grid (the decode engine); otherwise every global read
     // follows the wait, which makes programmatic dependent launch safe for any producer
     int b_early;
+    // the k_splits CTAs of a tile form a thread-block cluster: ranks 1.. hand their int32
+    // partials to rank 0's shared memory (GemmCfg::RED_BYTES), which sums them and stores
+    int cluster_k;
 };
 
 template <int BN>
@@ -161,10 +164,14 @@ struct GemmCfg {
     static constexpr int A_BYTES = GM_BM * GM_BK;
     static constexpr int B_BYTES = BN * GM_BK;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int STAGES = std::min(8, (196 * 1024) / STAGE);
-    static constexpr int OFF_BAR = STAGES * STAGE;
-    // full[S], empty[S], acc_full[2], acc_empty[2], drain
-    static constexpr int NBAR = 2 * STAGES + 5;
+    // partials of up to 3 cluster partners (128 rows x BN int32 each), 32-column tiles only
+    static constexpr int RED_MAX = 3;
+    static constexpr int RED_BYTES = BN == 32 ? RED_MAX * GM_BM * BN * 4 : 0;
+    static constexpr int STAGES = std::min(8, (196 * 1024 - RED_BYTES) / STAGE);
+    static constexpr int OFF_RED = STAGES * STAGE;
+    static constexpr int OFF_BAR = OFF_RED + RED_BYTES;
+    // full[S], empty[S], acc_full[2], acc_empty[2], drain, red (cluster partials landed)
+    static constexpr int NBAR = 2 * STAGES + 6;
     static constexpr int OFF_COL = OFF_BAR + NBAR * 8 + 16;      // f32 [2][BN]: scale_B, bias of the tile
     static constexpr int SMEM = OFF_COL + 2 * BN * 4 + 1024;     // + 1 KB for alignment
     static constexpr uint32_t ACC_COLS = BN < 32 ? 32 : BN;      // one accumulator
@@ -281,6 +288,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     auto accf_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
     auto acce_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * C::STAGES + 4);  // the MMA issuer's drain after an abort
+    const uint32_t red_bar = bar0 + 8u * (2 * C::STAGES + 5);    // cluster partials landed (rank 0)
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_BAR + C::NBAR * 8);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -304,6 +312,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             mbar_init(acce_bar(a), 4);   // one arrival per epilogue warp
         }
         mbar_init(drain_bar, 1);
+        mbar_init(red_bar, (p.k_splits - 1) * 128);  // every epilogue thread of every partner
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -313,6 +322,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
     }
     tc_fence_before();
     __syncthreads();
+    if (p.cluster_k) cluster_sync();  // rank 0's barrier is initialised before partners arrive on it
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -477,6 +487,56 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
+            } else if (p.cluster_k) {
+                // cluster split-K: partners push their int32 partials (valid rows only) into
+                // rank 0's shared memory and arrive on its barrier; rank 0 adds them (exact)
+                // to its own accumulator and runs the epilogue
+                const int lrow = quad * 32 + lane;  // row within the tile
+                if (ksi != 0) {
+                    const uint32_t red_l = smem_u32(smem + C::OFF_RED) +
+                                           (uint32_t)(((ksi - 1) * GM_BM + lrow) * BN * 4);
+                    const uint32_t red_r = mapa_shared(red_l, 0);
+#pragma unroll 1
+                    for (int c = 0; c < BN / 16; ++c) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)(c * 16), r);
+                        tmem_ld_wait();
+                        if (row_ok)
+#pragma unroll
+                            for (int q = 0; q < 16; q += 4)
+                                st_cluster_v4(red_r + (uint32_t)((c * 16 + q) * 4),
+                                              make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]));
+                    }
+                    tc_fence_before();
+                    mbar_arrive_cluster(mapa_shared(red_bar, 0));  // release: the stores above
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acce_bar(a));
+                } else {
+                    const bool got = ok && mbar_wait_cluster(red_bar, 0, p.err);
+                    if (!got) *abort_flag = 1;
+                    const int32_t* red = reinterpret_cast<const int32_t*>(smem + C::OFF_RED) + lrow * BN;
+#pragma unroll 1
+                    for (int c = 0; c < BN / 16; c += 2) {
+                        uint32_t r0[16], r1[16];
+                        tmem_ld16(tbase + (uint32_t)(c * 16), r0);
+                        tmem_ld16(tbase + (uint32_t)(c * 16 + 16), r1);
+                        tmem_ld_wait();
+                        if (got && row_ok) {
+                            for (int ks = 1; ks < p.k_splits; ++ks) {
+                                const int32_t* src = red + (ks - 1) * GM_BM * BN + c * 16;
+#pragma unroll
+                                for (int q = 0; q < 16; ++q) {
+                                    r0[q] = (uint32_t)((int32_t)r0[q] + src[q]);
+                                    r1[q] = (uint32_t)((int32_t)r1[q] + src[16 + q]);
+                                }
+                            }
+                            finish32(r0, r1, c);
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acce_bar(a));
+                }
             } else {
                 // split-K: park this k range's int32 partial, then the last of the k_splits
                 // arrivals for these 32 rows sums the partials (exact) and runs the epilogue
@@ -918,6 +978,23 @@ static int launch_tc(const GemmParams& p, const int32_t* A, const int32_t* BT, c
     if (!set_smem_attr_once((const void*)kfn, C::SMEM, slot)) return B2_ERR_CUDA;
     const int tiles = ((p.N + BN - 1) / BN) * ((p.M + GM_BM - 1) / GM_BM);
     const int grid = std::min(tiles * p.k_splits, num_sms_current_device());
+    if (p.cluster_k) {  // one CTA per (tile, k range); a tile's k ranges form a cluster
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(tiles * p.k_splits);
+        cfg.blockDim = dim3(GM_THREADS);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = p.k_splits;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl_enabled() ? 2 : 1;
+        return cudaLaunchKernelEx(&cfg, kfn, ma, mb, p) == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+    }
     return launch_kernel(kfn, dim3(grid), dim3(GM_THREADS), (size_t)C::SMEM, st, ma, mb, p) == cudaSuccess
                ? B2_OK
                : B2_ERR_CUDA;
@@ -929,6 +1006,7 @@ bool g_gemm_pairs = true;
 // Split-K plan for GEMMs whose tiles cannot fill the GPU (decode: M = batch <= 128): the
 // workspace holds [tiles] u32 tickets (zero at rest), then [k_splits][M][N] int32 partials.
 static void plan_split(GemmParams& p, int tiles, void* ws, size_t ws_bytes, int sms) {
+    p.cluster_k = 0;
     p.k_splits = 1;
     p.kb_per_split = (p.K + GM_BK - 1) / GM_BK;
     p.ws = nullptr;
@@ -1020,6 +1098,21 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
     const int t32 = mt * ((p.N + 31) / 32);
     if (!ws && t64 * 2 <= sms && t32 <= sms) {
         plan_split(p, t32, nullptr, 0, sms);
+        // Long contractions (decode FC2: K = 3072) split K over a cluster of 2 or 4 CTAs per
+        // tile, each keeping >= 6 k-blocks, whose int32 partials meet in rank 0's shared
+        // memory: the chain of MMA issues per CTA shrinks with the split (FC2 64x768x3072:
+        // 9.7 -> 6.8 us; 8 CTAs no faster; splitting K = 768 into 2 or 4 measured slower,
+        // 4.4 -> 5.1 us, the partial exchange then outweighing 3 k-blocks of MMAs).
+        static const bool cluster_off = getenv("B2_GEMM_CLUSTER") && strcmp(getenv("B2_GEMM_CLUSTER"), "0") == 0;
+        const int nk = (p.K + GM_BK - 1) / GM_BK;
+        int ks = 1;
+        for (int c = GemmCfg<32>::RED_MAX + 1; c >= 2; c /= 2)
+            if (nk >= 6 * c && t32 * c <= sms) { ks = c; break; }
+        if (!cluster_off && ks > 1 && !p.sc.q && p.k_splits == 1) {
+            p.k_splits = ks;
+            p.kb_per_split = (nk + ks - 1) / ks;
+            p.cluster_k = 1;
+        }
         return launch_tc<32, EPI, S32>(p, A, BT, st, 48 + EPI + (S32 ? 4 : 0));
     }
     plan_split(p, t64, S32 ? nullptr : ws, ws_bytes, sms);  // the raw-int32 view is never split

@@ -195,7 +195,10 @@ def test_gemm_split_k_bit_exact(b2, oracle, cuda, M, N, K, epi):
 # Decode-size GEMMs (M <= 128: one row tile, skinny 32-column tiles, A boxes trimmed to the
 # batch rows): every epilogue and the raw int32 view, ragged M and N, K tails.
 DECODE_SHAPES = [
-    (64, 768, 3072),     # GPT-2 FC2
+    (64, 768, 3072),     # GPT-2 FC2 (K split over a cluster of 4 CTAs per tile)
+    (64, 768, 1536),     # K split over a cluster of 2
+    (100, 800, 3072),    # cluster split with ragged rows and columns
+    (128, 768, 4096),    # cluster split, full 128-row tile
     (64, 2304, 768),     # GPT-2 QKV
     (1, 768, 768),       # one sequence
     (33, 1000, 640),     # ragged last tile
