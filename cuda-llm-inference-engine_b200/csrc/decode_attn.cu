@@ -55,6 +55,11 @@ struct DecodeAttnParams {
     int H_q, H_kv, block_size, num_blocks_per_seq, num_phys_blocks;
     int chunk_min;              // fewest cache blocks a CTA streams (balanced plan)
     int unit_cost;              // blocks' worth of time a CTA spends starting and merging a unit
+    // decode engine, two-units-per-CTA kernel: the caches' blocks before each sequence's last
+    // one, the block table and the context lengths were written before the previous kernel on
+    // the stream, so they are read before waiting on it (only Q and the newest token's block
+    // wait); the public entry points leave this 0 and read nothing before the wait
+    int kv_early;
     int unit_mode;              // 1: CTA u serves (sequence, KV head) unit u whole, no workspace
     float scale_log2;           // softmax scale * log2(e)
     unsigned int* err;          // device error word
@@ -816,13 +821,19 @@ decode_attn_pair_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
         misc[2] = 0;
         fence_mbar_init();
     }
-    griddep_wait();  // everything above touches only this CTA's shared memory
-    griddep_launch();
+    if (!p.kv_early) {
+        griddep_wait();  // everything above touches only this CTA's shared memory
+        griddep_launch();
+    }
     if (tid < 2) {
         const int u = (int)blockIdx.x * 2 + tid;
         ctx_s[tid] = u < U ? da_context(p, u / p.H_kv, u % p.H_kv == 0) : -1;
     }
     __syncthreads();
+    if (p.kv_early && warp != DA_NW) {  // consumers read Q and write O: after the previous grid
+        griddep_wait();
+        griddep_launch();
+    }
     // empty contexts: O = 0 (reference reduce writes o * 0, 13_decode_attn.cuh:48-52)
     for (int gr = 0; gr < 2; ++gr)
         if (ctx_s[gr] == 0) {
@@ -852,6 +863,7 @@ decode_attn_pair_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
             const uint32_t ring = smem_u32(smem);
             const int ntiles = (ctx + C::T - 1) / C::T;
             int issued = 0;
+            bool waited = !p.kv_early;
             for (int i = 0; i < ntiles; ++i) {
                 const int st = i % C::STAGES;
                 if (i >= C::STAGES &&
@@ -860,6 +872,10 @@ decode_attn_pair_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
                     break;
                 }
                 const int t0 = i * C::T;
+                if (!waited && t0 + C::T >= ctx) {  // this tile holds the newest token's block
+                    griddep_wait();
+                    waited = true;
+                }
                 const int n = min(C::T, ctx - t0);
                 const int nbt = (n + bs - 1) / bs;
                 const uint32_t sK = ring + stage(gr, st);
@@ -1138,7 +1154,8 @@ size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, 
 
 // Validates, plans and launches (in chunks of DA_MAX_B sequences). `counters_zeroed` false
 // makes the launcher clear the counter region first (stream-ordered memset).
-int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaStream_t st) {
+// kv_early (decode engine only): see DecodeAttnParams::kv_early.
+int decode_attn_launch_ex(const b2_decode_attn_args* a, bool counters_zeroed, bool kv_early, cudaStream_t st) {
     if (!a) return B2_ERR_INVALID;
     if (a->B < 0 || a->H_q <= 0 || a->H_kv <= 0 || a->block_size <= 0 || a->num_blocks_per_seq < 0 ||
         a->max_context_len < 0)
@@ -1181,6 +1198,7 @@ int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaS
         prm.B = Bc;
         prm.chunk_min = pl.chunk_min;
         prm.unit_cost = pl.unit_mode ? 0 : pl.unit_cost;
+        prm.kv_early = kv_early && pl.unit_mode && pl.pair ? 1 : 0;
         prm.unit_mode = pl.unit_mode;
         prm.ws_partial = nullptr;
         prm.ws_counter = nullptr;
@@ -1204,6 +1222,10 @@ int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaS
         if (e != cudaSuccess) return B2_ERR_CUDA;
     }
     return B2_OK;
+}
+
+int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaStream_t st) {
+    return decode_attn_launch_ex(a, counters_zeroed, false, st);
 }
 
 }  // namespace b2

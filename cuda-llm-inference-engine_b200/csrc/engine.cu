@@ -22,6 +22,13 @@
 namespace b2 {
 
 int decode_attn_launch(const b2_decode_attn_args* a, bool counters_zeroed, cudaStream_t st);
+int decode_attn_launch_ex(const b2_decode_attn_args* a, bool counters_zeroed, bool kv_early, cudaStream_t st);
+// Decode attention reads the caches' older blocks before waiting on the QKV GEMM (on unless
+// B2_ATTN_KV_EARLY=0).
+static bool kv_early_on() {
+    static const bool off = getenv("B2_ATTN_KV_EARLY") && strcmp(getenv("B2_ATTN_KV_EARLY"), "0") == 0;
+    return !off;
+}
 size_t decode_attn_workspace_size(int B, int H_q, int H_kv, int D, int max_ctx, int block_size);
 int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* scales, cudaStream_t st);
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
@@ -516,8 +523,8 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
         if (R.items)
             B2_TRY(launch_prefill_attention(R.items, R.n_items, Hl, dh, e->kv_dtype, R.q, kc, vc, R.block_table,
                                             e->blocks_per_seq, kBlock, R.pos, R.attn, st));
-        else
-            B2_TRY(decode_attn_launch(&a, true, st));
+        else  // the caches' older blocks, table and lengths predate the QKV GEMM before this launch
+            B2_TRY(decode_attn_launch_ex(&a, true, kv_early_on(), st));
         if (tp) {
             B2_TRY(row_parallel(R.attn, dl, L.out, "gemm_out"));
         } else {
