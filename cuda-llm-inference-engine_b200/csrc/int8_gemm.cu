@@ -312,7 +312,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             mbar_init(acce_bar(a), 4);   // one arrival per epilogue warp
         }
         mbar_init(drain_bar, 1);
-        mbar_init(red_bar, (p.k_splits - 1) * 128);  // every epilogue thread of every partner
+        mbar_init(red_bar, p.cluster_k ? (p.k_splits - 1) * 128 : 1);  // every epilogue thread of every partner
         *abort_flag = 0;
         fence_mbar_init();
     }
