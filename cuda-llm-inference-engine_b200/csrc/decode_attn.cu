@@ -262,8 +262,20 @@ struct DAWarp {
     }
 
     // This warp's token slice of a tile of n tokens (K rows at Kt, V rows at Vt).
+    // A full tile (n == T, most of them) takes a copy of the loop with every token bound
+    // known at compile time, so it carries no per-token range checks.
     __device__ __forceinline__ void tile(const unsigned char* Kt, const unsigned char* Vt, int n, int warp, int lane,
                                          float* xw) {
+        if (n == C::T)
+            tile_n<true>(Kt, Vt, C::T, warp, lane, xw);
+        else
+            tile_n<false>(Kt, Vt, n, warp, lane, xw);
+    }
+
+    template <bool FULL>
+    __device__ __forceinline__ void tile_n(const unsigned char* Kt, const unsigned char* Vt, int n, int warp, int lane,
+                                           float* xw) {
+        if constexpr (FULL) n = C::T;
 #pragma unroll
         for (int grp = 0; grp < C::TW / TPW; ++grp) {
             const int tok0 = warp * C::TW + grp * TPW;
