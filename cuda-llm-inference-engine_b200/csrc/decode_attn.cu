@@ -279,12 +279,12 @@ struct DAWarp {
 #pragma unroll
         for (int grp = 0; grp < C::TW / TPW; ++grp) {
             const int tok0 = warp * C::TW + grp * TPW;
-            if (tok0 >= n) break;  // warp-uniform
+            if (!FULL && tok0 >= n) break;  // warp-uniform
             float s[NV];
 #pragma unroll
             for (int t = 0; t < TPW; ++t) {
                 float kf[C::VPL];
-                if (tok0 + t < n) {
+                if (FULL || tok0 + t < n) {
                     load_row<KV, C::VPL>(Kt + (tok0 + t) * C::ROW + lane * C::VPL * C::ES, kf);
                 } else {
 #pragma unroll
@@ -299,7 +299,7 @@ struct DAWarp {
                 }
             }
             float sc = warp_transpose_sum<NV>(s, lane);
-            if (tok0 + my_t >= n) sc = -INFINITY;
+            if (!FULL && tok0 + my_t >= n) sc = -INFINITY;
             float tmax = sc;
 #pragma unroll
             for (int k = 0; k < ilog2(TPW); ++k)
@@ -326,7 +326,7 @@ struct DAWarp {
                 for (int j = 0; j < VP; ++j) acc[g][j] = fmul2(acc[g][j], make_float2(al[g], al[g]));
 #pragma unroll
             for (int t = 0; t < TPW; ++t) {
-                if (tok0 + t < n) {
+                if (FULL || tok0 + t < n) {
                     float vf[C::VPL];
                     load_row<KV, C::VPL>(Vt + (tok0 + t) * C::ROW + lane * C::VPL * C::ES, vf);
 #pragma unroll
