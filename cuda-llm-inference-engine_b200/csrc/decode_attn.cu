@@ -39,6 +39,15 @@ namespace b2 {
 constexpr int DA_NW = 8;                 // consumer warps
 constexpr int DA_NT = (DA_NW + 1) * 32;  // + producer warp
 constexpr int DA_MINB = 3;               // CTAs per SM the register budget is sized for (G <= 4)
+constexpr int DA_XW = 48;                // floats per warp of the p / alpha exchange (alpha at 32)
+// G = 4, head_dim 128: 2 CTAs per SM with a 96 KB ring and token groups of
+// 8 (32 dot products per reduction) instead of 3 CTAs with 64 KB and groups of 4: the registers
+// of 2 CTAs per SM hold the wider groups without spilling, and each SM keeps 192 KB in flight.
+// Config 3: fp32 187 -> 182 us, bf16 131 -> 116 us, the 8-way head shard 34.8 -> 31.5 us.
+template <int G, int D, typename KV>
+constexpr bool da_wide() { return G == 4 && D == 128; }
+template <int G, int D, typename KV>
+constexpr int da_minb() { return G >= 8 ? 2 : (da_wide<G, D, KV>() ? 2 : DA_MINB); }
 
 constexpr int DA_MAX_B = 256;           // sequences per launch of the kernel (larger batches are chunked)
 
@@ -79,15 +88,18 @@ struct DACfg {
     static constexpr int T1 = (16384 / ROW) < 32 ? 32 : ((16384 / ROW) > 128 ? 128 : (16384 / ROW));
     static constexpr int T = T1 / GR;
     static constexpr int STAGE = 2 * T * ROW;          // K tile then V tile, rows dense
-    static constexpr int STAGES_RAW = (64 * 1024) / (GR * STAGE);  // 64 KB ring: 3 CTAs per SM
+    // 64 KB ring: 3 CTAs per SM (96 KB, 2 CTAs per SM, for da_wide)
+    static constexpr int RING = da_wide<G, D, KV>() ? 96 * 1024 : 64 * 1024;
+    static constexpr int STAGES_RAW = RING / (GR * STAGE);
     static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
     static constexpr int VPL = D / 32;                 // head_dim columns per lane
     static constexpr int TW = T / NWG;                 // tokens of a tile per consumer warp
     // tokens per consumer group: as many as keep TPW * G <= 16 dot products per reduction
-    static constexpr int TPW = (16 / G) < TW ? (16 / G) : TW;
+    static constexpr int NVMAX = da_wide<G, D, KV>() ? 32 : 16;
+    static constexpr int TPW = (NVMAX / G) < TW ? (NVMAX / G) : TW;
     // shared-memory carve-up (bytes)
     static constexpr int OFF_X = GR * STAGES * STAGE;                    // f32 [NW][32] p / alpha exchange
-    static constexpr int OFF_ML = OFF_X + DA_NW * 32 * 4;                // f32 [NW][G][2]
+    static constexpr int OFF_ML = OFF_X + DA_NW * DA_XW * 4;             // f32 [NW][G][2]
     static constexpr int OFF_BT = OFF_ML + DA_NW * G * 2 * 4;            // i32 [BT_CAP] block-table slice
     static constexpr int BT_CAP = 256;                                   // (BT_CAP / GR per group)
     static constexpr int OFF_P = OFF_BT + BT_CAP * 4;                    // i32 [DA_MAX_B + 1] block prefix
@@ -311,12 +323,12 @@ struct DAWarp {
             m_run = m_new;
             if (owner) {
                 xw[idx] = pr;
-                if (my_t == 0) xw[16 + my_g] = alpha;
+                if (my_t == 0) xw[32 + my_g] = alpha;
             }
             __syncwarp();
             float al[G], pv[NV];
 #pragma unroll
-            for (int g = 0; g < G; ++g) al[g] = xw[16 + g];
+            for (int g = 0; g < G; ++g) al[g] = xw[32 + g];
 #pragma unroll
             for (int k = 0; k < NV; ++k) pv[k] = xw[k];
             __syncwarp();
@@ -579,7 +591,7 @@ struct DASched {
 // used when tiles hold whole blocks and the pool size is known. Otherwise the warp gathers
 // rows with cp.async.
 template <int G, int D, typename KV, bool TMA>
-__global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
+__global__ void __launch_bounds__(DA_NT, (da_minb<G, D, KV>()))
 decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    const DecodeAttnParams p) {
     using C = DACfg<G, D, KV>;
@@ -728,7 +740,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 
     // ---------------------------------------------------------------- consumer warps
     constexpr int NC = DA_NW * 32;
-    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
+    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * DA_XW;  // [0,NV) p, [32,32+G) alpha
     float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);           // [NW][G][2]
     DAWarp<G, D, KV> w;
     int used = 0;  // tiles consumed
@@ -804,7 +816,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 // independently. For short units (a few hundred tokens) whose count exceeds one wave of
 // CTAs: the GPU streams every unit at once instead of in 1.7 waves.
 template <int G, int D, typename KV>
-__global__ void __launch_bounds__(DA_NT, G >= 8 ? 2 : DA_MINB)
+__global__ void __launch_bounds__(DA_NT, (da_minb<G, D, KV>()))
 decode_attn_pair_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                         const DecodeAttnParams p) {
     using C = DACfg<G, D, KV, 2>;
@@ -918,7 +930,7 @@ decode_attn_pair_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
     if (ctx <= 0) return;  // the whole group leaves together
     const int u = (int)blockIdx.x * 2 + gr;
     const int b = u / p.H_kv, h = u % p.H_kv;
-    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * 32;  // [0,NV) p, [16,16+G) alpha
+    float* xw = reinterpret_cast<float*>(smem + C::OFF_X) + warp * DA_XW;  // [0,NV) p, [32,32+G) alpha
     float* ml_s = reinterpret_cast<float*>(smem + C::OFF_ML);           // [NW][G][2]
     DAWarp<G, D, KV, 2> w;
     w.begin(p, b, h * G, lane);
@@ -990,8 +1002,12 @@ struct AttnPlan {
     int pair;  // unit mode with two units per CTA (decode_attn_pair_kernel), when TMA is usable
 };
 
-// CTAs resident per SM (the kernel's launch bounds; the shared-memory ring allows as many)
-static int da_ctas_per_sm(int G) { return G >= 8 ? 2 : DA_MINB; }
+// CTAs resident per SM (the kernel's launch bounds, da_minb; D = 0: the largest count, which
+// sizes the workspace for every variant)
+static int da_ctas_per_sm(int G, int D = 0) {
+    if (G >= 8) return 2;
+    return (G == 4 && D == 128) ? 2 : DA_MINB;
+}
 
 // Bytes of one workspace piece (da_piece_floats) and of the counters of U units.
 static size_t da_piece_bytes(int G, int D) { return (size_t)(G * D + ((2 * G + 3) & ~3)) * sizeof(float); }
@@ -1004,14 +1020,14 @@ static int da_chunk_min(int block_size) { return std::max(2, (128 + block_size -
 
 // Balanced grid wanted for a launch of Bc sequences: one CTA per resident slot, fewer when
 // the longest possible batch has fewer chunks.
-static long long da_grid_wanted(int Bc, int H_kv, int G, int max_ctx, int block_size, int num_sms) {
+static long long da_grid_wanted(int Bc, int H_kv, int G, int max_ctx, int block_size, int num_sms, int D = 0) {
     const long long max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
     const long long chunks = ((long long)Bc * H_kv * max_blocks + da_chunk_min(block_size) - 1) / da_chunk_min(block_size);
     // the final merge stages (M, L) of up to gridDim.x pieces per head in one 32 KB ring stage
     const long long merge_cap = 3584 / G;  // 2 grid G floats of (M, L) + 4 KB of partial sums
     // one wave: 1.5, 2 and 3 waves of smaller CTAs measured 4-18% slower (config 3 and its
     // 4- and 8-way head shards), each CTA adding its start-up and merge
-    const long long slots = (long long)da_ctas_per_sm(G) * num_sms;
+    const long long slots = (long long)da_ctas_per_sm(G, D) * num_sms;
     return std::max(1LL, std::min<long long>(std::min<long long>(slots, chunks), merge_cap));
 }
 
@@ -1019,7 +1035,7 @@ static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int kv_bytes, int max_
                           size_t ws_bytes, int num_sms) {
     static const bool force_unit = getenv("B2_ATTN_PLAN") && strcmp(getenv("B2_ATTN_PLAN"), "unit") == 0;
     const long long U = (long long)Bc * H_kv;
-    const long long want = da_grid_wanted(Bc, H_kv, G, max_ctx, block_size, num_sms);
+    const long long want = da_grid_wanted(Bc, H_kv, G, max_ctx, block_size, num_sms, D);
     const size_t cnt = da_counter_bytes(U);
     const long long cap = ws_bytes > cnt ? (long long)((ws_bytes - cnt) / da_piece_bytes(G, D)) : 0;
     AttnPlan pl;
@@ -1034,14 +1050,14 @@ static AttnPlan plan_attn(int Bc, int H_kv, int G, int D, int kv_bytes, int max_
     // Charged only when the grid fills every slot: a narrower grid (short batches such as
     // config 1) gives each CTA more than a slot's share, and there the charge cut pieces
     // finer than the units' own shape (config 1: 10.7 us with it, 8.9 without).
-    pl.unit_cost = want >= (long long)da_ctas_per_sm(G) * num_sms
+    pl.unit_cost = want >= (long long)da_ctas_per_sm(G, D) * num_sms
                        ? std::max(0, (56 * 1024 + block_bytes / 2) / block_bytes) : 0;
     // Short units that fill the GPU 1.5 times or more by themselves run one CTA per unit:
     // cutting and grouping them costs more in item merges than the last wave loses (GPT-2
     // Small layer, B64 x 12 heads, contexts 129-256 with max_context_len 1024: 16.1-21.4 us
     // per launch one CTA per unit, 19.1-25.0 us balanced).
     const long long max_blocks = std::max(1, (max_ctx + block_size - 1) / block_size);
-    const bool short_units = max_blocks <= 64 && 2 * U >= 3LL * da_ctas_per_sm(G) * num_sms;
+    const bool short_units = max_blocks <= 64 && 2 * U >= 3LL * da_ctas_per_sm(G, D) * num_sms;
     // balanced when the workspace holds its pieces (grid + U rows) for a grid at least as
     // wide as one CTA per unit would be (or as wanted, when that is narrower)
     const long long g = std::min(want, cap - U);
