@@ -13,7 +13,8 @@
 // B200 design (one CTA per (split, kv_head, sequence)):
 //   - the CTA serves all G = H_q/H_kv query heads of its KV head, so every K/V byte is
 //     read from HBM once (the reference re-reads it once per query head);
-//   - warp 8 is a producer: it fills a 64 KB shared-memory ring with tiles of ~32 KB (32-128
+//   - warp 8 is a producer: it fills a 64 KB (96 KB for G 4 / d 128) shared-memory ring with
+//     tiles of ~32 KB (32-128
 //     tokens of K and V) found through the block table. When a tile holds whole cache blocks,
 //     its lane 0 issues one 3-D TMA load per block for K and one for V (a tensor map over the
 //     cache as [P * block_size][H_kv][D]) and the stage barrier counts the bytes; otherwise
@@ -23,7 +24,7 @@
 //   - warps 0..7 consume: each owns a slice of every tile's tokens and runs its own
 //     exp2-domain online softmax with no CTA barrier inside the loop; the warps' partial
 //     (o, m, l) are merged by log-sum-exp at the end of the split;
-//   - 3 CTAs per SM (ring 64 KB) hide the per-CTA start-up and merge latency;
+//   - 3 CTAs per SM (2 for G 4 / d 128 and G 8) hide the per-CTA start-up and merge latency;
 //   - the split merge is fused: every CTA of a (sequence, KV head) writes its partial to
 //     the workspace, and the last to arrive (atomic ticket) merges and writes O.
 #include "common.cuh"
