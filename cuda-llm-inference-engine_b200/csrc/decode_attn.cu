@@ -14,8 +14,7 @@
 //   - the CTA serves all G = H_q/H_kv query heads of its KV head, so every K/V byte is
 //     read from HBM once (the reference re-reads it once per query head);
 //   - warp 8 is a producer: it fills a 64 KB (96 KB for G 4 / d 128) shared-memory ring with
-//     tiles of ~32 KB (32-128
-//     tokens of K and V) found through the block table. When a tile holds whole cache blocks,
+//     tiles of ~32 KB (32-128 tokens of K and V) found through the block table. When a tile holds whole cache blocks,
 //     its lane 0 issues one 3-D TMA load per block for K and one for V (a tensor map over the
 //     cache as [P * block_size][H_kv][D]) and the stage barrier counts the bytes; otherwise
 //     the warp gathers rows with coalesced 16-byte cp.async and counts completion with
