@@ -46,7 +46,7 @@ _CXX = {
 # Every symbol include/*.h declares (checked by the CPU tests).
 C_ABI_SYMBOLS = [
     "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_decode_attn_noalloc", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
-    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_int8_gemm_f32a", "b2_layernorm", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
+    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_layernorm", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
 ]
 
 
@@ -97,8 +97,6 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     lib.b2_int8_gemm_ws.restype = i
     lib.b2_int8_gemm_s32.argtypes = [i, i, i, vp, vp, vp, vp]
     lib.b2_int8_gemm_s32.restype = i
-    lib.b2_int8_gemm_f32a.argtypes = [i, i, i, vp, vp, vp, vp, vp, vp, vp, i, vp, vp]
-    lib.b2_int8_gemm_f32a.restype = i
     lib.b2_layernorm.argtypes = [i, i, vp, vp, vp, ctypes.c_float, vp, vp, vp, vp]
     lib.b2_layernorm.restype = i
     lib.b2_get_device_error.argtypes = [i]
@@ -342,23 +340,6 @@ def make_gemm_workspace(M, N, K, device=None):
     import torch
 
     return torch.zeros(max(256, int8_gemm_workspace_size(M, N, K)), dtype=torch.uint8, device=device or "cuda")
-
-
-def int8_gemm_f32a(A, a_amax, BT_packed, scale_B, bias=None, residual=None, epilogue=EPI_PLAIN, C=None,
-                   c_amax=None, stream=None):
-    """INT8 linear with fp32 A quantised per row inside the GEMM from its row absmax ``a_amax``
-    (int32 tensor of float bits); ``c_amax`` (int32, zeroed by the caller) receives each output
-    row's max |C| as float bits."""
-    import torch
-
-    M, K = A.shape
-    N = BT_packed.shape[0]
-    if C is None:
-        C = torch.empty(M, N, dtype=torch.float32, device=A.device)
-    _check(load_library().b2_int8_gemm_f32a(M, N, K, _ptr(A), _ptr(a_amax), _ptr(BT_packed), _ptr(scale_B),
-                                            _ptr(bias), _ptr(residual), _ptr(C), epilogue, _ptr(c_amax),
-                                            _stream(stream)), "b2_int8_gemm_f32a")
-    return C
 
 
 def int8_gemm_s32(A_packed, BT_packed, C=None, stream=None):

@@ -20,7 +20,6 @@ int quantize_launch(int rows, int cols, const float* in, int32_t* out, float* sc
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
                 const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
                 void* ws = nullptr, size_t ws_bytes = 0);
-bool gemm_decode_path(int M, int N, int K);
 size_t gemm_workspace_size(int M, int N, int K);
 
 constexpr int kMaxDevices = 64;
@@ -66,11 +65,6 @@ unsigned int* device_error_ptr() {
 bool& pdl_enabled() {
     static thread_local bool on = false;
     return on;
-}
-
-GemmExtra& gemm_extra() {
-    static thread_local GemmExtra x;
-    return x;
 }
 
 bool& weights_constant() {
@@ -119,32 +113,6 @@ int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT
     PdlOn pdl;
     return gemm_launch(M, N, K, A_packed, BT_packed, scale_A, scale_B, bias, residual, C, epilogue, false,
                        static_cast<cudaStream_t>(stream));
-}
-
-int b2_int8_gemm_f32a(int M, int N, int K, const float* A, const uint32_t* a_amax, const int32_t* BT_packed,
-                      const float* scale_B, const float* bias, const float* residual, float* C, int epilogue,
-                      uint32_t* c_amax, b2_stream_t stream) {
-    if (M < 0 || N < 0 || K < 0) return t_last_status = B2_ERR_INVALID;
-    if (M == 0 || N == 0) return t_last_status = B2_OK;
-    if (!A || !a_amax || !BT_packed || !scale_B || !C || ((uintptr_t)A & 15) || (K & 3))
-        return t_last_status = B2_ERR_INVALID;
-    if (!gemm_decode_path(M, N, K)) return t_last_status = B2_ERR_UNSUPPORTED;
-    GemmExtra& x = gemm_extra();
-    x = GemmExtra{};
-    x.a_f32 = A;
-    x.a_amax = a_amax;
-    x.c_amax = c_amax;
-    int r;
-    {
-        PdlOn pdl;
-        // the int8 A operand and its scales are never read in this mode: B stands in for them
-        r = gemm_launch(M, N, K, BT_packed, BT_packed, scale_B, scale_B, bias, residual, C, epilogue, false,
-                        static_cast<cudaStream_t>(stream), nullptr, 0);
-    }
-    const bool used = x.used;
-    x = GemmExtra{};
-    if (r == B2_OK && !used) r = B2_ERR_UNSUPPORTED;  // not reached: gemm_decode_path agreed
-    return t_last_status = r;
 }
 
 size_t b2_int8_gemm_workspace_size(int M, int N, int K) {

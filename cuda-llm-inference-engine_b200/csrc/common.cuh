@@ -382,18 +382,6 @@ bool& pdl_enabled();
 // previous grid (the decode engine's step: its weights never change).
 bool& weights_constant();
 
-// Host (decode engine): extra duties for the next gemm_launch / gemm_launch_qkv on this thread
-// (GemmParams::a_f32 .. zero_rows). `used` is set when the launch took them; otherwise the
-// caller runs the standalone quantiser itself.
-struct GemmExtra {
-    const float* a_f32 = nullptr;
-    const unsigned int* a_amax = nullptr;
-    unsigned int* c_amax = nullptr;
-    unsigned int* zero_rows = nullptr;
-    bool used = false;
-};
-GemmExtra& gemm_extra();
-
 // Host: sets pdl_enabled() (and optionally weights_constant()) for a scope.
 struct PdlOn {
     bool saved_pdl, saved_w;

@@ -157,13 +157,6 @@ struct GemmParams {
     // the k_splits CTAs of a tile form a thread-block cluster: ranks 1.. hand their int32
     // partials to rank 0's shared memory (GemmCfg::RED_BYTES), which sums them and stores
     int cluster_k;
-    // decode engine: A given as fp32 [M, K] (a_f32) whose row absmax (float bits) the kernel
-    // that wrote it left in a_amax [M]; the epilogue warps quantise each k-block into the ring
-    // themselves (the standalone quantiser's arithmetic) instead of A arriving by TMA
-    const float* a_f32;
-    const unsigned int* a_amax;
-    unsigned int* c_amax;     // non-null: each output row's max |value| is atomically maxed in
-    unsigned int* zero_rows;  // non-null: CTA 0 clears these M words (a buffer two kernels old)
 };
 
 template <int BN>
@@ -180,8 +173,7 @@ struct GemmCfg {
     // full[S], empty[S], acc_full[2], acc_empty[2], drain, red (cluster partials landed)
     static constexpr int NBAR = 2 * STAGES + 6;
     static constexpr int OFF_COL = OFF_BAR + NBAR * 8 + 16;      // f32 [2][BN]: scale_B, bias of the tile
-    static constexpr int OFF_AS = OFF_COL + 2 * BN * 4;          // f32 [2][GM_BM]: scale_A, 1/scale_A (a_f32)
-    static constexpr int SMEM = OFF_AS + 2 * GM_BM * 4 + 1024;   // + 1 KB for alignment
+    static constexpr int SMEM = OFF_COL + 2 * BN * 4 + 1024;     // + 1 KB for alignment
     static constexpr uint32_t ACC_COLS = BN < 32 ? 32 : BN;      // one accumulator
     static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;          // double-buffered
 };
@@ -205,7 +197,7 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 template <int EPI, bool S32>
 __device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n, float sa, const float* sBs,
                                         const float* bis, const float (&rs)[16], const GemmParams& p,
-                                        long long sc_row = -1, float* rmax = nullptr) {
+                                        long long sc_row = -1) {
     if constexpr (S32) {
         int32_t* Crow = static_cast<int32_t*>(p.C) + (size_t)row * p.N;
         if (n + 16 <= p.N && (p.N & 3) == 0) {
@@ -223,11 +215,6 @@ __device__ __forceinline__ void store16(const uint32_t (&r)[16], int row, int n,
 #pragma unroll
         for (int j = 0; j < 16; ++j)
             v[j] = epilogue<EPI>((int32_t)r[j], sa, sBs[j], EPI != B2_EPI_PLAIN ? bis[j] : 0.f, rs[j]);
-        if (rmax) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (n + j < p.N) *rmax = fmaxf(*rmax, fabsf(v[j]));
-        }
         if (p.sc.q) {  // fused QKV split: 16 columns never straddle q/K/V (d % 16 == 0)
             const int part = n / p.sc.d, i = n - part * p.sc.d;
             if (part == 0) {
@@ -317,7 +304,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         prefetch_tensormap(&mapA);
         prefetch_tensormap(&mapB);
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(full_bar(s), p.a_f32 ? 5 : 1);  // + the 4 epilogue warps writing A (a_f32)
+            mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -356,7 +343,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                 npre = min(C::STAGES, kb1 - kb0);
                 for (int i = 0; i < npre; ++i) {
                     const uint32_t b_s = sbase + i * C::STAGE + C::A_BYTES;
-                    mbar_arrive_expect_tx(full_bar(i), (p.a_f32 ? 0 : p.a_rows * GM_BK) + C::B_BYTES);
+                    mbar_arrive_expect_tx(full_bar(i), p.a_rows * GM_BK + C::B_BYTES);
                     tma_load_2d(b_s, &mapB, (kb0 + i) * GM_BK, nt * BN, full_bar(i), pol);
                 }
             }
@@ -374,7 +361,7 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     const uint32_t a_s = sbase + s * C::STAGE;
                     const uint32_t b_s = a_s + C::A_BYTES;
                     if (it < npre) {  // B already requested
-                        if (!p.a_f32) tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
+                        tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
                         continue;
                     }
                     if (it >= C::STAGES) {
@@ -383,8 +370,8 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                             break;
                         }
                     }
-                    mbar_arrive_expect_tx(full_bar(s), (p.a_f32 ? 0 : p.a_rows * GM_BK) + C::B_BYTES);
-                    if (!p.a_f32) tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
+                    mbar_arrive_expect_tx(full_bar(s), p.a_rows * GM_BK + C::B_BYTES);
+                    tma_load_2d(a_s, &mapA, kb * GM_BK, mt * GM_BM, full_bar(s), pol);
                     tma_load_2d(b_s, &mapB, kb * GM_BK, nt * BN, full_bar(s), pol);
                 }
             }
@@ -440,9 +427,6 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
         griddep_wait();                   // scale_A / residual may come from the previous kernel
         float* sB_s = reinterpret_cast<float*>(smem + C::OFF_COL);
         float* bias_s = sB_s + BN;
-        float* sA_s = reinterpret_cast<float*>(smem + C::OFF_AS);  // a_f32: scale_A, then 1/scale_A
-        if (p.zero_rows && blockIdx.x == 0)
-            for (int r = et; r < p.M; r += 128) p.zero_rows[r] = 0u;
         int j = 0;
         for (int w = blockIdx.x; w < num_units; w += gridDim.x, ++j) {
             const int t = w / p.k_splits;
@@ -450,55 +434,6 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             const int a = j & 1, u = j >> 1;
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, mt, nt);
-            if (p.a_f32) {
-                // A from fp32: row scales (quantiser arithmetic of quant_row_warp), then every
-                // k-block of this unit quantised into the ring stage's A tile in the 128-byte
-                // swizzled layout TMA would have produced (one CTA holds one unit here)
-                for (int r = et; r < GM_BM; r += 128) {
-                    const int row = mt * GM_BM + r;
-                    const float amax = row < p.M ? __uint_as_float(__ldcg(p.a_amax + row)) : 0.f;
-                    const float sc = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-                    sA_s[r] = sc;
-                    sA_s[GM_BM + r] = __fdiv_rn(1.0f, sc);
-                }
-                named_barrier(2, 128);
-                const int kb0 = ksi * p.kb_per_split;
-                const int kb1 = min(nk, kb0 + p.kb_per_split);
-                const int rows = min(GM_BM, p.M - mt * GM_BM);
-                for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
-                    const int s = it % C::STAGES;
-                    if (it >= C::STAGES && (*abort_flag || !mbar_wait(empty_bar(s), ((it / C::STAGES) - 1) & 1, p.err))) {
-                        *abort_flag = 1;
-                        break;
-                    }
-                    unsigned char* a_tile = smem + s * C::STAGE;
-                    for (int c = et; c < rows * 8; c += 128) {  // 16-byte chunk c % 8 of row c / 8
-                        const int r = c >> 3, ch = c & 7;
-                        const int k0 = kb * GM_BK + ch * 16;
-                        const float inv = sA_s[GM_BM + r];
-                        const float* src = p.a_f32 + (size_t)(mt * GM_BM + r) * p.K + k0;
-                        uint32_t w4[4];
-#pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (k0 + 4 * q4 < p.K) v = __ldcg(reinterpret_cast<const float4*>(src) + q4);
-                            const float t4[4] = {v.x, v.y, v.z, v.w};
-                            uint32_t packed = 0;
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float qf = fminf(fmaxf(rintf(__fmul_rn(t4[e], inv)), -128.f), 127.f);
-                                packed |= (uint32_t)(uint8_t)(int8_t)(int)qf << (8 * e);
-                            }
-                            w4[q4] = packed;
-                        }
-                        *reinterpret_cast<uint4*>(a_tile + r * 128 + ((ch ^ (r & 7)) * 16)) =
-                            make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                    }
-                    fence_proxy_async();  // generic-proxy stores -> the MMA's async-proxy reads
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(full_bar(s));
-                }
-            }
             // stage this tile's column scales and biases while the MMAs run
             if constexpr (!S32) {
                 for (int c = et; c < BN; c += 128) {
@@ -524,9 +459,8 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
             tc_fence_after();
             const int row = mt * GM_BM + quad * 32 + lane;
             const bool row_ok = ok && row < p.M;
-            const float sa = (!S32 && row_ok) ? (p.a_f32 ? sA_s[quad * 32 + lane] : __ldg(p.scale_A + row)) : 0.f;
+            const float sa = (!S32 && row_ok) ? __ldg(p.scale_A + row) : 0.f;
             const uint32_t tbase = tmem + a * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
-            float rmax = 0.f;  // this row's max |output| over the tile (c_amax)
             // final dequantise/epilogue/store of columns [n, n+32) from accumulators r0, r1
             auto finish32 = [&](const uint32_t (&r0)[16], const uint32_t (&r1)[16], int c) {
                 const int n = nt * BN + c * 16;
@@ -537,11 +471,9 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     if (row_ok && n < p.N) load_res16(p, row, n, rs0);
                     if (row_ok && n + 16 < p.N) load_res16(p, row, n + 16, rs1);
                 }
-                float* rm = p.c_amax ? &rmax : nullptr;
-                if (row_ok && n < p.N)
-                    store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p, sc_row, rm);
+                if (row_ok && n < p.N) store16<EPI, S32>(r0, row, n, sa, sB_s + c * 16, bias_s + c * 16, rs0, p, sc_row);
                 if (row_ok && n + 16 < p.N)
-                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p, sc_row, rm);
+                    store16<EPI, S32>(r1, row, n + 16, sa, sB_s + c * 16 + 16, bias_s + c * 16 + 16, rs1, p, sc_row);
             };
             if (p.k_splits == 1) {
 #pragma unroll 1
@@ -552,7 +484,6 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     tmem_ld_wait();
                     finish32(r0, r1, c);
                 }
-                if (p.c_amax && row_ok) atomicMax(p.c_amax + row, __float_as_uint(rmax));  // rmax >= 0
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
@@ -602,7 +533,6 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                             finish32(r0, r1, c);
                         }
                     }
-                    if (p.c_amax && got && row_ok) atomicMax(p.c_amax + row, __float_as_uint(rmax));
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(acce_bar(a));
@@ -1183,33 +1113,10 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
             p.kb_per_split = (nk + ks - 1) / ks;
             p.cluster_k = 1;
         }
-        GemmExtra& x = gemm_extra();
-        // fp32 A quantised in the kernel: every CTA holds one unit, A rows 16-byte aligned
-        const bool a_ok = !x.a_f32 || (!S32 && ((uintptr_t)x.a_f32 & 15) == 0 && (p.K & 3) == 0 && x.a_amax);
-        if ((x.a_f32 || x.c_amax || x.zero_rows) && a_ok && !S32) {
-            p.a_f32 = x.a_f32;
-            p.a_amax = x.a_amax;
-            p.c_amax = x.c_amax;
-            p.zero_rows = x.zero_rows;
-            x.used = true;
-        }
         return launch_tc<32, EPI, S32>(p, A, BT, st, 48 + EPI + (S32 ? 4 : 0));
     }
     plan_split(p, t64, S32 ? nullptr : ws, ws_bytes, sms);  // the raw-int32 view is never split
     return launch_tc<64, EPI, S32>(p, A, BT, st, slot_base + 2);
-}
-
-// True when gemm_launch (no workspace) runs this shape as 32-column tiles, one unit per CTA:
-// the path that takes GemmExtra's duties.
-bool gemm_decode_path(int M, int N, int K) {
-    if (M <= 0 || N <= 0 || K <= 0 || (K & 15)) return false;
-    const int sms = num_sms_current_device();
-    const int mt = (M + GM_BM - 1) / GM_BM;
-    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
-    if (g_gemm_pairs && pair_tiles * 2 >= (sms * 3) / 4) return false;
-    const int t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128), t64 = mt * ((N + 63) / 64);
-    const int t32 = mt * ((N + 31) / 32);
-    return t256 < sms && t128 < sms && t64 * 2 <= sms && t32 <= sms;
 }
 
 // Workspace bytes that let gemm_launch split K for these shapes (0 when it would not split).
@@ -1272,11 +1179,6 @@ int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, co
     const int sms = num_sms_current_device();
     const int pair_tiles = (N + 255) / 256;
     if (g_gemm_pairs && pair_tiles * 2 >= (sms * 3) / 4) return B2_ERR_UNSUPPORTED;
-    GemmExtra& x = gemm_extra();
-    if (x.zero_rows && !x.a_f32 && !x.c_amax) {  // the only extra duty this launcher takes
-        p.zero_rows = x.zero_rows;
-        x.used = true;
-    }
     const int t256 = (N + 255) / 256, t128 = (N + 127) / 128, t64 = (N + 63) / 64, t32 = (N + 31) / 32;
     plan_split(p, 1, nullptr, 0, sms);  // one k range per tile (sets kb_per_split)
     if (t256 >= sms) return launch_tc<256, B2_EPI_BIAS, false>(p, A, BT, st, 0);

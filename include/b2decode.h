@@ -140,18 +140,6 @@ int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT
                  const float* scale_A, const float* scale_B, const float* bias,
                  const float* residual, float* C, int epilogue, b2_stream_t stream);
 
-/* The same linear with A given in fp32 and quantised per row inside the GEMM (decode engine:
- * the quantiser launch between two kernels disappears). a_amax [M] holds each row's
- * max |A| as float bits (the producer of A leaves it there, e.g. with atomicMax); the int8
- * bytes and scales are those b2_quantize_fp32_to_int8 would produce, so C equals
- * quantise + b2_int8_gemm bit for bit. c_amax (nullable) [M] receives atomicMax of each output
- * row's max |C| (float bits; clear it first). Decode shapes only (M <= 128 rows per tile, the
- * 32-column path): other shapes return B2_ERR_UNSUPPORTED and launch nothing. No counterpart
- * in the reference, whose engine quantises in a separate launch (src/gpt2_engine.cu:508, 524). */
-int b2_int8_gemm_f32a(int M, int N, int K, const float* A, const uint32_t* a_amax, const int32_t* BT_packed,
-                      const float* scale_B, const float* bias, const float* residual, float* C, int epilogue,
-                      uint32_t* c_amax, b2_stream_t stream);
-
 /* Bytes of workspace that let b2_int8_gemm_ws split the K dimension across CTAs for shapes
  * whose output tiles cannot fill the GPU (decode: M = batch); 0 when it would not split.
  * No counterpart in the reference (its dp4a kernel has a fixed 64x64 tile grid). */

@@ -239,32 +239,3 @@ def test_gemm_decode_shapes_bit_exact(b2, oracle, cuda, M, N, K, epi):
         np.testing.assert_allclose(g, want, rtol=1e-4, atol=1e-6)
     else:
         np.testing.assert_array_equal(g.view(np.uint32), want.view(np.uint32))
-
-
-@pytest.mark.parametrize("M,N,K", [(64, 768, 768), (64, 768, 3072), (64, 3072, 768), (37, 800, 1536), (128, 768, 4096)])
-@pytest.mark.parametrize("epi", [0, 1, 2, 3])
-def test_gemm_f32a_equals_quantise_then_gemm(b2, oracle, cuda, M, N, K, epi):
-    """b2_int8_gemm_f32a (A in fp32, quantised per row inside the GEMM from a given row absmax)
-    equals b2_quantize_fp32_to_int8 followed by b2_int8_gemm bit for bit, including the cluster
-    split-K shapes; its output row absmax equals max |C| per row exactly; two calls agree."""
-    import torch
-
-    rng = np.random.default_rng(M * 7 + N + K + epi)
-    A = rng.standard_normal((M, K)).astype(np.float32)
-    Bt = rng.standard_normal((N, K)).astype(np.float32)
-    Bp, sB = oracle.quantize(Bt)
-    bias = rng.standard_normal(N).astype(np.float32)
-    res = rng.standard_normal((M, N)).astype(np.float32)
-    tA, tBp, tsB = dev(torch, A, cuda), dev(torch, Bp, cuda), dev(torch, sB, cuda)
-    tb, tr = dev(torch, bias, cuda), dev(torch, res, cuda)
-    Aq, sA = b2.quantize_fp32_to_int8(tA)
-    want = b2.int8_gemm(Aq, tBp, sA, tsB, tb if epi else None, tr if epi == 3 else None, epilogue=epi)
-    amax = tA.abs().amax(dim=1).contiguous().view(torch.int32)
-    for _ in range(2):
-        camax = torch.zeros(M, dtype=torch.int32, device=cuda)
-        got = b2.int8_gemm_f32a(tA, amax, tBp, tsB, tb if epi else None, tr if epi == 3 else None, epilogue=epi,
-                                c_amax=camax)
-        torch.cuda.synchronize()
-        assert b2.device_error() == 0
-        np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32))
-        np.testing.assert_array_equal(camax.view(torch.float32).cpu().numpy(), got.abs().amax(dim=1).cpu().numpy())
