@@ -62,6 +62,7 @@ __device__ __forceinline__ unsigned long long vt_key(float v, int idx) {
 struct VocabParams {
     int M, N, K;               // batch, vocab rows held here, d_model
     int n_offset;              // global index of this shard's first vocab row (tensor parallel)
+    int a_rows;                // rows of the activation tiles each stage loads (M rounded to 8, <= 128)
     float* logits;             // [M, N] or null
     unsigned long long* keys;  // [M] argmax keys (reset by the caller before the step)
     unsigned int* err;
@@ -132,7 +133,7 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
                 npre = min(VT_STAGES, nk);
                 for (int i = 0; i < npre; ++i) {
                     const uint32_t w_s = sbase + i * VT_STAGE + 2 * VT_A;
-                    mbar_arrive_expect_tx(full_bar(i), VT_STAGE);
+                    mbar_arrive_expect_tx(full_bar(i), 2 * p.a_rows * VT_BKB + 2 * VT_B);
                     tma_load_2d(w_s, &mWh, i * 64, nt * VT_BN, full_bar(i), pol_w);
                     tma_load_2d(w_s + VT_B, &mWl, i * 64, nt * VT_BN, full_bar(i), pol_w);
                 }
@@ -152,7 +153,7 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
                             *abort_flag = 1;
                             break;
                         }
-                        mbar_arrive_expect_tx(full_bar(s), VT_STAGE);
+                        mbar_arrive_expect_tx(full_bar(s), 2 * p.a_rows * VT_BKB + 2 * VT_B);
                         tma_load_2d(w_s, &mWh, kb * 64, nt * VT_BN, full_bar(s), pol_w);
                         tma_load_2d(w_s + VT_B, &mWl, kb * 64, nt * VT_BN, full_bar(s), pol_w);
                     }
@@ -272,7 +273,7 @@ vocab_bf16x3_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_consta
 #pragma unroll
                     for (int q = 0; q < 32; ++q) {
                         const float v = __uint_as_float(q < 16 ? r0[q] : r1[q - 16]);
-                        if (n0 + q < p.N && v >= thr) {
+                        if (row_ok && n0 + q < p.N && v >= thr) {  // rows past M hold stale products
                             const int i = atomicAdd(p.cand_cnt + row, 1);
                             if (i < p.cand_cap)
                                 p.cand[(size_t)row * p.cand_cap + i] = make_int2(__float_as_int(v), n0 + q);
@@ -340,12 +341,15 @@ int launch_vocab_bf16x3(int M, int N, int K, const void* h_hi, const void* h_lo,
                         int* cand_cnt, void* cand, int cand_cap) {
     if ((K & 7) || M <= 0 || N <= 0) return B2_ERR_UNSUPPORTED;
     CUtensorMap ah, al, wh, wl;
-    if (!encode_bf16(&ah, h_hi, M, K, VT_BM) || !encode_bf16(&al, h_lo, M, K, VT_BM) ||
+    // a decode batch loads only its own rows of the activation tiles (the MMA rows past them
+    // read stale shared memory and are never stored): half the activation bytes at M = 64
+    const int a_rows = M < VT_BM ? ((M + 7) & ~7) : VT_BM;
+    if (!encode_bf16(&ah, h_hi, M, K, a_rows) || !encode_bf16(&al, h_lo, M, K, a_rows) ||
         !encode_bf16(&wh, w_hi, N, K, VT_BN) || !encode_bf16(&wl, w_lo, N, K, VT_BN))
         return B2_ERR_CUDA;
     if (!set_smem_attr_once((const void*)vocab_bf16x3_kernel, VT_SMEM, 60)) return B2_ERR_CUDA;
     const int tiles = ((M + VT_BM - 1) / VT_BM) * ((N + VT_BN - 1) / VT_BN);
-    VocabParams p{M, N, K, n_offset, logits, keys, device_error_ptr(), cand_delta, cand_cnt,
+    VocabParams p{M, N, K, n_offset, a_rows, logits, keys, device_error_ptr(), cand_delta, cand_cnt,
                   static_cast<int2*>(cand), cand_cap};
     const int grid = std::min(tiles, num_sms_current_device());
     return launch_kernel(vocab_bf16x3_kernel, dim3(grid), dim3(VT_THREADS), (size_t)VT_SMEM, st, ah, al, wh, wl, p) ==
