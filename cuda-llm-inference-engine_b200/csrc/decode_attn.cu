@@ -10,22 +10,27 @@
 // reads them, 13_decode_attn.cuh:56), a zero-length context yields O = 0, head_dim 128
 // and bf16 caches are supported, and cache offsets are 64-bit.
 //
-// B200 design (one CTA per (split, kv_head, sequence)):
+// B200 design:
+//   - work schedule: every CTA of one wave reads the context lengths and streams an equal
+//     share of the batch's cache blocks (units = (sequence, KV head) laid end to end, each
+//     charged a start-and-merge cost), so ragged batches balance; a unit cut across CTAs is
+//     merged from its pieces. Short units that fill the GPU by themselves run whole, two per
+//     CTA (decode_attn_pair_kernel) for head_dim 64;
 //   - the CTA serves all G = H_q/H_kv query heads of its KV head, so every K/V byte is
 //     read from HBM once (the reference re-reads it once per query head);
 //   - warp 8 is a producer: it fills a 64 KB (96 KB for G 4 / d 128) shared-memory ring with
-//     tiles of ~32 KB (32-128 tokens of K and V) found through the block table. When a tile holds whole cache blocks,
-//     its lane 0 issues one 3-D TMA load per block for K and one for V (a tensor map over the
-//     cache as [P * block_size][H_kv][D]) and the stage barrier counts the bytes; otherwise
-//     the warp gathers rows with coalesced 16-byte cp.async and counts completion with
-//     cp.async.mbarrier.arrive. 1-D bulk copies of single rows were measured to be
-//     request-rate bound here (fp32 and bf16 took equal time);
+//     tiles of ~32 KB (32-128 tokens of K and V) found through the block table. When a tile
+//     holds whole cache blocks, its lane 0 issues one 3-D TMA load per block for K and one for
+//     V (a tensor map over the cache as [P * block_size][H_kv][D]) and the stage barrier counts
+//     the bytes; otherwise the warp gathers rows with coalesced 16-byte cp.async and counts
+//     completion with cp.async.mbarrier.arrive. 1-D bulk copies of single rows were measured
+//     to be request-rate bound here (fp32 and bf16 took equal time);
 //   - warps 0..7 consume: each owns a slice of every tile's tokens and runs its own
 //     exp2-domain online softmax with no CTA barrier inside the loop; the warps' partial
-//     (o, m, l) are merged by log-sum-exp at the end of the split;
+//     (o, m, l) are merged by log-sum-exp at the end of each unit's piece;
 //   - 3 CTAs per SM (2 for G 4 / d 128 and G 8) hide the per-CTA start-up and merge latency;
-//   - the split merge is fused: every CTA of a (sequence, KV head) writes its partial to
-//     the workspace, and the last to arrive (atomic ticket) merges and writes O.
+//   - the split merge is fused: every piece of a cut unit goes to the workspace, and the
+//     last to arrive (atomic ticket) merges them and writes O.
 #include "common.cuh"
 #include <cuda_bf16.h>
 #include <algorithm>
