@@ -960,6 +960,30 @@ def run_only(args):
         ws = b2.make_decode_workspace(B, hq, hkv, D, int(lens.max()), BS, device=dev)
         fn = lambda: b2.decode_attn(q, kc, vc, btd, lensd, int(lens.max()), O=O, workspace=ws)  # noqa: E731
         by = attn_alg_bytes(lens, hkv, hq, D, 2 if dt == torch.bfloat16 else 4, bt.shape[1])
+    elif args.only == "gemm_c5":
+        # config-5 decode GEMM shapes per tensor-parallel shard (batch 128, d 4096, d_ff 16384):
+        # 12 weight copies rotated in one graph so the weights stream from HBM, not L2
+        copies = 12
+        for (M, N, K, tag) in [(128, 3072, 4096, "qkv tp4"), (128, 4096, 4096, "fc1/fc2 tp4"),
+                               (128, 1536, 4096, "qkv tp8"), (128, 2048, 4096, "fc1/fc2 tp8"),
+                               (128, 4096, 1024, "out tp4"), (128, 6144, 4096, "qkv tp2"),
+                               (128, 8192, 4096, "fc1/fc2 tp2")]:
+            A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev).view(torch.int32)
+            Bts = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev).view(torch.int32)
+                   for _ in range(copies)]
+            sA, sB = torch.rand(M, device=dev), torch.rand(N, device=dev)
+            C = torch.empty(M, N, device=dev)
+            ws = b2.make_gemm_workspace(M, N, K, device=dev)
+            for wname, w in (("no workspace", None), ("workspace", ws)):
+                g = graph_of(torch, lambda: [b2.int8_gemm(A, Bt, sA, sB, C=C, workspace=w) for Bt in Bts])
+                steps = max(2, args.steps // copies)
+                ms = time_steps(torch, g.replay, steps, args.warmup) / (steps * copies)
+                assert b2.device_error() == 0
+                by = N * K + M * K + 4 * (M * N + M + N)
+                print(f"gemm_c5 {M}x{N}x{K} ({tag}, {wname}): {ms * 1e3:.2f} us/launch, "
+                      f"{by / (ms * 1e-3) / 1e9:.0f} GB/s (not a bench value)", flush=True)
+            del Bts
+        return
     else:
         M, N, K = {"gemm2048": (2048,) * 3, "gemm8192": (8192,) * 3, "gemm_rect": (64, 3072, 768)}[args.only]
         A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev).view(torch.int32)
@@ -981,7 +1005,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--only", default=None,
-                    choices=["attn", "attn_bf16", "attn_wide", "attn_gpt2", "attn_c1", "gemm2048", "gemm8192", "gemm_rect", "gpt2"],
+                    choices=["attn", "attn_bf16", "attn_wide", "attn_gpt2", "attn_c1", "gemm2048", "gemm8192", "gemm_rect", "gemm_c5", "gpt2"],
                     help="run one workload for a few steps with no JSON line (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -46,7 +46,7 @@ _CXX = {
 # Every symbol include/*.h declares (checked by the CPU tests).
 C_ABI_SYMBOLS = [
     "b2_decode_attn_workspace_size", "b2_decode_attn", "b2_decode_attn_noalloc", "b2_quantize_fp32_to_int8", "b2_int8_gemm",
-    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_layernorm", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
+    "b2_int8_gemm_workspace_size", "b2_int8_gemm_ws", "b2_int8_gemm_s32", "b2_int8_gemm_s32_ws", "b2_layernorm", "b2_get_device_error", "b2_last_status", "b2_status_string", "b2_version",
 ]
 
 
@@ -97,6 +97,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     lib.b2_int8_gemm_ws.restype = i
     lib.b2_int8_gemm_s32.argtypes = [i, i, i, vp, vp, vp, vp]
     lib.b2_int8_gemm_s32.restype = i
+    lib.b2_int8_gemm_s32_ws.argtypes = [i, i, i, vp, vp, vp, vp, sz, vp]
+    lib.b2_int8_gemm_s32_ws.restype = i
     lib.b2_layernorm.argtypes = [i, i, vp, vp, vp, ctypes.c_float, vp, vp, vp, vp]
     lib.b2_layernorm.restype = i
     lib.b2_get_device_error.argtypes = [i]
@@ -342,15 +344,22 @@ def make_gemm_workspace(M, N, K, device=None):
     return torch.zeros(max(256, int8_gemm_workspace_size(M, N, K)), dtype=torch.uint8, device=device or "cuda")
 
 
-def int8_gemm_s32(A_packed, BT_packed, C=None, stream=None):
+def int8_gemm_s32(A_packed, BT_packed, C=None, stream=None, workspace=None):
+    """Raw int32 accumulators; ``workspace`` (make_gemm_workspace) as for ``int8_gemm``."""
     import torch
 
     M, K4 = A_packed.shape
     N = BT_packed.shape[0]
     if C is None:
         C = torch.empty(M, N, dtype=torch.int32, device=A_packed.device)
-    _check(load_library().b2_int8_gemm_s32(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(C), _stream(stream)),
-           "b2_int8_gemm_s32")
+    lib = load_library()
+    if workspace is None:
+        _check(lib.b2_int8_gemm_s32(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(C), _stream(stream)),
+               "b2_int8_gemm_s32")
+    else:
+        _check(lib.b2_int8_gemm_s32_ws(M, N, 4 * K4, _ptr(A_packed), _ptr(BT_packed), _ptr(C), _ptr(workspace),
+                                       workspace.numel() * workspace.element_size(), _stream(stream)),
+               "b2_int8_gemm_s32_ws")
     return C
 
 

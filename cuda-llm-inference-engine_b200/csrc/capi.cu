@@ -136,6 +136,14 @@ int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t
                        static_cast<cudaStream_t>(stream));
 }
 
+int b2_int8_gemm_s32_ws(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed, int32_t* C_acc,
+                        void* workspace, size_t workspace_bytes, b2_stream_t stream) {
+    if (workspace && ((uintptr_t)workspace & 255)) return B2_ERR_INVALID;
+    PdlOn pdl;
+    return gemm_launch(M, N, K, A_packed, BT_packed, nullptr, nullptr, nullptr, nullptr, C_acc, B2_EPI_PLAIN, true,
+                       static_cast<cudaStream_t>(stream), workspace, workspace_bytes);
+}
+
 int b2_layernorm(int rows, int cols, const float* x, const float* gamma, const float* beta, float eps, float* out,
                  int32_t* q_packed, float* scales, b2_stream_t stream) {
     if (rows < 0 || cols <= 0) return B2_ERR_INVALID;

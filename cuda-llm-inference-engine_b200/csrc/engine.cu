@@ -35,6 +35,7 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
                 const float* bias, const float* residual, void* C, int epi, bool s32, cudaStream_t st,
                 void* ws = nullptr, size_t ws_bytes = 0);
 size_t gemm_workspace_size(int M, int N, int K);
+size_t gemm_rs_workspace_size(int M, int N, int K);
 
 // NCCL is resolved at run time, only when tensor parallelism is used, preferring a
 // libnccl.so.2 the process already loaded (e.g. PyTorch's), so loading this library never
@@ -145,6 +146,10 @@ struct b2_engine {
     std::vector<void*> ipc_opened;
     float* amax = nullptr;    // [B] row absmax (row-parallel quantisation)
     int32_t* acc32 = nullptr; // [B, d] int32 partials of the row-parallel linears
+    // exchange rows of the decode GEMMs whose K range is reduce-scattered over a cluster
+    // (large activations: d_model or d_ff >= 2048 at batch 128)
+    void* gemm_ws = nullptr;
+    size_t gemm_ws_bytes = 0;
     std::vector<void*> allocs;  // every device allocation, freed by the destructor
     float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
     std::vector<Layer> layers;
@@ -270,6 +275,15 @@ int alloc_runtime(b2_engine* e) {
     e->attn_ws_bytes = std::max<size_t>(256, decode_attn_workspace_size(B, e->Hl, e->Hl, c.d_head, c.max_seq_len,
                                                                          kBlock));
     e->attn_ws = e->alloc<unsigned char>(e->attn_ws_bytes);
+    {
+        const int kl = d / e->tp_size, kf = c.d_ff / e->tp_size;
+        const size_t g = std::max({gemm_rs_workspace_size(B, 3 * e->dl, d), gemm_rs_workspace_size(B, d, kl),
+                                   gemm_rs_workspace_size(B, e->ffl, d), gemm_rs_workspace_size(B, d, kf)});
+        if (g) {
+            e->gemm_ws = e->alloc<unsigned char>(g);
+            e->gemm_ws_bytes = g;
+        }
+    }
     if (e->failed) return B2_ERR_CUDA;
     if (!e->k_pool || !e->v_pool || !e->attn_ws || !e->logits) return B2_ERR_CUDA;
     if (cudaMemset(e->attn_ws, 0, e->attn_ws_bytes) != cudaSuccess) return B2_ERR_CUDA;
@@ -426,6 +440,8 @@ struct RowSet {
     int32_t *xq = nullptr, *acc32 = nullptr;
     void* attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
+    void* gemm_ws = nullptr;  // reduce-scatter exchange rows (decode rows only)
+    size_t gemm_ws_bytes = 0;
     int max_ctx = 0;
     bool p2p = false;  // the peer-memory exchange (its buffers are the decode step's)
     // prefill: causal attention over work items (first row, rows) of one sequence each
@@ -447,6 +463,10 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
     B2_TRY(launch_embed(B, d, R.tokens, R.pos, e->wte, e->wpe, R.x, R.ctx, R.keys, st));
     const bool tp = e->tp_size > 1;
     const int Hl = e->Hl, dl = e->dl, ffl = e->ffl;
+    // the exchange rows go only to GEMMs that take the reduce-scatter split: a workspace
+    // given to another shape would select the global-memory split-K path instead
+    auto gws = [&](int N, int K) { return gemm_rs_workspace_size(B, N, K) ? R.gemm_ws : nullptr; };
+    auto gwb = [&](int N, int K) { return gemm_rs_workspace_size(B, N, K) && R.gemm_ws ? R.gemm_ws_bytes : 0; };
     // all-reduces of the tensor-parallel step (NCCL on the step's stream; captured in the graph)
     auto allreduce = [&](void* buf, size_t n, ncclDataType_t t, ncclRedOp_t op) {
         return nccl_call_bounded(nccl(), e->comm, [&] { return nccl().AllReduce(buf, buf, n, t, op, e->comm, st); },
@@ -461,7 +481,7 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
             if ((r2 = launch_tp_quantize(B, kl, act, R.xq, R.xs, e->peers, st)) != B2_OK) return r2;
             M(gemm_label);
             if ((r2 = gemm_launch(B, d, kl, R.xq, W.w, nullptr, nullptr, nullptr, nullptr, R.acc32, B2_EPI_PLAIN,
-                                  true, st)) != B2_OK)
+                                  true, st, gws(d, kl), gwb(d, kl))) != B2_OK)
                 return r2;
             M("tp_reduce");
             return launch_tp_reduce(B, d, R.xs, W.s, W.bias, e->peers, st);
@@ -474,7 +494,7 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
         if ((r2 = launch_quantize_scaled(B, kl, act, R.amax, R.xq, R.xs, st)) != B2_OK) return r2;
         M(gemm_label);
         if ((r2 = gemm_launch(B, d, kl, R.xq, W.w, nullptr, nullptr, nullptr, nullptr, R.acc32, B2_EPI_PLAIN, true,
-                              st)) != B2_OK)
+                              st, gws(d, kl), gwb(d, kl))) != B2_OK)
             return r2;
         M("allreduce_partials");
         if ((r2 = allreduce(R.acc32, (size_t)B * d, ncclInt32, ncclSum)) != B2_OK) return r2;
@@ -501,11 +521,12 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
         qa.block_size = kBlock;
         qa.nbps = e->blocks_per_seq;
         qa.bf16 = e->kv_dtype == B2_KV_BF16;
-        r = e->fuse_qkv ? gemm_launch_qkv(B, 3 * dl, d, R.xq, L.qkv.w, R.xs, L.qkv.s, L.qkv.bias, qa, st)
+        r = e->fuse_qkv ? gemm_launch_qkv(B, 3 * dl, d, R.xq, L.qkv.w, R.xs, L.qkv.s, L.qkv.bias, qa, st,
+                                          gws(3 * dl, d), gwb(3 * dl, d))
                         : B2_ERR_UNSUPPORTED;
         if (r == B2_ERR_UNSUPPORTED) {
             B2_TRY(gemm_launch(B, 3 * dl, d, R.xq, L.qkv.w, R.xs, L.qkv.s, L.qkv.bias, nullptr, R.qkv, B2_EPI_BIAS,
-                               false, st));
+                               false, st, gws(3 * dl, d), gwb(3 * dl, d)));
             M("qkv_scatter");
             B2_TRY(launch_qkv_scatter(B, dl, Hl, dh, kBlock, e->blocks_per_seq, R.qkv, R.pos, R.block_table, R.q, kc,
                                       vc, e->kv_dtype, st));
@@ -532,14 +553,14 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
             B2_TRY(quantize_launch(B, d, R.attn, R.xq, R.xs, st));
             M("gemm_out");
             B2_TRY(gemm_launch(B, d, d, R.xq, L.out.w, R.xs, L.out.s, L.out.bias, R.x, R.x, B2_EPI_BIAS_RESIDUAL,
-                               false, st));
+                               false, st, gws(d, d), gwb(d, d)));
         }
         // MLP sub-block
         M("ln_quant");
         B2_TRY(launch_ln_quant(B, d, R.x, L.ln2_g, L.ln2_b, kLnEps, R.xq, R.xs, nullptr, st));
         M("gemm_fc1");
         B2_TRY(gemm_launch(B, ffl, d, R.xq, L.up.w, R.xs, L.up.s, L.up.bias, nullptr, R.hbuf, B2_EPI_BIAS_GELU, false,
-                           st));
+                           st, gws(ffl, d), gwb(ffl, d)));
         if (tp) {
             B2_TRY(row_parallel(R.hbuf, ffl, L.down, "gemm_fc2"));
         } else {
@@ -547,7 +568,7 @@ int enqueue_layers(b2_engine* e, const RowSet& R, cudaStream_t st, StepProfiler*
             B2_TRY(quantize_launch(B, ff, R.hbuf, R.xq, R.xs, st));
             M("gemm_fc2");
             B2_TRY(gemm_launch(B, d, ff, R.xq, L.down.w, R.xs, L.down.s, L.down.bias, R.x, R.x, B2_EPI_BIAS_RESIDUAL,
-                               false, st));
+                               false, st, gws(d, ff), gwb(d, ff)));
         }
     }
 #undef B2_TRY
@@ -573,6 +594,8 @@ int enqueue_step(b2_engine* e, cudaStream_t st, StepProfiler* prof = nullptr) {
     R.xq = e->xq; R.acc32 = e->acc32;
     R.attn_ws = e->attn_ws;
     R.attn_ws_bytes = e->attn_ws_bytes;
+    R.gemm_ws = e->gemm_ws;
+    R.gemm_ws_bytes = e->gemm_ws_bytes;
     R.max_ctx = c.max_seq_len;
     R.p2p = e->p2p;
     int r;

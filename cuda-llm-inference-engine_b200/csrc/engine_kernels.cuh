@@ -18,7 +18,8 @@ int launch_prefill_attention(const int2* items, int n_items, int H, int D, int k
                              const void* k_cache, const void* v_cache, const int* block_table, int nbps,
                              int block_size, const int* pos, float* O, cudaStream_t st);
 int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
-                    const float* bias, const QkvScatterArgs& sc, cudaStream_t st);
+                    const float* bias, const QkvScatterArgs& sc, cudaStream_t st, void* ws = nullptr,
+                    size_t ws_bytes = 0);
 
 // keys: [2 * B] argmax keys (approximate, then exact), both zeroed for the step
 int launch_embed(int B, int d, const int* tokens, const int* pos, const float* wte, const float* wpe, float* x,

@@ -154,8 +154,11 @@ struct GemmParams {
     // kernel waits on the previous grid (the decode engine); otherwise every global read
     // follows the wait, which makes programmatic dependent launch safe for any producer
     int b_early;
-    // the k_splits CTAs of a tile form a thread-block cluster: ranks 1.. hand their int32
+    // the k_splits CTAs of a tile form a thread-block cluster. 1: ranks 1.. hand their int32
     // partials to rank 0's shared memory (GemmCfg::RED_BYTES), which sums them and stores
+    // the tile; 2 (reduce-scatter): rank r owns the tile's columns [r S, (r+1) S),
+    // S = BN / k_splits, receives every partner's partial of them through exchange rows in
+    // ws and stores them
     int cluster_k;
 };
 
@@ -164,7 +167,8 @@ struct GemmCfg {
     static constexpr int A_BYTES = GM_BM * GM_BK;
     static constexpr int B_BYTES = BN * GM_BK;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    // partials of up to 3 cluster partners (128 rows x BN int32 each), 32-column tiles only
+    // cluster partials: 32-column tiles gather up to 3 partners' 128 x 32 int32 partials in
+    // rank 0 (the reduce-scatter of 128-column tiles exchanges through global memory)
     static constexpr int RED_MAX = 3;
     static constexpr int RED_BYTES = BN == 32 ? RED_MAX * GM_BM * BN * 4 : 0;
     static constexpr int STAGES = std::min(8, (196 * 1024 - RED_BYTES) / STAGE);
@@ -487,6 +491,86 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(acce_bar(a));  // accumulator a may be overwritten
+            } else if (p.cluster_k == 2) {
+                // cluster reduce-scatter: rank ksi owns the tile's columns [ksi S, ksi S + S).
+                // It writes every other slice of its int32 partial to the owner's exchange
+                // rows in global memory (L2: distributed shared memory moves only ~30-40 GB/s
+                // per SM in an all-to-all), arrives on the owner's barrier with release at
+                // cluster scope, waits (acquire) for its own partners, adds the slices they
+                // wrote to its own (exact) and runs the epilogue on its columns. Exchange rows
+                // are laid out [tile][owner][slot][granule][row] (16-byte granules), so a warp's
+                // 32 rows of one granule are 512 contiguous bytes.
+                const int S = BN / p.k_splits;  // 16, 32 or 64 columns
+                const int G4 = S / 4;           // 16-byte granules per slice row
+                const int lrow = quad * 32 + lane;
+                const size_t slice_i4 = (size_t)G4 * GM_BM;  // int4 per (owner, slot) slice
+                int4* xt = reinterpret_cast<int4*>(p.ws) + (size_t)t * p.k_splits * (p.k_splits - 1) * slice_i4;
+#pragma unroll 1
+                for (int pr = 1; pr < p.k_splits; ++pr) {
+                    const int dst = (ksi + pr) % p.k_splits;  // staggered: partners fill different owners first
+                    const int slot = ksi < dst ? ksi : ksi - 1;
+                    int4* xs = xt + ((size_t)dst * (p.k_splits - 1) + slot) * slice_i4 + lrow;
+#pragma unroll 1
+                    for (int c = 0; c < S / 16; ++c) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)(dst * S + c * 16), r);
+                        tmem_ld_wait();
+                        if (row_ok)
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                __stcg(xs + (size_t)(c * 4 + q) * GM_BM,
+                                       make_int4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]));
+                    }
+                }
+                // one release for all the stores above (a releasing arrive per owner would wait
+                // for its stores each time), then the arrivals
+                asm volatile("fence.acq_rel.cluster;" ::: "memory");
+#pragma unroll 1
+                for (int pr = 1; pr < p.k_splits; ++pr)
+                    mbar_arrive_cluster(mapa_shared(red_bar, (uint32_t)((ksi + pr) % p.k_splits)));
+                const bool got = ok && mbar_wait_cluster(red_bar, 0, p.err);
+                if (!got) *abort_flag = 1;
+                const int4* xo = xt + (size_t)ksi * (p.k_splits - 1) * slice_i4 + lrow;
+#pragma unroll 1
+                for (int c = 0; c < S / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tbase + (uint32_t)(ksi * S + c * 16), r);
+                    tmem_ld_wait();
+                    if (got && row_ok) {
+                        // the partners' slices in batches of 4, every load of a batch in flight
+                        const int ns = p.k_splits - 1;
+                        for (int sl0 = 0; sl0 < ns; sl0 += 4) {
+                            int4 v[4][4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    v[j][q] = sl0 + j < ns ? __ldcg(xo + (sl0 + j) * slice_i4 + (size_t)(c * 4 + q) * GM_BM)
+                                                           : make_int4(0, 0, 0, 0);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    r[4 * q] = (uint32_t)((int32_t)r[4 * q] + v[j][q].x);
+                                    r[4 * q + 1] = (uint32_t)((int32_t)r[4 * q + 1] + v[j][q].y);
+                                    r[4 * q + 2] = (uint32_t)((int32_t)r[4 * q + 2] + v[j][q].z);
+                                    r[4 * q + 3] = (uint32_t)((int32_t)r[4 * q + 3] + v[j][q].w);
+                                }
+                        }
+                        const int cc = (ksi * S) / 16 + c;  // 16-column chunk of the tile
+                        const int n = nt * BN + cc * 16;
+                        float rs[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) rs[i] = 0.f;
+                        if constexpr (EPI == B2_EPI_BIAS_RESIDUAL && !S32) {
+                            if (n < p.N) load_res16(p, row, n, rs);
+                        }
+                        if (n < p.N) store16<EPI, S32>(r, row, n, sa, sB_s + cc * 16, bias_s + cc * 16, rs, p, sc_row);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acce_bar(a));
             } else if (p.cluster_k) {
                 // cluster split-K: partners push their int32 partials (valid rows only) into
                 // rank 0's shared memory and arrive on its barrier; rank 0 adds them (exact)
@@ -633,6 +717,9 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
 
     tc_fence_before();
     __syncthreads();
+    // reduce-scatter: no CTA of the cluster exits while a partner may still address its
+    // shared memory
+    if (p.cluster_k == 2) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
@@ -1065,6 +1152,79 @@ static int launch_tc2(const GemmParams& p, const int32_t* A, const int32_t* BT, 
     return cudaLaunchKernelEx(&cfg, kfn, ma, mb, mc, p, c_tma) == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
+constexpr int kMaxGemmDevices = 64;
+
+// Clusters of c CTAs of the 128-column kernel that the device holds at once (cached).
+template <int EPI, bool S32>
+static int rs_resident_clusters(int c) {
+    static int cached[4][kMaxGemmDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxGemmDevices) return 0;
+    const int ci = c == 2 ? 0 : c == 4 ? 1 : 2;
+    if (cached[ci][dev]) return cached[ci][dev] - 1;
+    auto kfn = int8_gemm_tc_kernel<128, EPI, S32>;
+    int n = 0;
+    if (set_smem_attr_once((const void*)kfn, GemmCfg<128>::SMEM, 0)) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c);
+        cfg.blockDim = dim3(GM_THREADS);
+        cfg.dynamicSmemBytes = GemmCfg<128>::SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = c;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+    }
+    cached[ci][dev] = n + 1;
+    return n;
+}
+
+// Cluster size of the reduce-scatter split (GemmParams::cluster_k == 2) for a decode
+// contraction, or 1. With one 128-row tile, the 32-column path streams the whole activation
+// through every one of its CTAs (config-5 shard 128 x 4096 x 4096: 128 CTAs x 512 KB of A
+// for 16 MB of weights, ~10 us of TMA per CTA); 128-column tiles whose K range is split over
+// a cluster of c CTAs stream A[:, k range] once per (tile, k range) instead, 4x less at the
+// same CTA count, and exchange (c - 1) / c of a 128 x 128 int32 partial through L2.
+// Used once the activation holds >= 256 KB (B2_GEMM_RS_MIN_KB sets the bound in KB,
+// B2_GEMM_RS=0 turns it off), with every cluster resident at once (a second wave of
+// clusters doubles the time), >= 4 k-blocks per CTA and no empty k range.
+template <int EPI, bool S32>
+static int rs_cluster_size(const GemmParams& p, int sms) {
+    static const bool off = getenv("B2_GEMM_RS") && strcmp(getenv("B2_GEMM_RS"), "0") == 0;
+    static const long long min_a = (getenv("B2_GEMM_RS_MIN_KB") ? atoll(getenv("B2_GEMM_RS_MIN_KB")) : 256) * 1024;
+    if (off || p.M > GM_BM || (long long)p.a_rows * p.K < min_a) return 1;
+    const int t128 = (p.N + 127) / 128;
+    const int nk = (p.K + GM_BK - 1) / GM_BK;
+    for (int c = 8; c >= 2; c /= 2) {
+        const int kbps = (nk + c - 1) / c;
+        if (t128 * c > sms || kbps < 4 || (c - 1) * kbps >= nk) continue;
+        if (t128 > rs_resident_clusters<EPI, S32>(c)) continue;
+        return c;
+    }
+    return 1;
+}
+
+// Exchange bytes of the reduce-scatter split: (c - 1) 128 x (128 / c) int32 slices per
+// (tile, owner).
+static size_t rs_ws_bytes(int N, int c) {
+    return (size_t)((N + 127) / 128) * (c - 1) * GM_BM * 128 * sizeof(int32_t);
+}
+
+static void set_rs_split(GemmParams& p, int c, void* ws) {
+    const int nk = (p.K + GM_BK - 1) / GM_BK;
+    p.k_splits = c;
+    p.kb_per_split = (nk + c - 1) / c;
+    p.cluster_k = 2;
+    p.ws = static_cast<int32_t*>(ws);
+    p.counters = nullptr;
+}
+
 template <int EPI, bool S32>
 static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, void* ws, size_t ws_bytes,
                          cudaStream_t st) {
@@ -1094,6 +1254,10 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
         plan_split(p, t128, nullptr, 0, sms);
         return launch_tc<128, EPI, S32>(p, A, BT, st, slot_base + 1);
     }
+    if (const int rc = rs_cluster_size<EPI, S32>(p, sms); rc > 1 && ws && ws_bytes >= rs_ws_bytes(p.N, rc)) {
+        set_rs_split(p, rc, ws);
+        return launch_tc<128, EPI, S32>(p, A, BT, st, slot_base + 1);
+    }
     // skinny outputs (decode: M = batch): 32-column tiles double the CTAs streaming the weights
     const int t32 = mt * ((p.N + 31) / 32);
     if (!ws && t64 * 2 <= sms && t32 <= sms) {
@@ -1119,15 +1283,38 @@ static int gemm_dispatch(GemmParams& p, const int32_t* A, const int32_t* BT, voi
     return launch_tc<64, EPI, S32>(p, A, BT, st, slot_base + 2);
 }
 
+// Exchange bytes the reduce-scatter split needs for this shape (0 when gemm_launch would take
+// another path: CTA pairs, a tile per SM, or a small activation).
+size_t gemm_rs_workspace_size(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0 || (K & 15)) return 0;
+    const int sms = num_sms_current_device();
+    const int mt = (M + GM_BM - 1) / GM_BM;
+    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    if ((g_gemm_pairs && pair_tiles * 2 >= (sms * 3) / 4) || mt * ((N + 255) / 256) >= sms ||
+        mt * ((N + 127) / 128) >= sms)
+        return 0;
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.a_rows = M <= GM_BM ? ((M + 7) & ~7) : GM_BM;
+    const int rc = rs_cluster_size<B2_EPI_PLAIN, false>(p, sms);
+    return rc > 1 ? rs_ws_bytes(N, rc) : 0;
+}
+
 // Workspace bytes that let gemm_launch split K for these shapes (0 when it would not split).
 size_t gemm_workspace_size(int M, int N, int K) {
     const int sms = num_sms_current_device();
     const int mt = (M + GM_BM - 1) / GM_BM;
     const int tiles = mt * ((N + 63) / 64);
     const int nk = (K + GM_BK - 1) / GM_BK;
-    if (mt * ((N + 127) / 128) >= sms || tiles >= sms || nk < 2) return 0;
-    const size_t ctr_bytes = (((size_t)tiles * sizeof(unsigned int)) + 255) & ~(size_t)255;
-    return ctr_bytes + (size_t)std::min(std::min(nk, sms / std::max(1, tiles)), 32) * M * N * sizeof(int32_t);
+    if (mt * ((N + 127) / 128) >= sms || nk < 2) return 0;
+    size_t need = 0;
+    if (tiles < sms) {
+        const size_t ctr_bytes = (((size_t)tiles * sizeof(unsigned int)) + 255) & ~(size_t)255;
+        need = ctr_bytes + (size_t)std::min(std::min(nk, sms / std::max(1, tiles)), 32) * M * N * sizeof(int32_t);
+    }
+    return std::max(need, gemm_rs_workspace_size(M, N, K));
 }
 
 int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
@@ -1159,7 +1346,7 @@ int gemm_launch(int M, int N, int K, const int32_t* A, const int32_t* BT, const 
 // Only the one-CTA tcgen05 kernel implements it; shapes that would take another kernel (or
 // N != 3 d, d % 16 != 0) return B2_ERR_UNSUPPORTED and the caller runs the two steps apart.
 int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, const float* sA, const float* sB,
-                    const float* bias, const QkvScatterArgs& sc, cudaStream_t st) {
+                    const float* bias, const QkvScatterArgs& sc, cudaStream_t st, void* ws, size_t ws_bytes) {
     if (M <= 0 || N <= 0 || (K & 15) || K == 0 || ((uintptr_t)A & 15) || ((uintptr_t)BT & 15)) return B2_ERR_UNSUPPORTED;
     if (!A || !BT || !sA || !sB || !bias || !sc.q || !sc.k || !sc.v || !sc.pos || !sc.block_table)
         return B2_ERR_INVALID;
@@ -1183,6 +1370,10 @@ int gemm_launch_qkv(int M, int N, int K, const int32_t* A, const int32_t* BT, co
     plan_split(p, 1, nullptr, 0, sms);  // one k range per tile (sets kb_per_split)
     if (t256 >= sms) return launch_tc<256, B2_EPI_BIAS, false>(p, A, BT, st, 0);
     if (t128 >= sms) return launch_tc<128, B2_EPI_BIAS, false>(p, A, BT, st, 0);
+    if (const int rc = rs_cluster_size<B2_EPI_BIAS, false>(p, sms); rc > 1 && ws && ws_bytes >= rs_ws_bytes(N, rc)) {
+        set_rs_split(p, rc, ws);
+        return launch_tc<128, B2_EPI_BIAS, false>(p, A, BT, st, 0);
+    }
     if (t64 * 2 <= sms && t32 <= sms) return launch_tc<32, B2_EPI_BIAS, false>(p, A, BT, st, 0);
     return launch_tc<64, B2_EPI_BIAS, false>(p, A, BT, st, 0);
 }

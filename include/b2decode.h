@@ -143,6 +143,10 @@ int b2_int8_gemm(int M, int N, int K, const int32_t* A_packed, const int32_t* BT
 /* Bytes of workspace that let b2_int8_gemm_ws split the K dimension across CTAs for shapes
  * whose output tiles cannot fill the GPU (decode: M = batch); 0 when it would not split.
  * No counterpart in the reference (its dp4a kernel has a fixed 64x64 tile grid). */
+/* When M <= 128 and the activation holds >= 256 KB (batch 128 at K >= 2048), the workspace
+ * holds the exchange rows of the reduce-scatter split instead: 128-column tiles whose K range
+ * is split over a thread-block cluster of 2, 4 or 8 CTAs, each CTA finishing one column slice
+ * from its partners' exact int32 partials. */
 size_t b2_int8_gemm_workspace_size(int M, int N, int K);
 
 /* b2_int8_gemm with a caller workspace for split-K: each CTA contracts a K range into
@@ -160,6 +164,11 @@ int b2_int8_gemm_ws(int M, int N, int K, const int32_t* A_packed, const int32_t*
  * (kernels/quantization/14_int8_gemm.cu:96-140), which the reference never exposes. */
 int b2_int8_gemm_s32(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
                      int32_t* C_acc, b2_stream_t stream);
+
+/* b2_int8_gemm_s32 with a caller workspace (b2_int8_gemm_workspace_size bytes, 256-byte
+ * aligned), as b2_int8_gemm_ws; bit-identical to b2_int8_gemm_s32. */
+int b2_int8_gemm_s32_ws(int M, int N, int K, const int32_t* A_packed, const int32_t* BT_packed,
+                        int32_t* C_acc, void* workspace, size_t workspace_bytes, b2_stream_t stream);
 
 /* ------------------------------------------------------------------ LayerNorm */
 

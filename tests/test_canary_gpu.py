@@ -94,6 +94,7 @@ def test_quantiser_stays_in_its_buffers(b2, oracle, cuda):
 @pytest.mark.parametrize("M,N,K,split", [(77, 130, 96, False),    # partial tiles, tensor-core path
                                          (5, 40, 100, False),     # K % 16 != 0: SIMT path
                                          (64, 2304, 768, True),   # decode shape, split-K workspace
+                                         (100, 1000, 8192, True),  # reduce-scatter exchange rows, ragged
                                          (1800, 2100, 256, False)])  # CTA-pair path (72 tiles), ragged edges
 def test_int8_gemm_stays_in_its_buffers(b2, oracle, cuda, M, N, K, split):
     import torch

@@ -133,6 +133,31 @@ def test_fused_qkv_split_equals_separate_kernel(b2, cuda, kv_dtype, monkeypatch)
     assert np.array_equal(out[0][1], out[1][1])
 
 
+def test_fused_qkv_split_reduce_scatter_gemm(b2, cuda, monkeypatch):
+    """d_model 2048 at batch 128: the QKV GEMM (128 x 6144 x 2048) takes the 128-column tiles
+    whose K range is reduce-scattered over a cluster, with the q / paged K/V split in that
+    epilogue; with the fusion off the same GEMM writes qkv and the scatter kernel splits it.
+    Tokens and logits are identical."""
+    cfg = dict(n_layers=1, n_heads=16, d_model=2048, d_ff=2048, vocab_size=512, max_seq_len=32, d_head=128)
+    rng = np.random.default_rng(5)
+    prompts = _prompts(rng, 128, cfg["vocab_size"], [3] * 128)
+    out = []
+    for fuse in ("1", "0"):
+        monkeypatch.setenv("B2_ENGINE_FUSE_QKV", fuse)
+        e = b2.Engine.random(cfg, max_batch=128, kv_dtype=0, seed=23)
+        e.start(prompts, 4, seed=7)
+        e.keep_logits(True)
+        logits = []
+        for _ in range(4):
+            e.step()
+            logits.append(e.logits())
+        out.append((e.tokens(), np.stack(logits)))
+        e.close()
+    assert b2.device_error() == 0
+    assert np.array_equal(out[0][0], out[1][0])
+    assert np.array_equal(out[0][1], out[1][1])
+
+
 @pytest.mark.parametrize("kv_dtype", [0, 1])
 def test_prefill_matches_token_by_token(b2, cuda, kv_dtype):
     """Batched prefill of equal-length prompts, then decode steps, against the same prompts fed

@@ -155,7 +155,7 @@ def test_gemm_invalid_args(b2, cuda):
         b2.int8_gemm(A, A, s, s, torch.zeros(4, device=cuda), epilogue=b2.EPI_BIAS_RESIDUAL)
 
 
-SPLIT_SHAPES = [(64, 768, 3072), (64, 2304, 768), (64, 3072, 768), (1, 768, 3072), (128, 768, 4096),
+SPLIT_SHAPES = [(64, 768, 3072), (64, 2304, 768), (64, 3072, 768), (1, 768, 3072), (128, 768, 1536),
                 (100, 200, 1024), (3, 50, 2048)]
 
 
@@ -192,6 +192,55 @@ def test_gemm_split_k_bit_exact(b2, oracle, cuda, M, N, K, epi):
     assert int(ws[:256].view(torch.int32).abs().sum()) == 0  # tickets back to zero
 
 
+# Reduce-scatter split (workspace given, activation >= 256 KB): 128-column tiles whose K range
+# is split over a cluster of 2, 4 or 8 CTAs, int32 partial slices exchanged through the
+# workspace; exact, so equal to the oracle bit for bit.
+RS_SHAPES = [
+    (128, 4096, 4096),   # 4-CTA clusters, 32-column slices
+    (128, 2048, 4096),   # 8 or 4 CTAs (as many as stay resident)
+    (128, 6144, 4096),   # 2-CTA clusters, 64-column slices
+    (128, 768, 4096),    # 8-CTA clusters over 6 tiles
+    (100, 1000, 8192),   # ragged rows and a ragged last tile
+    (64, 1536, 4096),    # 64 rows (A = 256 KB)
+    (128, 3072, 2064),   # K tail past the last full k-block
+]
+
+
+@pytest.mark.parametrize("M,N,K", RS_SHAPES)
+@pytest.mark.parametrize("epi", [0, 1, 2, 3, "s32"])
+def test_gemm_reduce_scatter_bit_exact(b2, oracle, cuda, M, N, K, epi):
+    import torch
+
+    assert b2.int8_gemm_workspace_size(M, N, K) > 0
+    rng = np.random.default_rng(M * 11 + N * 3 + K)
+    A, Bt = quantized_pair(rng, M, N, K)
+    Ap, sA = oracle.quantize(A)
+    Bp, sB = oracle.quantize(Bt)
+    acc = oracle.int8_gemm_s32(Ap, Bp, nthreads=0)
+    t = {k: dev(torch, v, cuda) for k, v in dict(Ap=Ap, Bp=Bp, sA=sA, sB=sB).items()}
+    ws = b2.make_gemm_workspace(M, N, K, device=cuda)
+    if epi == "s32":
+        for _ in range(2):  # repeated launches reuse the exchange rows
+            got = b2.int8_gemm_s32(t["Ap"], t["Bp"], workspace=ws)
+            torch.cuda.synchronize()
+            assert b2.device_error() == 0
+            np.testing.assert_array_equal(got.cpu().numpy(), acc)
+        return
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    want = oracle.epilogue(acc, sA, sB, bias, res, epi)
+    for _ in range(2):
+        got = b2.int8_gemm(t["Ap"], t["Bp"], t["sA"], t["sB"], dev(torch, bias, cuda) if epi else None,
+                           dev(torch, res, cuda) if epi == 3 else None, epilogue=epi, workspace=ws)
+        torch.cuda.synchronize()
+        assert b2.device_error() == 0
+        g = got.cpu().numpy()
+        if epi == 2:
+            np.testing.assert_allclose(g, want, rtol=1e-4, atol=1e-6)
+        else:
+            np.testing.assert_array_equal(g.view(np.uint32), want.view(np.uint32))
+
+
 # Decode-size GEMMs (M <= 128: one row tile, skinny 32-column tiles, A boxes trimmed to the
 # batch rows): every epilogue and the raw int32 view, ragged M and N, K tails.
 DECODE_SHAPES = [
@@ -203,7 +252,11 @@ DECODE_SHAPES = [
     (1, 768, 768),       # one sequence
     (33, 1000, 640),     # ragged last tile
     (7, 130, 1040),      # N % 4 != 0 (scalar stores), K tail of 16 past the last full k-block
-    (128, 2048, 4096),   # config-5 shard: full 128-row tile
+    (128, 2048, 4096),   # config-5 shard: 128-column tiles, K reduce-scattered over 8 CTAs
+    (128, 4096, 4096),   # reduce-scatter over 4 CTAs (32-column slices)
+    (128, 6144, 4096),   # reduce-scatter over 2 CTAs (64-column slices)
+    (100, 1000, 8192),   # reduce-scatter with ragged rows and a ragged last tile
+    (64, 1536, 4096),    # reduce-scatter at 64 rows (A = 256 KB)
     (100, 200, 48),      # one k-block
     (120, 4100, 272),    # wide N, 3 k-blocks
 ]
