@@ -274,6 +274,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
 }
+// The same with an arrival count (one thread arriving for `count` threads).
+__device__ __forceinline__ void mbar_arrive_cluster_count(uint32_t cluster_addr, uint32_t count) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0], %1;" :: "r"(cluster_addr), "r"(count)
+                 : "memory");
+}
 // 2-D TMA load of a CTA pair: each CTA loads into its own shared memory, and the transaction
 // bytes are counted on the mbarrier at `lead_bar`, the even CTA's barrier as a shared::cluster
 // address (from mapa_shared).

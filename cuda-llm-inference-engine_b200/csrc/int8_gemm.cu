@@ -523,11 +523,12 @@ int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_const
                     }
                 }
                 // one release for all the stores above (a releasing arrive per owner would wait
-                // for its stores each time), then the arrivals
+                // for its stores each time); then lane j arrives for the whole warp on owner
+                // ksi + 1 + j, so the remote arrivals go out in one instruction
                 asm volatile("fence.acq_rel.cluster;" ::: "memory");
-#pragma unroll 1
-                for (int pr = 1; pr < p.k_splits; ++pr)
-                    mbar_arrive_cluster(mapa_shared(red_bar, (uint32_t)((ksi + pr) % p.k_splits)));
+                __syncwarp();
+                if (lane < p.k_splits - 1)
+                    mbar_arrive_cluster_count(mapa_shared(red_bar, (uint32_t)((ksi + 1 + lane) % p.k_splits)), 32u);
                 const bool got = ok && mbar_wait_cluster(red_bar, 0, p.err);
                 if (!got) *abort_flag = 1;
                 const int4* xo = xt + (size_t)ksi * (p.k_splits - 1) * slice_i4 + lrow;
