@@ -20,6 +20,9 @@ pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CFG = dict(n_layers=2, n_heads=8, d_model=512, d_ff=2048, vocab_size=999, max_seq_len=64, d_head=64)
+# batch 128 at d_model 2048: the QKV, FC1 and row-parallel FC2 shards (activations of 256 KB and
+# more) take the reduce-scatter GEMM split on both the sharded and the single-GPU engine
+WIDE = dict(n_layers=1, n_heads=16, d_model=2048, d_ff=8192, vocab_size=999, max_seq_len=32, d_head=128)
 
 
 def _need_gpus(n):
@@ -29,12 +32,16 @@ def _need_gpus(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-@pytest.mark.parametrize("kv_dtype,collectives", [(0, "p2p"), (1, "p2p"), (0, "nccl")])
-def test_tp2_matches_single_gpu(b2, cuda, tmp_path, kv_dtype, collectives):
+@pytest.mark.parametrize("model,kv_dtype,collectives",
+                         [("small", 0, "p2p"), ("small", 1, "p2p"), ("small", 0, "nccl"), ("wide", 0, "p2p")])
+def test_tp2_matches_single_gpu(b2, cuda, tmp_path, model, kv_dtype, collectives):
     _need_gpus(2)
     rng = np.random.default_rng(5)
-    prompts = [list(map(int, rng.integers(0, CFG["vocab_size"], n))) for n in (4, 7, 2)]
-    spec = dict(cfg=CFG, max_batch=3, kv_dtype=kv_dtype, seed=13, block_seed=2, prompts=prompts, new=5, steps=10)
+    cfg = CFG if model == "small" else WIDE
+    lens = (4, 7, 2) if model == "small" else tuple(int(n) for n in rng.integers(1, 9, 128))
+    prompts = [list(map(int, rng.integers(0, cfg["vocab_size"], n))) for n in lens]
+    B = len(prompts)
+    spec = dict(cfg=cfg, max_batch=B, kv_dtype=kv_dtype, seed=13, block_seed=2, prompts=prompts, new=5, steps=10)
     nid = b2.nccl_unique_id().hex()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     env.pop("B2_TP_COLLECTIVES", None)
@@ -45,7 +52,7 @@ def test_tp2_matches_single_gpu(b2, cuda, tmp_path, kv_dtype, collectives):
     for p in procs:
         assert p.wait(timeout=300) == 0
     outs = [np.load(tmp_path / f"r{r}.npz") for r in range(2)]
-    e = b2.Engine.random(CFG, max_batch=3, kv_dtype=kv_dtype, seed=13)
+    e = b2.Engine.random(cfg, max_batch=B, kv_dtype=kv_dtype, seed=13)
     e.start(prompts, 5, seed=2)
     e.keep_logits(True)
     ref = []
